@@ -1,0 +1,281 @@
+"""mvcc_b200 -- B200-native MoE block of mvcc's examples/qwen behind its C ABI (include/moe_block.h).
+
+The compute path is libmoe_b200.so (hand-written sm_100a CUDA, built in-tree by mvcc_b200/build.py). This module
+is the host-side mirror of the reference's launch interface for the block: `MoeLayer` carries the fields of the
+reference's `Layer`/`Model` (qwen.cu:99-124) plus the INT4 group size, and `MoeBlock` owns the workspace the
+reference's `Work` held (qwen.cu:227-293) and issues the calls forward() makes at qwen.cu:429-448.
+PyTorch is used only for device memory and streams. There is no CPU fallback: if the library is missing the
+import fails, and every call raises on a non-zero cudaError_t.
+"""
+import ctypes
+import dataclasses
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmoe_b200.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is missing: build it with `python mvcc_b200/build.py` (nvcc, sm_100a)")
+_lib = ctypes.CDLL(LIB_PATH)
+
+
+class MoeLayerWeights(ctypes.Structure):
+    """ctypes mirror of `moe_layer_weights` (include/moe_block.h)."""
+
+    _fields_ = [
+        ("rms2", ctypes.c_void_p),
+        ("router", ctypes.c_void_p),
+        ("exp_gu_q", ctypes.c_void_p),
+        ("exp_gu_s", ctypes.c_void_p),
+        ("exp_dn_q", ctypes.c_void_p),
+        ("exp_dn_s", ctypes.c_void_p),
+        ("shared_gate_up", ctypes.c_void_p),
+        ("shared_down", ctypes.c_void_p),
+        ("shared_gate", ctypes.c_void_p),
+        ("H", ctypes.c_int32),
+        ("E", ctypes.c_int32),
+        ("TOPK", ctypes.c_int32),
+        ("I", ctypes.c_int32),
+        ("Is", ctypes.c_int32),
+        ("G", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+    ]
+
+
+class MoeTrace(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("logits", "idx", "wts", "routed", "sout", "gate")]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_W = ctypes.POINTER(MoeLayerWeights)
+_SIGS = {
+    "moe_check_shape": (_I, [_W]),
+    "moe_workspace_bytes": (ctypes.c_size_t, [_W, _I]),
+    "moe_workspace_init": (_I, [_P, ctypes.c_size_t, _P]),
+    "moe_workspace_error": (_I, [_P, ctypes.c_size_t, _P]),
+    "moe_block_forward": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _I, _P]),
+    "moe_block_forward_events": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _I, ctypes.POINTER(_P), _P]),
+    "moe_event_create": (_I, [ctypes.POINTER(_P)]),
+    "moe_event_destroy": (_I, [_P]),
+    "moe_event_elapsed_ms": (_I, [_P, _P, ctypes.POINTER(ctypes.c_float)]),
+    "moe_router_topk": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _I, _P]),
+    "moe_routed_experts": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _P, _I, _P]),
+    "moe_shared_expert": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _I, _P]),
+    "moe_workspace_trace": (_I, [_W, _P, ctypes.c_size_t, _I, ctypes.POINTER(MoeTrace)]),
+    "moe_synth_normal_bf16": (_I, [_P, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
+                                   ctypes.c_float, _P]),
+    "moe_synth_int4_rows": (_I, [_P, _P, ctypes.c_int64, _I, _I, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
+                                 _P]),
+    "moe_version": (ctypes.c_char_p, []),
+}
+for _name, (_res, _args) in _SIGS.items():
+    _fn = getattr(_lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+EXPORTED = tuple(_SIGS)
+
+
+class MoeError(RuntimeError):
+    pass
+
+
+def _check(rc, what):
+    if rc != 0:
+        raise MoeError(f"{what} failed: cudaError {rc}")
+
+
+def version():
+    return _lib.moe_version().decode()
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+class Event:
+    """A CUDA timing event owned by libmoe_b200 (recordable inside graph capture through forward_events)."""
+
+    def __init__(self):
+        h = ctypes.c_void_p()
+        _check(_lib.moe_event_create(ctypes.byref(h)), "moe_event_create")
+        self.handle = h
+
+    def elapsed_ms(self, later):
+        ms = ctypes.c_float()
+        _check(_lib.moe_event_elapsed_ms(self.handle, later.handle, ctypes.byref(ms)), "moe_event_elapsed_ms")
+        return ms.value
+
+    def __del__(self):
+        if getattr(self, "handle", None) and _lib is not None:
+            _lib.moe_event_destroy(self.handle)
+            self.handle = None
+
+
+@dataclasses.dataclass(frozen=True)
+class MoeShape:
+    """Geometry of one MoE layer (the reference's pack config, convert.py:327-334) plus the INT4 group size."""
+
+    H: int = 2048
+    E: int = 256
+    TOPK: int = 8
+    I: int = 512
+    Is: int = 512
+    G: int = 64
+    eps: float = 1e-6
+
+    def expert_bytes(self):
+        """Weight + scale bytes of one routed expert (the reference's decode_weight_bytes term, qwen.cu:470)."""
+        return 2 * self.I * self.H // 2 + self.H * self.I // 2 + 2 * (2 * self.I * (self.H // self.G)
+                                                                     + self.H * (self.I // self.G))
+
+
+class MoeLayer:
+    """Device tensors of one layer in the reference's pack layout (convert.py:6-20, 388-415)."""
+
+    NAMES = ("rms2", "router", "exp_gu_q", "exp_gu_s", "exp_dn_q", "exp_dn_s", "shared_gate_up", "shared_down",
+             "shared_gate")
+
+    def __init__(self, shape: MoeShape, tensors: dict):
+        self.shape = shape
+        self.t = dict(tensors)
+        s = shape
+        expect = {
+            "rms2": ((s.H,), torch.int16), "router": ((s.E, s.H), torch.int16),
+            "exp_gu_q": ((s.E, 2 * s.I, s.H // 2), torch.uint8),
+            "exp_gu_s": ((s.E, 2 * s.I, s.H // s.G), torch.int16),
+            "exp_dn_q": ((s.E, s.H, s.I // 2), torch.uint8),
+            "exp_dn_s": ((s.E, s.H, s.I // s.G), torch.int16),
+            "shared_gate_up": ((2 * s.Is, s.H), torch.int16), "shared_down": ((s.H, s.Is), torch.int16),
+            "shared_gate": ((s.H,), torch.int16),
+        }
+        for n, (shp, dt) in expect.items():
+            v = self.t[n]
+            if tuple(v.shape) != shp or v.dtype != dt or not v.is_contiguous() or not v.is_cuda:
+                raise ValueError(f"{n}: expected contiguous cuda {dt} {shp}, got {v.dtype} {tuple(v.shape)}")
+        self.c = MoeLayerWeights(*[ctypes.c_void_p(self.t[n].data_ptr()) for n in self.NAMES],
+                                 s.H, s.E, s.TOPK, s.I, s.Is, s.G, s.eps)
+        _check(_lib.moe_check_shape(ctypes.byref(self.c)), "moe_check_shape")
+
+
+class MoeBlock:
+    """Workspace owner and launcher for one layer's MoE block (the reference's Work + forward() steps)."""
+
+    def __init__(self, layer: MoeLayer, max_T: int):
+        self.layer = layer
+        self.max_T = max_T
+        nbytes = _lib.moe_workspace_bytes(ctypes.byref(layer.c), max_T)
+        if nbytes == 0:
+            raise MoeError("moe_workspace_bytes rejected the shape")
+        self.ws_bytes = nbytes
+        dev = layer.t["router"].device
+        self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        _check(_lib.moe_workspace_init(_ptr(self.ws), nbytes, _stream(None)), "moe_workspace_init")
+        # The zeroing is stream-ordered; wait for it so the block may be used from any stream afterwards.
+        torch.cuda.current_stream(dev).synchronize()
+
+    def _args(self):
+        return ctypes.byref(self.layer.c), _ptr(self.ws), self.ws_bytes
+
+    def forward(self, hidden, attn_out, normed, next_rms1=None, T=None, stream=None):
+        """qwen.cu:429-448 for T tokens: hidden (fp32 [T,H], in/out), attn_out (bf16 bits [T,H]), normed (out)."""
+        T = hidden.shape[0] if T is None else T
+        _check(_lib.moe_block_forward(*self._args(), _ptr(hidden), _ptr(attn_out), _ptr(normed), _ptr(next_rms1),
+                                      T, _stream(stream)), "moe_block_forward")
+
+    def forward_events(self, hidden, attn_out, normed, events, next_rms1=None, T=None, stream=None):
+        """forward() that records the 4 Event handles before the block and after each of its kernels."""
+        T = hidden.shape[0] if T is None else T
+        arr = (ctypes.c_void_p * 4)(*[e.handle for e in events])
+        _check(_lib.moe_block_forward_events(*self._args(), _ptr(hidden), _ptr(attn_out), _ptr(normed),
+                                             _ptr(next_rms1), T, arr, _stream(stream)), "moe_block_forward_events")
+
+    def router_topk(self, normed, logits, idx, wts, T=None, stream=None):
+        T = normed.shape[0] if T is None else T
+        _check(_lib.moe_router_topk(*self._args(), _ptr(normed), _ptr(logits), _ptr(idx), _ptr(wts), T,
+                                    _stream(stream)), "moe_router_topk")
+
+    def routed_experts(self, normed, idx, wts, routed, inter=None, T=None, stream=None):
+        T = normed.shape[0] if T is None else T
+        _check(_lib.moe_routed_experts(*self._args(), _ptr(normed), _ptr(idx), _ptr(wts), _ptr(routed), _ptr(inter),
+                                       T, _stream(stream)), "moe_routed_experts")
+
+    def shared_expert(self, normed, sout, T=None, stream=None):
+        T = normed.shape[0] if T is None else T
+        _check(_lib.moe_shared_expert(*self._args(), _ptr(normed), _ptr(sout), T, _stream(stream)),
+               "moe_shared_expert")
+
+    def error_word(self, stream=None):
+        rc = _lib.moe_workspace_error(_ptr(self.ws), self.ws_bytes, _stream(stream))
+        if rc < 0:
+            raise MoeError(f"moe_workspace_error failed: cudaError {-rc}")
+        return rc
+
+    def trace(self, T):
+        """Device views of the last forward's intermediates (logits, idx, wts, routed, sout, gate)."""
+        tr = MoeTrace()
+        _check(_lib.moe_workspace_trace(*self._args(), T, ctypes.byref(tr)), "moe_workspace_trace")
+        s = self.layer.shape
+        base = self.ws.data_ptr()
+
+        def view(ptr, n, dtype):
+            off = ptr - base
+            nb = n * torch.empty((), dtype=dtype).element_size()
+            return self.ws[off:off + nb].view(dtype)
+
+        return {
+            "logits": view(tr.logits, T * s.E, torch.float32).view(T, s.E),
+            "idx": view(tr.idx, T * s.TOPK, torch.int32).view(T, s.TOPK),
+            "wts": view(tr.wts, T * s.TOPK, torch.float32).view(T, s.TOPK),
+            "routed": view(tr.routed, T * s.H, torch.float32).view(T, s.H),
+            "sout": view(tr.sout, T * s.H, torch.int16).view(T, s.H),
+            "gate": view(tr.gate, T, torch.float32),
+        }
+
+
+def synth_layer(shape: MoeShape, seed: int, device="cuda", std=0.02, stream=None) -> MoeLayer:
+    """Seeded synthetic layer on the device (weights bf16 N(0, std); experts INT4 with absmax/7 group scales)."""
+    s = shape
+    dev = torch.device(device)
+    st = _stream(stream)
+    t = {}
+
+    def normal(name, shp, sid, mean, sd):
+        x = torch.empty(shp, dtype=torch.int16, device=dev)
+        _check(_lib.moe_synth_normal_bf16(_ptr(x), x.numel(), seed, sid, mean, sd, st), "moe_synth_normal_bf16")
+        t[name] = x
+
+    normal("rms2", (s.H,), 1, 1.0, 0.0)
+    normal("router", (s.E, s.H), 2, 0.0, std)
+    normal("shared_gate_up", (2 * s.Is, s.H), 3, 0.0, std)
+    normal("shared_down", (s.H, s.Is), 4, 0.0, std)
+    normal("shared_gate", (s.H,), 5, 0.0, std)
+    t["exp_gu_q"] = torch.empty((s.E, 2 * s.I, s.H // 2), dtype=torch.uint8, device=dev)
+    t["exp_gu_s"] = torch.empty((s.E, 2 * s.I, s.H // s.G), dtype=torch.int16, device=dev)
+    t["exp_dn_q"] = torch.empty((s.E, s.H, s.I // 2), dtype=torch.uint8, device=dev)
+    t["exp_dn_s"] = torch.empty((s.E, s.H, s.I // s.G), dtype=torch.int16, device=dev)
+    _check(_lib.moe_synth_int4_rows(_ptr(t["exp_gu_q"]), _ptr(t["exp_gu_s"]), s.E * 2 * s.I, s.H, s.G, seed, 6, std,
+                                    st), "moe_synth_int4_rows")
+    _check(_lib.moe_synth_int4_rows(_ptr(t["exp_dn_q"]), _ptr(t["exp_dn_s"]), s.E * s.H, s.I, s.G, seed, 7, std, st),
+           "moe_synth_int4_rows")
+    return MoeLayer(shape, t)
+
+
+def synth_activations(shape: MoeShape, T: int, seed: int, device="cuda", stream=None):
+    """hidden fp32 [T,H] ~ N(0,1) (via bf16) and attn_out bf16 [T,H] ~ N(0,1), seeded."""
+    dev = torch.device(device)
+    st = _stream(stream)
+    h16 = torch.empty((T, shape.H), dtype=torch.int16, device=dev)
+    a16 = torch.empty((T, shape.H), dtype=torch.int16, device=dev)
+    _check(_lib.moe_synth_normal_bf16(_ptr(h16), h16.numel(), seed, 101, 0.0, 1.0, st), "moe_synth_normal_bf16")
+    _check(_lib.moe_synth_normal_bf16(_ptr(a16), a16.numel(), seed, 102, 0.0, 1.0, st), "moe_synth_normal_bf16")
+    hidden = (h16.to(torch.int32) << 16).view(torch.float32).contiguous()
+    return hidden, a16

@@ -1,0 +1,248 @@
+// moe_api.cu -- the extern "C" entry points declared in include/moe_block.h.
+//
+// Host-side launch code replacing the MoE part of forward() (qwen.cu:429-448) and moe() (qwen.cu:345-363).
+// Every entry point validates the shape and the workspace size before launching anything and returns
+// cudaErrorInvalidValue on a violation; no entry point allocates memory or synchronises the stream (except
+// moe_workspace_error, which reads the error word back).
+#include <algorithm>
+#include <cstring>
+
+#include "moe_common.cuh"
+#include "moe_decode.h"
+
+using namespace moe;
+
+namespace {
+
+bool shape_ok(const moe_layer_weights* w) {
+  if (!w) return false;
+  const int H = w->H, E = w->E, K = w->TOPK, I = w->I, Is = w->Is, G = w->G;
+  if (H <= 0 || E <= 0 || K <= 0 || I <= 0 || Is <= 0 || G <= 0) return false;
+  if (H % 256 || I % 128 || Is % 128) return false;
+  if (G != 32 && G != 64 && G != 128) return false;
+  if (H % G || I % G) return false;
+  if (K > 8 || E > 256 || K > E) return false;
+  if (H > 4096 || I > 2048 || Is > 2048) return false;
+  return true;
+}
+
+bool weights_present(const moe_layer_weights* w, bool router, bool routed, bool shared) {
+  if (router && (!w->router || !w->rms2)) return false;
+  if (routed && (!w->exp_gu_q || !w->exp_gu_s || !w->exp_dn_q || !w->exp_dn_s)) return false;
+  if (shared && (!w->shared_gate_up || !w->shared_down || !w->shared_gate)) return false;
+  return true;
+}
+
+BlockArgs make_args(const moe_layer_weights* w, void* ws, const WsLayout& L, int T) {
+  BlockArgs a;
+  memset(&a, 0, sizeof a);
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  a.w = *w;
+  a.T = T;
+  a.ticket = reinterpret_cast<uint32_t*>(b + L.ticket);
+  a.err = reinterpret_cast<uint32_t*>(b + L.err);
+  a.logits = reinterpret_cast<float*>(b + L.logits);
+  a.idx = reinterpret_cast<int32_t*>(b + L.idx);
+  a.wts = reinterpret_cast<float*>(b + L.wts);
+  a.gate = reinterpret_cast<float*>(b + L.gate);
+  a.nuniq = reinterpret_cast<int32_t*>(b + L.nuniq);
+  a.uniq = reinterpret_cast<int32_t*>(b + L.uniq);
+  a.uoff = reinterpret_cast<int32_t*>(b + L.uoff);
+  a.upairs = reinterpret_cast<int32_t*>(b + L.upairs);
+  a.inter = reinterpret_cast<uint16_t*>(b + L.inter);
+  a.sinter = reinterpret_cast<uint16_t*>(b + L.sinter);
+  a.routed = reinterpret_cast<float*>(b + L.routed);
+  a.sout = reinterpret_cast<uint16_t*>(b + L.sout);
+  return a;
+}
+
+WsLayout layout_for(const moe_layer_weights* w, int T) { return ws_layout(w->H, w->E, w->TOPK, w->I, w->Is, T); }
+
+// The decode kernels stage one chunk of tokens in shared memory; larger T runs chunk by chunk.
+int chunk_tokens(const moe_layer_weights* w) { return decode_max_tokens(w->H, w->TOPK, w->I, w->Is); }
+
+int check_common(const moe_layer_weights* w, void* ws, size_t bytes, int T) {
+  if (!shape_ok(w) || !ws || T < 1) return (int)cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(ws) % 256) return (int)cudaErrorInvalidValue;
+  const int Tc = std::min(T, chunk_tokens(w));
+  if (bytes < layout_for(w, Tc).total) return (int)cudaErrorInvalidValue;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_check_shape(const moe_layer_weights* w) { return shape_ok(w) ? 0 : (int)cudaErrorInvalidValue; }
+
+size_t moe_workspace_bytes(const moe_layer_weights* w, int max_T) {
+  if (!shape_ok(w) || max_T < 1) return 0;
+  return layout_for(w, max_T).total;
+}
+
+int moe_workspace_init(void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  if (!workspace || workspace_bytes == 0) return (int)cudaErrorInvalidValue;
+  return (int)cudaMemsetAsync(workspace, 0, workspace_bytes, (cudaStream_t)stream);
+}
+
+int moe_workspace_error(void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  if (!workspace || workspace_bytes < 512) return -(int)cudaErrorInvalidValue;
+  const WsLayout L = ws_layout(256, 1, 1, 128, 128, 1);  // ticket/err offsets do not depend on the geometry
+  uint32_t* errp = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + L.err);
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, errp, sizeof v, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(errp, 0, sizeof v, (cudaStream_t)stream);
+  if (e != cudaSuccess) return -(int)e;
+  return (int)v;
+}
+
+namespace {
+// Records `ev` on `s`; inside stream capture the record becomes a graph node that timestamps every replay.
+cudaError_t record_event(void* ev, cudaStream_t s) {
+  if (!ev) return cudaSuccess;
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(s, &st);
+  if (e != cudaSuccess) return e;
+  if (st == cudaStreamCaptureStatusActive)
+    return cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev), s, cudaEventRecordExternal);
+  return cudaEventRecord(static_cast<cudaEvent_t>(ev), s);
+}
+
+int block_forward_impl(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
+                       const uint16_t* attn_out, uint16_t* normed, const uint16_t* next_rms1, int T,
+                       void* const* events, cudaStream_t s) {
+  int rc = check_common(w, workspace, workspace_bytes, T);
+  if (rc) return rc;
+  if (!hidden || !attn_out || !normed || !weights_present(w, true, true, true)) return (int)cudaErrorInvalidValue;
+  const int chunk = chunk_tokens(w);
+  for (int t0 = 0; t0 < T; t0 += chunk) {
+    const int Tc = std::min(chunk, T - t0);
+    const WsLayout L = layout_for(w, Tc);
+    BlockArgs a = make_args(w, workspace, L, Tc);
+    const int64_t off = (int64_t)t0 * w->H;
+    a.hidden = hidden + off;
+    a.attn_out = attn_out + off;
+    a.normed = normed + off;
+    a.next_rms1 = next_rms1;
+    const bool first = t0 == 0, last = t0 + chunk >= T;
+    cudaError_t e = first && events ? record_event(events[0], s) : cudaSuccess;
+    if (e == cudaSuccess) e = launch_route(a, true, true, s);
+    if (e == cudaSuccess && last && events) e = record_event(events[1], s);
+    if (e == cudaSuccess) e = launch_gate_up(a, true, true, s);
+    if (e == cudaSuccess && last && events) e = record_event(events[2], s);
+    if (e == cudaSuccess) e = launch_down_combine(a, 1 | 2 | 4 | (next_rms1 ? 8 : 0), s);
+    if (e == cudaSuccess && last && events) e = record_event(events[3], s);
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
+}
+}  // namespace
+
+int moe_block_forward(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
+                      const uint16_t* attn_out, uint16_t* normed, const uint16_t* next_rms1, int T,
+                      moe_stream_t stream) {
+  return block_forward_impl(w, workspace, workspace_bytes, hidden, attn_out, normed, next_rms1, T, nullptr,
+                            (cudaStream_t)stream);
+}
+
+int moe_block_forward_events(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
+                             const uint16_t* attn_out, uint16_t* normed, const uint16_t* next_rms1, int T,
+                             void* const* events, moe_stream_t stream) {
+  if (!events) return (int)cudaErrorInvalidValue;
+  return block_forward_impl(w, workspace, workspace_bytes, hidden, attn_out, normed, next_rms1, T, events,
+                            (cudaStream_t)stream);
+}
+
+int moe_event_create(void** ev) {
+  if (!ev) return (int)cudaErrorInvalidValue;
+  return (int)cudaEventCreate(reinterpret_cast<cudaEvent_t*>(ev));
+}
+
+int moe_event_destroy(void* ev) { return (int)cudaEventDestroy(static_cast<cudaEvent_t>(ev)); }
+
+int moe_event_elapsed_ms(void* start, void* stop, float* ms) {
+  if (!ms) return (int)cudaErrorInvalidValue;
+  return (int)cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(stop));
+}
+
+int moe_router_topk(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const uint16_t* normed,
+                    float* logits, int32_t* idx, float* wts, int T, moe_stream_t stream) {
+  int rc = check_common(w, workspace, workspace_bytes, T);
+  if (rc) return rc;
+  if (!normed || !logits || !idx || !wts || !w->router) return (int)cudaErrorInvalidValue;
+  const int chunk = chunk_tokens(w);
+  for (int t0 = 0; t0 < T; t0 += chunk) {
+    const int Tc = std::min(chunk, T - t0);
+    BlockArgs a = make_args(w, workspace, layout_for(w, Tc), Tc);
+    a.normed = const_cast<uint16_t*>(normed) + (int64_t)t0 * w->H;
+    a.logits = logits + (int64_t)t0 * w->E;
+    a.idx = idx + (int64_t)t0 * w->TOPK;
+    a.wts = wts + (int64_t)t0 * w->TOPK;
+    cudaError_t e = launch_route(a, false, false, (cudaStream_t)stream);
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
+}
+
+int moe_routed_experts(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const uint16_t* normed,
+                       const int32_t* idx, const float* wts, float* routed, uint16_t* inter_out, int T,
+                       moe_stream_t stream) {
+  int rc = check_common(w, workspace, workspace_bytes, T);
+  if (rc) return rc;
+  if (!normed || !idx || !wts || !routed || !weights_present(w, false, true, false)) return (int)cudaErrorInvalidValue;
+  const cudaStream_t s = (cudaStream_t)stream;
+  const int chunk = chunk_tokens(w);
+  for (int t0 = 0; t0 < T; t0 += chunk) {
+    const int Tc = std::min(chunk, T - t0);
+    BlockArgs a = make_args(w, workspace, layout_for(w, Tc), Tc);
+    a.normed = const_cast<uint16_t*>(normed) + (int64_t)t0 * w->H;
+    a.idx = const_cast<int32_t*>(idx) + (int64_t)t0 * w->TOPK;
+    a.wts = const_cast<float*>(wts) + (int64_t)t0 * w->TOPK;
+    a.routed = routed + (int64_t)t0 * w->H;
+    if (inter_out) a.inter = inter_out + (int64_t)t0 * w->TOPK * w->I;
+    cudaError_t e = launch_route_table(a, s);
+    if (e == cudaSuccess) e = launch_gate_up(a, true, false, s);
+    if (e == cudaSuccess) e = launch_down_combine(a, 1, s);
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
+}
+
+int moe_shared_expert(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const uint16_t* normed,
+                      uint16_t* sout, int T, moe_stream_t stream) {
+  int rc = check_common(w, workspace, workspace_bytes, T);
+  if (rc) return rc;
+  if (!normed || !sout || !weights_present(w, false, false, true)) return (int)cudaErrorInvalidValue;
+  const cudaStream_t s = (cudaStream_t)stream;
+  const int chunk = chunk_tokens(w);
+  for (int t0 = 0; t0 < T; t0 += chunk) {
+    const int Tc = std::min(chunk, T - t0);
+    BlockArgs a = make_args(w, workspace, layout_for(w, Tc), Tc);
+    a.normed = const_cast<uint16_t*>(normed) + (int64_t)t0 * w->H;
+    a.sout = sout + (int64_t)t0 * w->H;
+    cudaError_t e = launch_gate_up(a, false, true, s);
+    if (e == cudaSuccess) e = launch_down_combine(a, 2, s);
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
+}
+
+int moe_workspace_trace(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, int T, moe_trace* out) {
+  if (!shape_ok(w) || !workspace || !out || T < 1 || T > chunk_tokens(w)) return (int)cudaErrorInvalidValue;
+  const int Tc = T;
+  const WsLayout L = layout_for(w, Tc);
+  if (workspace_bytes < L.total) return (int)cudaErrorInvalidValue;
+  const BlockArgs a = make_args(w, workspace, L, Tc);
+  out->logits = a.logits;
+  out->idx = a.idx;
+  out->wts = a.wts;
+  out->routed = a.routed;
+  out->sout = a.sout;
+  out->gate = a.gate;
+  return 0;
+}
+
+const char* moe_version(void) { return "moe_b200 0.1 sm_100a"; }
+
+}  // extern "C"

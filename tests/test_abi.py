@@ -1,0 +1,78 @@
+"""CPU tests of the C-ABI library: it loads, exports every entry point include/moe_block.h declares, and its
+host-side shape and workspace checks behave. No kernel is launched here."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "moe_block.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^MOE_API\s+[\w\s\*]+?\b(moe_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    import mvcc_b200
+    names = _declared()
+    assert len(names) >= 10
+    lib = ctypes.CDLL(mvcc_b200.LIB_PATH)
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) <= set(mvcc_b200.EXPORTED)
+
+
+def test_version():
+    import mvcc_b200
+    assert "sm_100a" in mvcc_b200.version()
+
+
+def _w(**kw):
+    import mvcc_b200
+    d = dict(H=2048, E=256, TOPK=8, I=512, Is=512, G=64, eps=1e-6)
+    d.update(kw)
+    return mvcc_b200.MoeLayerWeights(*([None] * 9), d["H"], d["E"], d["TOPK"], d["I"], d["Is"], d["G"], d["eps"])
+
+
+@pytest.mark.parametrize("kw,ok", [
+    ({}, True), ({"G": 128}, True), ({"G": 32}, True), ({"H": 1024, "E": 32}, True),
+    ({"G": 48}, False), ({"H": 2000}, False), ({"TOPK": 9}, False), ({"E": 512}, False), ({"I": 500}, False),
+    ({"TOPK": 0}, False), ({"E": 4, "TOPK": 8}, False),
+])
+def test_shape_check(kw, ok):
+    import mvcc_b200
+    rc = mvcc_b200._lib.moe_check_shape(ctypes.byref(_w(**kw)))
+    assert (rc == 0) == ok
+
+
+def test_workspace_bytes_monotone_and_aligned():
+    import mvcc_b200
+    w = _w()
+    prev = 0
+    for T in (1, 2, 16, 128, 4096):
+        b = mvcc_b200._lib.moe_workspace_bytes(ctypes.byref(w), T)
+        assert b > prev and b % 256 == 0
+        prev = b
+    assert mvcc_b200._lib.moe_workspace_bytes(ctypes.byref(_w(G=48)), 1) == 0
+
+
+def test_entry_points_reject_bad_arguments_before_launch():
+    """Invalid shapes, null workspaces and T < 1 return cudaErrorInvalidValue without touching the GPU."""
+    import mvcc_b200
+    lib = mvcc_b200._lib
+    w = _w()
+    assert lib.moe_block_forward(ctypes.byref(w), None, 0, None, None, None, None, 1, None) == 1
+    assert lib.moe_block_forward(ctypes.byref(_w(G=48)), ctypes.c_void_p(256), 1 << 30, None, None, None, None, 1,
+                                 None) == 1
+    assert lib.moe_router_topk(ctypes.byref(w), ctypes.c_void_p(256), 1 << 30, None, None, None, None, 0, None) == 1
+    # misaligned workspace
+    assert lib.moe_shared_expert(ctypes.byref(w), ctypes.c_void_p(8), 1 << 30, None, None, 1, None) == 1
+
+
+def test_expert_bytes_match_reference_formula():
+    """decode_weight_bytes (qwen.cu:463-477) at G=64: 1,671,168 bytes per routed expert."""
+    import mvcc_b200
+    assert mvcc_b200.MoeShape().expert_bytes() == 1_671_168

@@ -1,0 +1,69 @@
+"""Pins the CPU oracle to golden vectors produced by the reference's own CUDA kernels (examples/qwen/kernels.cuh,
+run on a B200 by tests/golden/make_golden.py). Inputs are regenerated from the committed seeds and checked
+against the stored SHA-256 first, so a drifting generator fails loudly instead of comparing different inputs.
+The reference takes its decode kernels for T < 8 and its sort + tile kernels for T >= 8 (qwen.cu:347); the oracle
+is run in the same mode. Bars: routing indices identical wherever the 8th/9th logit margin exceeds the logit
+difference, int4 outputs within 2e-2, bf16 outputs within 1e-2 (max relative error)."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+META = json.load(open(os.path.join(HERE, "ref_block_meta.json")))
+
+
+def _gen():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(HERE, "make_golden.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+G = _gen()
+SHAPE = O.Shape(**META["shape"])
+
+
+@pytest.fixture(scope="module")
+def layer():
+    L = O.make_layer(SHAPE, META["layer_seed"])
+    assert G.layer_digest(L) == META["layer_sha256"], "input generator drifted from the golden vectors"
+    return L
+
+
+@pytest.mark.parametrize("name", sorted(META["cases"]))
+def test_oracle_matches_reference_golden(orc, layer, name):
+    case = META["cases"][name]
+    T = case["T"]
+    hidden, attn, nr = G.case_inputs(SHAPE, T, case["seed"], case["next"])
+    assert G.digest(hidden, attn, nr) == case["inputs_sha256"]
+    ref = dict(np.load(os.path.join(HERE, f"ref_block_{name}.npz")))
+    out = orc.block_forward(SHAPE, layer, hidden, attn, next_rms1=nr, mode=-1)
+    s = SHAPE
+    dl = np.abs(out["logits"] - ref["logits"]).max(axis=1)
+    assert O.max_rel_err(out["logits"], ref["logits"]) < 2e-3
+    srt = np.sort(ref["logits"], axis=1)[:, ::-1]
+    ok = (srt[:, s.TOPK - 1] - srt[:, s.TOPK]) > 2 * dl + 1e-6
+    assert ok.mean() >= 0.5
+    assert np.array_equal(out["idx"][ok], ref["idx"][ok])
+    assert np.allclose(out["wts"][ok], ref["wts"][ok], rtol=1e-3, atol=1e-6)
+    assert O.max_rel_err(out["routed"][ok], ref["routed"][ok]) < 2e-2
+    assert O.max_rel_err(O.bf16_to_f32(out["sout"]), O.bf16_to_f32(ref["sout"])) < 1e-2
+    assert O.max_rel_err(out["hidden"][ok], ref["hidden"][ok]) < 1e-2
+    assert O.max_rel_err(O.bf16_to_f32(out["normed"][ok]), O.bf16_to_f32(ref["normed"][ok])) < 1e-2
+    if "inter" in ref:
+        gi = O.bf16_to_f32(out["inter"][ok])
+        assert O.max_rel_err(gi, O.bf16_to_f32(ref["inter"][ok])) < 1e-2
+
+
+def test_golden_routing_is_a_pure_function_of_logits(orc):
+    """The reference's top-k rule applied by the oracle to the reference's own logits reproduces its indices."""
+    for name in META["cases"]:
+        ref = np.load(os.path.join(HERE, f"ref_block_{name}.npz"))
+        idx, wts = orc.topk(ref["logits"], SHAPE.TOPK)
+        assert np.array_equal(idx, ref["idx"])
+        assert np.allclose(wts, ref["wts"], rtol=2e-6, atol=1e-8)
