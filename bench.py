@@ -161,10 +161,12 @@ def capture(fn, steps, stream):
     return g
 
 
-def run_graphs(graphs_counts):
-    for g, n in graphs_counts:
-        for _ in range(n):
-            g.replay()
+def run_graphs(graphs_counts, stream):
+    """Replays on `stream` (CUDAGraph.replay launches on the current stream)."""
+    with torch.cuda.stream(stream):
+        for g, n in graphs_counts:
+            for _ in range(n):
+                g.replay()
 
 
 def b200_arm(args, rank, world, local):
@@ -204,7 +206,7 @@ def b200_arm(args, rank, world, local):
     rem = K % S
     g_rem = capture(step, rem, stream) if rem else None
     plan = [(g_main, K // S)] + ([(g_rem, 1)] if g_rem else [])
-    g_main.replay()  # graph upload, untimed
+    run_graphs([(g_main, 1)], stream)  # graph upload, untimed
     torch.cuda.synchronize()
 
     clocks = ClockSampler(dev)
@@ -215,7 +217,7 @@ def b200_arm(args, rank, world, local):
     torch.cuda.synchronize()
     t0 = time.time()
     e0.record(stream)
-    run_graphs(plan)
+    run_graphs(plan, stream)
     e1.record(stream)
     torch.cuda.synchronize()
     t1 = time.time()
@@ -228,12 +230,12 @@ def b200_arm(args, rank, world, local):
     evs = [[m.Event() for _ in range(4)] for _ in range(S)]
     g_ev = capture(lambda i: blocks[i % LAYER_COPIES].forward_events(hidden, attn, normed, evs[i], stream=stream),
                    S, stream)
-    g_ev.replay()
+    run_graphs([(g_ev, 1)], stream)
     torch.cuda.synchronize()
     reps = max(1, min(K // S, 8))
     acc = np.zeros(3)
     for _ in range(reps):
-        g_ev.replay()
+        run_graphs([(g_ev, 1)], stream)
         torch.cuda.synchronize()
         for e in evs:
             acc += [e[0].elapsed_ms(e[1]), e[1].elapsed_ms(e[2]), e[2].elapsed_ms(e[3])]
@@ -255,12 +257,12 @@ def b200_arm(args, rank, world, local):
     ge = capture(e2e_step, S, stream)
     ge_rem = capture(e2e_step, rem, stream) if rem else None
     plan_e = [(ge, K // S)] + ([(ge_rem, 1)] if ge_rem else [])
-    ge.replay()
+    run_graphs([(ge, 1)], stream)
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     e0.record(stream)
-    run_graphs(plan_e)
+    run_graphs(plan_e, stream)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
