@@ -102,6 +102,17 @@ MOE_API int moe_routed_experts(const moe_layer_weights* w, void* workspace, size
 MOE_API int moe_shared_expert(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const uint16_t* normed,
                       uint16_t* sout, int T, moe_stream_t stream);
 
+/* moe_router_topk without a workspace, for callers that cannot allocate device memory: a host runtime that owns all
+ * device memory through its own allocator and forbids allocations after start-up has no workspace of ours to pass.
+ * No counterpart in the reference. Same outputs as moe_router_topk; its scratch (ticket, error word, unique-expert
+ * table: at most 3.6 KiB for E <= 256, TOPK <= 8) lives in a fixed 8 KiB array in the library's device memory,
+ * held on every GPU that loads the library until exit; shapes whose scratch would not fit are rejected with
+ * cudaErrorInvalidValue. The first call on each device looks up the array's device address (cudaGetSymbolAddress),
+ * so make it before any stream capture. All calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller. Allocates nothing. */
+MOE_API int moe_router_topk_noalloc(const moe_layer_weights* w, const uint16_t* normed, float* logits, int32_t* idx,
+                                    float* wts, int T, moe_stream_t stream);
+
 /* Intermediates of the last moe_block_forward of T tokens on this workspace (device pointers into it, valid until
  * the next call): logits [T,E], idx [T,TOPK], wts [T,TOPK], routed [T,H] fp32, sout [T,H] bf16, gate [T] fp32.
  * Only for T up to the decode chunk (16 tokens at the Qwen3.5-MoE geometry); larger T returns

@@ -62,6 +62,7 @@ _SIGS = {
     "moe_event_destroy": (_I, [_P]),
     "moe_event_elapsed_ms": (_I, [_P, _P, ctypes.POINTER(ctypes.c_float)]),
     "moe_router_topk": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _I, _P]),
+    "moe_router_topk_noalloc": (_I, [_W, _P, _P, _P, _P, _I, _P]),
     "moe_routed_experts": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _P, _I, _P]),
     "moe_shared_expert": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _I, _P]),
     "moe_workspace_trace": (_I, [_W, _P, ctypes.c_size_t, _I, ctypes.POINTER(MoeTrace)]),
@@ -239,6 +240,14 @@ class MoeBlock:
             "sout": view(tr.sout, T * s.H, torch.int16).view(T, s.H),
             "gate": view(tr.gate, T, torch.float32),
         }
+
+
+def router_topk_noalloc(layer: MoeLayer, normed, logits, idx, wts, T=None, stream=None):
+    """Router + top-k with no workspace (moe_router_topk_noalloc): for callers that cannot allocate device memory.
+    Calls that overlap on the GPU share the library's fixed scratch and must be serialised."""
+    T = normed.shape[0] if T is None else T
+    _check(_lib.moe_router_topk_noalloc(ctypes.byref(layer.c), _ptr(normed), _ptr(logits), _ptr(idx), _ptr(wts), T,
+                                        _stream(stream)), "moe_router_topk_noalloc")
 
 
 def synth_layer(shape: MoeShape, seed: int, device="cuda", std=0.02, stream=None) -> MoeLayer:
