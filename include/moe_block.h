@@ -62,7 +62,9 @@ MOE_API int moe_workspace_init(void* workspace, size_t workspace_bytes, moe_stre
 /* Reads (synchronously) and clears the workspace error word: 0 = no error recorded, else a code of moe_errc. */
 MOE_API int moe_workspace_error(void* workspace, size_t workspace_bytes, moe_stream_t stream);
 
-enum moe_errc { MOE_ERR_NONE = 0, MOE_ERR_EXPERT_INDEX = 1, MOE_ERR_SHAPE = 2 };
+/* Error-word bits. MOE_ERR_BARRIER: a grid barrier of the fused decode kernel gave up waiting (bounded spin); the
+ * call's results are invalid and the workspace must be re-initialised with moe_workspace_init. */
+enum moe_errc { MOE_ERR_NONE = 0, MOE_ERR_EXPERT_INDEX = 1, MOE_ERR_SHAPE = 2, MOE_ERR_BARRIER = 4 };
 
 /* The whole block, replacing qwen.cu:429-448 for one layer:
  *   hidden[T,H] (fp32, in/out)  += attn_out[T,H] (bf16)                      residual_rmsnorm, qwen.cu:429

@@ -7,8 +7,11 @@
 #include <algorithm>
 #include <cstring>
 
+#include <cstdlib>
+
 #include "moe_common.cuh"
 #include "moe_decode.h"
+#include "moe_fused.h"
 
 using namespace moe;
 
@@ -109,12 +112,38 @@ cudaError_t record_event(void* ev, cudaStream_t s) {
   return cudaEventRecord(static_cast<cudaEvent_t>(ev), s);
 }
 
+// The fused single-launch decode kernel serves T <= kFusedMaxT unless the environment sets MOE_B200_FUSED=0
+// (read once per process), which selects the three-kernel path.
+bool fused_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("MOE_B200_FUSED");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 int block_forward_impl(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
                        const uint16_t* attn_out, uint16_t* normed, const uint16_t* next_rms1, int T,
                        void* const* events, cudaStream_t s) {
   int rc = check_common(w, workspace, workspace_bytes, T);
   if (rc) return rc;
   if (!hidden || !attn_out || !normed || !weights_present(w, true, true, true)) return (int)cudaErrorInvalidValue;
+  int fs = 0, frows = 0;
+  size_t fsmem = 0;
+  if (fused_enabled() && fused_config(*w, T, &fs, &fsmem, &frows)) {
+    const WsLayout L = layout_for(w, T);
+    BlockArgs a = make_args(w, workspace, L, T);
+    a.hidden = hidden;
+    a.attn_out = attn_out;
+    a.normed = normed;
+    a.next_rms1 = next_rms1;
+    unsigned long long* gbar = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) + L.gbar);
+    cudaError_t e = events ? record_event(events[0], s) : cudaSuccess;
+    if (e == cudaSuccess) e = launch_fused_decode(a, gbar, next_rms1 != nullptr, s);
+    for (int k = 1; k < 4 && events && e == cudaSuccess; ++k) e = record_event(events[k], s);
+    return (int)e;
+  }
   const int chunk = chunk_tokens(w);
   for (int t0 = 0; t0 < T; t0 += chunk) {
     const int Tc = std::min(chunk, T - t0);

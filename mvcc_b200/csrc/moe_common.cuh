@@ -132,7 +132,7 @@ __device__ __forceinline__ void lds_pairs(const void* p, u64& a, u64& b) {
 
 // Offsets (bytes) of the sections of the caller-owned workspace; every section is 256-byte aligned.
 struct WsLayout {
-  size_t ticket, err, logits, idx, wts, gate, nuniq, uniq, uoff, upairs, inter, sinter, routed, sout, total;
+  size_t ticket, err, gbar, logits, idx, wts, gate, nuniq, uniq, uoff, upairs, inter, sinter, routed, sout, total;
   int maxT;
 };
 
@@ -145,6 +145,7 @@ __host__ __device__ inline WsLayout ws_layout(int H, int E, int TOPK, int I, int
   L.maxT = maxT;
   L.ticket = o; o = ws_align(o + 16 * sizeof(uint32_t));
   L.err = o;    o = ws_align(o + sizeof(uint32_t));
+  L.gbar = o;   o = ws_align(o + sizeof(unsigned long long));  // fixed offset: shared by every T
   L.logits = o; o = ws_align(o + sizeof(float) * (size_t)maxT * E);
   L.idx = o;    o = ws_align(o + sizeof(int32_t) * pairs);
   L.wts = o;    o = ws_align(o + sizeof(float) * pairs);
