@@ -63,8 +63,9 @@ MOE_API int moe_workspace_init(void* workspace, size_t workspace_bytes, moe_stre
 MOE_API int moe_workspace_error(void* workspace, size_t workspace_bytes, moe_stream_t stream);
 
 /* Error-word bits. MOE_ERR_BARRIER: a grid barrier of the fused decode kernel gave up waiting (bounded spin); the
- * call's results are invalid and the workspace must be re-initialised with moe_workspace_init. */
-enum moe_errc { MOE_ERR_NONE = 0, MOE_ERR_EXPERT_INDEX = 1, MOE_ERR_SHAPE = 2, MOE_ERR_BARRIER = 4 };
+ * call's results are invalid and the workspace must be re-initialised with moe_workspace_init. MOE_ERR_TIMEOUT: a
+ * bounded pipeline wait inside a prefill GEMM tile gave up; that call's results are invalid. */
+enum moe_errc { MOE_ERR_NONE = 0, MOE_ERR_EXPERT_INDEX = 1, MOE_ERR_SHAPE = 2, MOE_ERR_BARRIER = 4, MOE_ERR_TIMEOUT = 8 };
 
 /* The whole block, replacing qwen.cu:429-448 for one layer:
  *   hidden[T,H] (fp32, in/out)  += attn_out[T,H] (bf16)                      residual_rmsnorm, qwen.cu:429
@@ -116,9 +117,11 @@ MOE_API int moe_router_topk_noalloc(const moe_layer_weights* w, const uint16_t* 
                                     float* wts, int T, moe_stream_t stream);
 
 /* Intermediates of the last moe_block_forward of T tokens on this workspace (device pointers into it, valid until
- * the next call): logits [T,E], idx [T,TOPK], wts [T,TOPK], routed [T,H] fp32, sout [T,H] bf16, gate [T] fp32.
- * Only for T up to the decode chunk (16 tokens at the Qwen3.5-MoE geometry); larger T returns
- * cudaErrorInvalidValue because the intermediates are produced chunk by chunk. */
+ * the next call): logits [T,E], idx [T,TOPK], wts [T,TOPK], routed [T,H] fp32, sout [T,H] bf16, gate [T] fp32; on
+ * the prefill path (T >= the prefill threshold) also the expert sort: sorted [T*TOPK] (pair indices t*TOPK+slot
+ * grouped by expert, ascending within an expert) and offsets [E+1] (NULL on the decode path). Decode calls above the
+ * decode chunk (16 tokens at the Qwen3.5-MoE geometry) return cudaErrorInvalidValue: their intermediates are
+ * produced chunk by chunk. */
 typedef struct moe_trace {
   const float* logits;
   const int32_t* idx;
@@ -126,9 +129,19 @@ typedef struct moe_trace {
   const float* routed;
   const uint16_t* sout;
   const float* gate;
+  const int32_t* sorted;
+  const int32_t* offsets;
 } moe_trace;
 MOE_API int moe_workspace_trace(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, int T,
                         moe_trace* out);
+
+/* Path selection. Calls with T >= the prefill threshold (default 8, the reference's switch from the GEMV kernels
+ * to the sort + tile kernels in moe(), qwen.cu:347) take the prefill path: tcgen05 tile GEMMs with the reference's
+ * tile numerics (weights dequantized to bf16, fp32 accumulation, per-slot partials summed in slot order). Smaller T
+ * takes the decode kernels. This sets the threshold for the whole process (0 restores the default; values below 8
+ * act as 8; INT_MAX keeps every call on the decode kernels, chunk by chunk). The environment variable
+ * MOE_B200_PREFILL=0 makes INT_MAX the default. No reference counterpart (the reference hard-codes 8). */
+MOE_API int moe_set_prefill_min_tokens(int T);
 
 /* ---- synthetic inputs for tests and the benchmark (no reference counterpart: the reference loads GPTQ
  * checkpoints through convert.py; these fill the same layout from a counter-based generator, seeded). */

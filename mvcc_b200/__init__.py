@@ -45,7 +45,8 @@ class MoeLayerWeights(ctypes.Structure):
 
 
 class MoeTrace(ctypes.Structure):
-    _fields_ = [(n, ctypes.c_void_p) for n in ("logits", "idx", "wts", "routed", "sout", "gate")]
+    _fields_ = [(n, ctypes.c_void_p) for n in ("logits", "idx", "wts", "routed", "sout", "gate", "sorted",
+                                               "offsets")]
 
 
 _P = ctypes.c_void_p
@@ -66,6 +67,7 @@ _SIGS = {
     "moe_routed_experts": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _P, _I, _P]),
     "moe_shared_expert": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _I, _P]),
     "moe_workspace_trace": (_I, [_W, _P, ctypes.c_size_t, _I, ctypes.POINTER(MoeTrace)]),
+    "moe_set_prefill_min_tokens": (_I, [_I]),
     "moe_synth_normal_bf16": (_I, [_P, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                    ctypes.c_float, _P]),
     "moe_synth_int4_rows": (_I, [_P, _P, ctypes.c_int64, _I, _I, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
@@ -232,7 +234,7 @@ class MoeBlock:
             nb = n * torch.empty((), dtype=dtype).element_size()
             return self.ws[off:off + nb].view(dtype)
 
-        return {
+        out = {
             "logits": view(tr.logits, T * s.E, torch.float32).view(T, s.E),
             "idx": view(tr.idx, T * s.TOPK, torch.int32).view(T, s.TOPK),
             "wts": view(tr.wts, T * s.TOPK, torch.float32).view(T, s.TOPK),
@@ -240,6 +242,16 @@ class MoeBlock:
             "sout": view(tr.sout, T * s.H, torch.int16).view(T, s.H),
             "gate": view(tr.gate, T, torch.float32),
         }
+        if tr.sorted:  # prefill path: the stable expert sort
+            out["sorted"] = view(tr.sorted, T * s.TOPK, torch.int32)
+            out["offsets"] = view(tr.offsets, s.E + 1, torch.int32)
+        return out
+
+
+def set_prefill_min_tokens(T: int):
+    """Process-wide token count from which calls take the prefill path (0 = default 8; a huge value keeps every
+    call on the decode kernels)."""
+    _check(_lib.moe_set_prefill_min_tokens(int(T)), "moe_set_prefill_min_tokens")
 
 
 def router_topk_noalloc(layer: MoeLayer, normed, logits, idx, wts, T=None, stream=None):

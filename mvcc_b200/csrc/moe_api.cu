@@ -5,6 +5,8 @@
 // cudaErrorInvalidValue on a violation; no entry point allocates memory or synchronises the stream (except
 // moe_workspace_error, which reads the error word back).
 #include <algorithm>
+#include <atomic>
+#include <climits>
 #include <cstring>
 
 #include <cstdlib>
@@ -12,6 +14,7 @@
 #include "moe_common.cuh"
 #include "moe_decode.h"
 #include "moe_fused.h"
+#include "moe_prefill.h"
 
 using namespace moe;
 
@@ -56,6 +59,18 @@ BlockArgs make_args(const moe_layer_weights* w, void* ws, const WsLayout& L, int
   a.sinter = reinterpret_cast<uint16_t*>(b + L.sinter);
   a.routed = reinterpret_cast<float*>(b + L.routed);
   a.sout = reinterpret_cast<uint16_t*>(b + L.sout);
+  if (L.maxT >= kPrefillMinT) {
+    a.bits = reinterpret_cast<uint32_t*>(b + L.bits);
+    a.wpre = reinterpret_cast<uint32_t*>(b + L.wpre);
+    a.counts = reinterpret_cast<int32_t*>(b + L.counts);
+    a.offsets = reinterpret_cast<int32_t*>(b + L.offsets);
+    a.tiles = b + L.tiles;
+    a.ntiles = reinterpret_cast<int32_t*>(b + L.ntiles);
+    a.sorted = reinterpret_cast<int32_t*>(b + L.sorted);
+    a.slot = reinterpret_cast<float*>(b + L.slot);
+    a.nwp = L.nwp;
+    a.max_tiles = L.max_tiles;
+  }
   return a;
 }
 
@@ -64,11 +79,28 @@ WsLayout layout_for(const moe_layer_weights* w, int T) { return ws_layout(w->H, 
 // The decode kernels stage one chunk of tokens in shared memory; larger T runs chunk by chunk.
 int chunk_tokens(const moe_layer_weights* w) { return decode_max_tokens(w->H, w->TOPK, w->I, w->Is); }
 
+// T >= kPrefillMinT takes the prefill path (tcgen05 GEMMs, the reference's tile numerics) unless the environment
+// sets MOE_B200_PREFILL=0 (read once per process), which keeps the decode kernels, chunk by chunk.
+// moe_set_prefill_min_tokens moves the threshold (0 restores the default).
+std::atomic<int> g_prefill_min{0};
+int prefill_min_tokens() {
+  int v = g_prefill_min.load(std::memory_order_relaxed);
+  if (v == 0) {
+    const char* e = getenv("MOE_B200_PREFILL");
+    v = (e && e[0] == '0') ? INT_MAX : kPrefillMinT;
+  }
+  return v;
+}
+bool use_prefill(const moe_layer_weights* w, int T) {
+  return T >= kPrefillMinT && T >= prefill_min_tokens() && prefill_supported(*w);
+}
+// Tokens the workspace layout of one call is computed for.
+int layout_tokens(const moe_layer_weights* w, int T) { return use_prefill(w, T) ? T : std::min(T, chunk_tokens(w)); }
+
 int check_common(const moe_layer_weights* w, void* ws, size_t bytes, int T) {
   if (!shape_ok(w) || !ws || T < 1) return (int)cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(ws) % 256) return (int)cudaErrorInvalidValue;
-  const int Tc = std::min(T, chunk_tokens(w));
-  if (bytes < layout_for(w, Tc).total) return (int)cudaErrorInvalidValue;
+  if (bytes < layout_for(w, layout_tokens(w, T)).total) return (int)cudaErrorInvalidValue;
   return 0;
 }
 
@@ -129,6 +161,17 @@ int block_forward_impl(const moe_layer_weights* w, void* workspace, size_t works
   int rc = check_common(w, workspace, workspace_bytes, T);
   if (rc) return rc;
   if (!hidden || !attn_out || !normed || !weights_present(w, true, true, true)) return (int)cudaErrorInvalidValue;
+  if (use_prefill(w, T)) {
+    BlockArgs a = make_args(w, workspace, layout_for(w, T), T);
+    a.hidden = hidden;
+    a.attn_out = attn_out;
+    a.normed = normed;
+    a.next_rms1 = next_rms1;
+    cudaError_t e = events ? record_event(events[0], s) : cudaSuccess;
+    if (e == cudaSuccess) e = prefill_block(a, s);
+    for (int k = 1; k < 4 && events && e == cudaSuccess; ++k) e = record_event(events[k], s);
+    return (int)e;
+  }
   int fs = 0, frows = 0;
   size_t fsmem = 0;
   if (fused_enabled() && fused_config(*w, T, &fs, &fsmem, &frows)) {
@@ -200,6 +243,14 @@ int moe_router_topk(const moe_layer_weights* w, void* workspace, size_t workspac
   int rc = check_common(w, workspace, workspace_bytes, T);
   if (rc) return rc;
   if (!normed || !logits || !idx || !wts || !w->router) return (int)cudaErrorInvalidValue;
+  if (use_prefill(w, T)) {
+    BlockArgs a = make_args(w, workspace, layout_for(w, T), T);
+    a.normed = const_cast<uint16_t*>(normed);
+    a.logits = logits;
+    a.idx = idx;
+    a.wts = wts;
+    return (int)prefill_router(a, (cudaStream_t)stream);
+  }
   const int chunk = chunk_tokens(w);
   for (int t0 = 0; t0 < T; t0 += chunk) {
     const int Tc = std::min(chunk, T - t0);
@@ -221,6 +272,14 @@ int moe_routed_experts(const moe_layer_weights* w, void* workspace, size_t works
   if (rc) return rc;
   if (!normed || !idx || !wts || !routed || !weights_present(w, false, true, false)) return (int)cudaErrorInvalidValue;
   const cudaStream_t s = (cudaStream_t)stream;
+  if (use_prefill(w, T)) {
+    BlockArgs a = make_args(w, workspace, layout_for(w, T), T);
+    a.normed = const_cast<uint16_t*>(normed);
+    a.idx = const_cast<int32_t*>(idx);
+    a.wts = const_cast<float*>(wts);
+    a.routed = routed;
+    return (int)prefill_routed(a, inter_out, s);
+  }
   const int chunk = chunk_tokens(w);
   for (int t0 = 0; t0 < T; t0 += chunk) {
     const int Tc = std::min(chunk, T - t0);
@@ -244,6 +303,12 @@ int moe_shared_expert(const moe_layer_weights* w, void* workspace, size_t worksp
   if (rc) return rc;
   if (!normed || !sout || !weights_present(w, false, false, true)) return (int)cudaErrorInvalidValue;
   const cudaStream_t s = (cudaStream_t)stream;
+  if (use_prefill(w, T)) {
+    BlockArgs a = make_args(w, workspace, layout_for(w, T), T);
+    a.normed = const_cast<uint16_t*>(normed);
+    a.sout = sout;
+    return (int)prefill_shared(a, s);
+  }
   const int chunk = chunk_tokens(w);
   for (int t0 = 0; t0 < T; t0 += chunk) {
     const int Tc = std::min(chunk, T - t0);
@@ -258,7 +323,8 @@ int moe_shared_expert(const moe_layer_weights* w, void* workspace, size_t worksp
 }
 
 int moe_workspace_trace(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, int T, moe_trace* out) {
-  if (!shape_ok(w) || !workspace || !out || T < 1 || T > chunk_tokens(w)) return (int)cudaErrorInvalidValue;
+  if (!shape_ok(w) || !workspace || !out || T < 1 || (T > chunk_tokens(w) && !use_prefill(w, T)))
+    return (int)cudaErrorInvalidValue;
   const int Tc = T;
   const WsLayout L = layout_for(w, Tc);
   if (workspace_bytes < L.total) return (int)cudaErrorInvalidValue;
@@ -269,6 +335,15 @@ int moe_workspace_trace(const moe_layer_weights* w, void* workspace, size_t work
   out->routed = a.routed;
   out->sout = a.sout;
   out->gate = a.gate;
+  const bool pf = use_prefill(w, T);
+  out->sorted = pf ? a.sorted : nullptr;
+  out->offsets = pf ? a.offsets : nullptr;
+  return 0;
+}
+
+int moe_set_prefill_min_tokens(int T) {
+  if (T < 0) return (int)cudaErrorInvalidValue;
+  g_prefill_min.store(T, std::memory_order_relaxed);
   return 0;
 }
 

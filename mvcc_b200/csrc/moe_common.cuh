@@ -132,9 +132,19 @@ __device__ __forceinline__ void lds_pairs(const void* p, u64& a, u64& b) {
 
 // Offsets (bytes) of the sections of the caller-owned workspace; every section is 256-byte aligned.
 struct WsLayout {
-  size_t ticket, err, gbar, logits, idx, wts, gate, nuniq, uniq, uoff, upairs, inter, sinter, routed, sout, total;
-  int maxT;
+  size_t ticket, err, gbar, logits, idx, wts, gate, nuniq, uniq, uoff, upairs, inter, sinter, routed, sout;
+  // prefill sections (present when maxT >= kPrefillMinT): per-expert pair bitmaps and their word prefixes, expert
+  // counts and offsets, the grouped-GEMM tile list, the pairs sorted by expert, the per-pair down partials
+  size_t bits, wpre, counts, offsets, tiles, ntiles, sorted, slot;
+  size_t total;
+  int maxT, nwp, max_tiles;
 };
+
+// The reference switches moe() to its sort + tile path at T >= 8 (qwen.cu:347); so does this library.
+constexpr int kPrefillMinT = 8;
+
+// Upper bound of the grouped-GEMM tiles (128 pairs each) for P pairs over E experts: sum_e ceil(n_e / 128).
+__host__ __device__ inline int prefill_max_tiles(int P, int E) { return P / 128 + (E < P ? E : P) + 1; }
 
 __host__ __device__ inline size_t ws_align(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -158,12 +168,25 @@ __host__ __device__ inline WsLayout ws_layout(int H, int E, int TOPK, int I, int
   L.sinter = o; o = ws_align(o + sizeof(uint16_t) * (size_t)maxT * Is);
   L.routed = o; o = ws_align(o + sizeof(float) * (size_t)maxT * H);
   L.sout = o;   o = ws_align(o + sizeof(uint16_t) * (size_t)maxT * H);
+  L.nwp = (int)((pairs + 31) / 32);
+  L.max_tiles = prefill_max_tiles((int)pairs, E);
+  L.bits = L.wpre = L.counts = L.offsets = L.tiles = L.ntiles = L.sorted = L.slot = o;
+  if (maxT >= kPrefillMinT) {
+    L.bits = o;    o = ws_align(o + sizeof(uint32_t) * (size_t)E * L.nwp);
+    L.wpre = o;    o = ws_align(o + sizeof(uint32_t) * (size_t)E * L.nwp);
+    L.counts = o;  o = ws_align(o + sizeof(int32_t) * (size_t)E);
+    L.offsets = o; o = ws_align(o + sizeof(int32_t) * ((size_t)E + 1));
+    L.tiles = o;   o = ws_align(o + 16 * (size_t)L.max_tiles);
+    L.ntiles = o;  o = ws_align(o + sizeof(int32_t));
+    L.sorted = o;  o = ws_align(o + sizeof(int32_t) * pairs);
+    L.slot = o;    o = ws_align(o + sizeof(float) * pairs * H);
+  }
   L.total = o;
   return L;
 }
 
 // Ticket slots (self-resetting counters for the last-block pattern).
-enum { TICKET_ROUTE = 0, TICKET_COMBINE = 1 };
+enum { TICKET_ROUTE = 0, TICKET_COMBINE = 1, TICKET_SCAN = 2 };
 
 // Device-side view of one call: weights, geometry and workspace pointers.
 struct BlockArgs {
@@ -189,6 +212,16 @@ struct BlockArgs {
   uint16_t* sinter;
   float* routed;
   uint16_t* sout;
+  // prefill sections (null below kPrefillMinT tokens)
+  uint32_t* bits;
+  uint32_t* wpre;
+  int32_t* counts;
+  int32_t* offsets;
+  void* tiles;
+  int32_t* ntiles;
+  int32_t* sorted;
+  float* slot;
+  int nwp, max_tiles;
 };
 
 }  // namespace moe

@@ -1,0 +1,22 @@
+// moe_prefill.h -- launch sequences of the prefill path (T >= kPrefillMinT tokens), moe_prefill.cu.
+#pragma once
+#include "moe_common.cuh"
+
+namespace moe {
+
+// Geometry the prefill path serves (the tile GEMMs need E % 16 == 0 for their row-padded router tile; every other
+// constraint follows from the shapes the library accepts). Other geometries run the decode kernels chunk by chunk.
+bool prefill_supported(const moe_layer_weights& w);
+
+// Whole block (qwen.cu:429-448 at T >= 8): residual RMSNorm, router GEMM + top-k, stable expert sort, grouped INT4
+// GEMMs, shared-expert GEMMs, slot-order combine (+ the next layer's RMSNorm when a.next_rms1 is set).
+cudaError_t prefill_block(const BlockArgs& a, cudaStream_t s);
+// Router GEMM + top-k from a.normed into a.logits / a.idx / a.wts.
+cudaError_t prefill_router(const BlockArgs& a, cudaStream_t s);
+// moe() for caller routing a.idx / a.wts: sort, grouped GEMMs, slot-order sum into a.routed; inter_out
+// (nullable) receives the bf16 [T, TOPK, I] intermediate in pair order.
+cudaError_t prefill_routed(const BlockArgs& a, uint16_t* inter_out, cudaStream_t s);
+// Shared expert from a.normed into a.sout.
+cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s);
+
+}  // namespace moe

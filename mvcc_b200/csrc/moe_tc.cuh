@@ -1,0 +1,128 @@
+// moe_tc.cuh -- sm_100a tensor-core building blocks for the prefill GEMMs: tcgen05.mma issue, TMEM allocation and
+// loads, UMMA shared-memory and instruction descriptors, mbarriers with bounded waits.
+//
+// Descriptor formats (PTX ISA, tcgen05 matrix descriptors; the same fields CUTLASS names in
+// cute/arch/mma_sm100_desc.hpp):
+//   shared-memory descriptor (64 bit): start address >> 4 in bits [0,14), leading byte offset >> 4 in [16,30),
+//     stride byte offset >> 4 in [32,46), version 1 in [46,48), layout type in [61,64) (2 = 128-byte swizzle).
+//   instruction descriptor (32 bit, kind::f16): D format in [4,6) (1 = f32), A format in [7,10) and B format in
+//     [10,13) (1 = bf16), A/B major in bits 15/16 (0 = K-major), N >> 3 in [17,23), M >> 4 in [24,29).
+// Operand tiles are K-major with the 128-byte swizzle: a row holds 64 bf16 (128 bytes, eight 16-byte chunks),
+// eight rows form a 1024-byte atom, chunk j of row r sits at chunk position j ^ (r % 8); atoms follow each other
+// at 1024 bytes (the stride byte offset). Each MMA consumes K = 16 (32 bytes), selected by advancing the start
+// address within the 128-byte row.
+#pragma once
+#include <stdint.h>
+
+#include "moe_common.cuh"
+
+namespace moe {
+namespace tc {
+
+// Byte offset of element (row r, k) in a swizzled K-major tile of 64-wide rows (k in [0, 64)).
+__device__ __forceinline__ uint32_t sw128_offset(int r, int k) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((k >> 3) ^ (r & 7))) << 4) + (k & 7) * 2);
+}
+// Byte offset of 16-byte chunk j (k = 8j .. 8j+7) of row r.
+__device__ __forceinline__ uint32_t sw128_chunk(int r, int j) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// K-major, 128-byte swizzle, 1024-byte atoms; smem_addr must be 1024-byte aligned (plus the K-step offset).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major): 16 bytes
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: 1024 bytes between 8-row atoms
+  d |= (uint64_t)1 << 46;             // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;             // 128-byte swizzle
+  return d;
+}
+
+// bf16 x bf16 -> f32, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier when every tcgen05.mma this thread issued before has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(mbar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Generic-proxy writes to shared memory become visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Warp-wide TMEM allocation; the address is written to *slot (shared memory).
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane (warp w reads lanes 32 (w % 4) .. + 31).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(mbar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+// Waits for phase `parity` of the mbarrier to complete; gives up after `limit` polls and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, long long limit) {
+  const uint32_t a = smem_u32(mbar);
+  for (long long i = 0; i < limit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t"
+        ".reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void cp_async16_zfill(void* smem_dst, const void* gmem_src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+}  // namespace tc
+}  // namespace moe

@@ -17,3 +17,12 @@ def pytest_configure(config):
 def orc():
     from oracle import oracle as O
     return O.Oracle()
+
+
+@pytest.fixture
+def decode_only():
+    """Keeps every call of the test on the decode kernels (prefill threshold above any T), then restores it."""
+    import mvcc_b200 as m
+    m.set_prefill_min_tokens(1 << 30)
+    yield
+    m.set_prefill_min_tokens(0)

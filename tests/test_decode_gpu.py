@@ -8,7 +8,7 @@ import torch
 
 from oracle import oracle as O
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("decode_only")]
 
 SHAPES = {
     "h1024_g128": O.Shape(H=1024, E=32, TOPK=8, I=512, Is=512, G=128),

@@ -10,7 +10,7 @@ import torch
 
 from oracle import oracle as O
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("decode_only")]
 
 
 @pytest.mark.parametrize("T", [1, 16, 21])
