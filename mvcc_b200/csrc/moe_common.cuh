@@ -143,8 +143,10 @@ struct WsLayout {
 // The reference switches moe() to its sort + tile path at T >= 8 (qwen.cu:347); so does this library.
 constexpr int kPrefillMinT = 8;
 
-// Upper bound of the grouped-GEMM tiles (128 pairs each) for P pairs over E experts: sum_e ceil(n_e / 128).
-__host__ __device__ inline int prefill_max_tiles(int P, int E) { return P / 128 + (E < P ? E : P) + 1; }
+// Rows (sorted pairs of one expert) per grouped-GEMM tile, and the upper bound of the tiles for P pairs over E
+// experts: sum_e ceil(n_e / kTileRows).
+constexpr int kTileRows = 256;
+__host__ __device__ inline int prefill_max_tiles(int P, int E) { return P / kTileRows + (E < P ? E : P) + 1; }
 
 __host__ __device__ inline size_t ws_align(size_t x) { return (x + 255) & ~(size_t)255; }
 

@@ -1,28 +1,35 @@
-// moe_gemm.cu -- warp-specialized tcgen05 tile GEMM for the prefill path: the dense router / shared-expert
-// GEMMs (dense(), qwen.cu:298-319) and the grouped INT4 expert GEMMs (moe_gate_up_tile_kernel,
+// moe_gemm.cu -- persistent, warp-specialized tcgen05 tile GEMM for the prefill path: the dense router and
+// shared-expert GEMMs (dense(), qwen.cu:298-319) and the grouped INT4 expert GEMMs (moe_gate_up_tile_kernel,
 // moe_down_tile_kernel, kernels.cuh:942-1057).
 //
-// One CTA computes a 128 x BN tile of D = A . B^T with K-steps of 64 through a ring of shared-memory stages:
-//   warp 0      A producer: gathers the tile's 128 A rows (one per token or (token, slot) pair) with cp.async
-//               into the 128-byte-swizzled K-major layout, arrives on fullA[s] when its copies land;
-//   warp 1      B producer: bf16 B rows straight into the swizzled layout, or INT4 rows (32 bytes per row and
-//               step) into a raw staging buffer; arrives on fullB[s];
-//   warp 3      INT4 only: copies the tile's fp16 group scales (all of K) once;
-//   warps 4-7   INT4 only: dequantize raw[s] into bf16 B[s] exactly as dequant32_bf16 does
-//               (kernels.cuh:925-940: bf16((q - 8) * scale), one rounding), fence the writes to the async proxy
-//               and arrive on deq[s]; after the main loop the same warps run the epilogue from TMEM;
-//   warp 2      allocates the TMEM accumulator (BN fp32 columns x 128 lanes); one lane issues the four
-//               tcgen05.mma (M=128, N=BN, K=16) of each stage and commits them to empty[s] (which frees the
-//               stage for the producers) and, after the last stage, to acc_full.
-// Every mbarrier wait is bounded: after kWaitNs the waiting thread records MOE_ERR_TIMEOUT in the error word,
-// raises the CTA's abort flag (other waits poll it) and leaves its loop; the CTA then drains its copies, frees
-// TMEM and exits.
+// One CTA per SM walks work items (tile of up to 256 A rows) x (n-tile of BN B rows), K in steps of 64, through
+// three shared-memory rings; 16 warps:
+//   warps 0-1   A producers: contiguous A rows come in as one 2D TMA tile (box 64 x 128, 128-byte swizzle) per
+//               128-row sub-tile and step; gathered rows (one per (token, slot) pair of the sorted pair list) come
+//               in by cp.async, eight lanes per row so that each row is one 128-byte line request, into the same
+//               swizzled K-major layout (cp.async.mbarrier.arrive.noinc on fullA[s]);
+//   warp 2      B producer, one lane: TMA tiles of bf16 B rows straight into the B ring (fullB), or of INT4 rows
+//               (box 32 bytes x BN rows) into the raw ring (fullR) plus, once per item, the item's fp16 group
+//               scales; completion by transaction count (mbarrier expect_tx). No load uses cluster multicast;
+//   warp 3      allocates TMEM (two accumulator buffers of (rows / 128) x BN fp32 columns) and, from one lane,
+//               issues the tcgen05.mma of each step (M=128 per 128-row sub-tile, N=BN, K=16 x 4), committing to
+//               emptyA / emptyB (stage free) and, after an item's last step, to acc_full[buffer];
+//   warps 4-7   epilogue: wait acc_full, tcgen05.ld the accumulator rows of their TMEM lane quarter, apply the
+//               epilogue, store, release the buffer (acc_empty) -- overlapping the next item's main loop;
+//   warps 8-15  INT4 only: dequantize raw[r] into bf16 B[s] as dequant32_bf16 does (kernels.cuh:925-940:
+//               bf16((q - 8) * scale), one rounding), fence the writes to the async proxy, arrive on fullB.
+// Every wait is bounded: kWaitNs after its first miss a waiting thread records MOE_ERR_TIMEOUT in the error word,
+// raises the CTA's abort flag (other waits poll it) and leaves its loop; the CTA then drains its copies, frees TMEM
+// and exits.
 //
 // Exact dequantization without a conversion instruction per nibble: a nibble q at bit position 4p of a word,
 // OR-ed into 0x4B000000, is the float 2^23 + q * 2^(4p); subtracting 2^23 + 8 * 2^(4p) leaves (q - 8) * 2^(4p)
 // exactly, and multiplying by scale * 2^(-4p) gives (q - 8) * scale exactly (at most 15 significant bits); one
 // cvt.rn.bf16x2.f32 rounds two such values to bf16, the reference's single rounding.
+#include <cuda.h>
+
 #include <algorithm>
+#include <cstring>
 
 #include "moe_common.cuh"
 #include "moe_gemm.h"
@@ -32,26 +39,37 @@ namespace moe {
 
 using namespace tc;
 
-constexpr int kBM = 128, kBK = 64, kGThreads = 256;
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far beyond any tile's main loop
+constexpr int kBK = 64;
+constexpr int kGWarps = 16, kGThreads = kGWarps * 32;
+constexpr int kDeqWarp0 = 8, kDeqThreads = 256;
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far beyond any item's main loop
 
-struct GemmSmem {
+struct GemmCfg {
+  int bn, mt, sa, sb, sr, ksc, sstride;  // BN, 128-row sub-tiles per tile, ring depths, scales per row, row stride
+  int rk;                                // k-steps per raw INT4 stage (a row's 32 * rk contiguous bytes per load)
+  int a_tma, s_tma;                      // A by TMA tiles (contiguous rows), scales by TMA (rows >= 16 bytes)
   size_t a, b, raw, sc, bar, total;
 };
 
 __host__ __device__ inline size_t g_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-__host__ __device__ inline GemmSmem gemm_smem(int bn, bool int4, int stages, int K, int G) {
-  GemmSmem L;
+__host__ __device__ inline GemmCfg gemm_cfg(int bn, int mt, bool int4, int sa, int sb, int sr, int K, int G) {
+  GemmCfg c;
+  c.bn = bn; c.mt = mt; c.sa = sa; c.sb = sb; c.sr = int4 ? sr : 0;
+  const int nk = K / kBK;
+  c.rk = nk % 4 == 0 ? 4 : (nk % 2 == 0 ? 2 : 1);
+  c.ksc = int4 ? K / G : 0;
+  c.sstride = c.ksc * 2;
+  c.a_tma = 0;
+  c.s_tma = int4 && c.sstride >= 16;
   size_t o = 0;
-  L.a = o;   o += (size_t)stages * kBM * 128;  // 16 KiB per stage; every stage 1024-byte aligned
-  L.b = o;   o += (size_t)stages * bn * 128;
-  L.raw = o; if (int4) o += (size_t)stages * bn * 32;
-  L.sc = o;  if (int4) o = g_align(o + (size_t)bn * (K / G) * 2, 16);
-  L.bar = g_align(o, 8);
-  o = L.bar + 8 * (4 * (size_t)stages + 4);
-  L.total = o + 1024;  // the dynamic base is aligned up to 1024 bytes at run time
-  return L;
+  c.a = o;   o += (size_t)sa * mt * 128 * 128;  // 16 KiB per 128-row sub-tile and stage (1024-byte aligned)
+  c.b = o;   o += (size_t)sb * bn * 128;
+  c.raw = o; o += (size_t)c.sr * bn * 32 * c.rk;
+  c.sc = o;  o = g_align(o + (int4 ? 2 * (size_t)bn * c.sstride : 0), 128);
+  c.bar = o; o += 8 * (size_t)(2 * sa + 2 * sb + 2 * c.sr + 8) + 16;
+  c.total = o + 1024;  // the dynamic base is aligned up to 1024 bytes at run time
+  return c;
 }
 
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* mbar) {
@@ -63,6 +81,30 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
       ".reg .b64 st;\n\t"
       "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t"
       "}" ::"r"(smem_u32(mbar))
+      : "memory");
+}
+__device__ __forceinline__ void cp_async_n(void* dst, const void* src, int bytes) {
+  const uint32_t d = smem_u32(dst);
+  if (bytes == 16) asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+  else if (bytes == 8) asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(src) : "memory");
+  else asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+
+// 2D TMA tile load into this CTA's shared memory, completion counted in bytes on mbar (no multicast).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(mbar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t"
+      ".reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t"
+      "}" ::"r"(smem_u32(mbar)),
+      "r"(bytes)
       : "memory");
 }
 
@@ -159,333 +201,481 @@ __device__ __forceinline__ int64_t b_row(const GemmParams& p, int e, int nt, int
   return (int64_t)e * p.b_rows_per_e + row;
 }
 
-template <int BN, bool INT4, int EPI>
-__global__ void __launch_bounds__(kGThreads, 1) moe_gemm_kernel(const GemmParams p, int stages) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const int S = stages;
-  const GemmSmem L = gemm_smem(BN, INT4, S, p.K, p.G);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nN = p.N / BN;
-  const int tix = blockIdx.x / nN, nt = blockIdx.x - tix * nN;
+__device__ __forceinline__ GemmTile load_tile(const GemmParams& p, int ti, int tile_rows) {
   GemmTile t;
   if (p.tiles) {
-    if (tix >= *p.ntiles) return;
-    t = p.tiles[tix];
+    t = p.tiles[ti];
   } else {
     t.e = 0;
-    t.m0 = tix * kBM;
+    t.m0 = ti * tile_rows;
     t.mcount = p.M - t.m0;
   }
   t.e = min(max(t.e, 0), p.E - 1);
-  t.mcount = min(t.mcount, kBM);
-  if (t.mcount <= 0 || t.m0 < 0) return;
+  t.mcount = max(0, min(t.mcount, tile_rows));
+  if (t.m0 < 0) t.mcount = 0;
+  return t;
+}
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
+template <int BN, bool INT4, int EPI>
+__global__ void __launch_bounds__(kGThreads, 1)
+    moe_gemm_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ CUtensorMap tmA,
+                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS, const GemmCfg c) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int MT = c.mt, tile_rows = 128 * MT, SA = c.sa, SB = c.sb, SR = c.sr;
+  const int nN = p.N / BN, nk = p.K / kBK;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + c.bar);
   uint64_t* fullA = bars;
-  uint64_t* fullB = bars + S;
-  uint64_t* deq = bars + 2 * S;
-  uint64_t* empty = bars + 3 * S;
-  uint64_t* sc_full = bars + 4 * S;
-  uint64_t* acc_full = bars + 4 * S + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 4 * S + 3);
-  constexpr uint32_t kCols = BN < 32 ? 32 : BN;
+  uint64_t* emptyA = fullA + SA;
+  uint64_t* fullB = emptyA + SA;
+  uint64_t* emptyB = fullB + SB;
+  uint64_t* fullR = emptyB + SB;
+  uint64_t* freeR = fullR + SR;
+  uint64_t* sc_full = freeR + SR;      // [2]
+  uint64_t* sc_free = sc_full + 2;     // [2]
+  uint64_t* acc_full = sc_free + 2;    // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t cols = 2u * MT * BN;  // 128, 256 or 512
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&fullA[s], 32);
-      mbar_init(&fullB[s], 32);
-      mbar_init(&deq[s], 128);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(&fullA[s], c.a_tma ? 1 : 64);
+      mbar_init(&emptyA[s], 1);
     }
-    mbar_init(sc_full, 32);
-    mbar_init(acc_full, 1);
+    for (int s = 0; s < SB; ++s) {
+      mbar_init(&fullB[s], INT4 ? kDeqThreads / 32 : 1);
+      mbar_init(&emptyB[s], 1);
+    }
+    for (int s = 0; s < SR; ++s) {
+      mbar_init(&fullR[s], 1);
+      mbar_init(&freeR[s], kDeqThreads / 32);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sc_full[i], c.s_tma ? 1 : 32);
+      mbar_init(&sc_free[i], kDeqThreads / 32);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
-  if (warp == 2) tmem_alloc(tmem_slot, kCols);
+  // everything above touches only this CTA's shared memory: it overlaps the previous kernel under PDL
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int ntiles = p.tiles ? min(*p.ntiles, 1 << 20) : (p.M + tile_rows - 1) / tile_rows;
+  const int n_items = ntiles * nN;
+  if ((int)blockIdx.x >= n_items) return;  // uniform for the CTA, before any TMEM is held
+  if (warp == 3) tmem_alloc(tmem_slot, cols);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  const int nk = p.K / kBK;
-  const int ksc = p.K / p.G;  // scales per B row
 
-  if (warp == 0) {
-    // ---- A producer: 4 rows per lane, 8 chunks each per stage
-    const uint16_t* arow[4];
-    bool aval[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = lane + 32 * i;
-      aval[i] = r < t.mcount;
-      int src = 0;
-      if (aval[i]) {
-        src = p.a_rows ? __ldg(p.a_rows + min(t.m0 + r, p.list_len - 1)) / p.a_div : t.m0 + r;
-        src = min(max(src, 0), p.a_nrows - 1);
-      }
-      arow[i] = p.A + (int64_t)src * p.lda;
-    }
-    for (int kt = 0; kt < nk; ++kt) {
-      const int s = kt % S;
-      if (kt >= S && !wait_bar(&empty[s], ((kt / S) - 1) & 1, abort_flag, p.err)) break;
-      uint8_t* dst = smem + L.a + (size_t)s * kBM * 128;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = lane + 32 * i;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          cp_async16_zfill(dst + sw128_chunk(r, j), arow[i] + kt * kBK + j * 8, aval[i]);
-      }
-      cp_async_arrive_noinc(&fullA[s]);
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp == 1) {
-    // ---- B producer
-    constexpr int RPL = BN / 32;  // rows per lane
-    int64_t brow[RPL];
-#pragma unroll
-    for (int i = 0; i < RPL; ++i) brow[i] = b_row<BN>(p, t.e, nt, lane + 32 * i);
-    for (int kt = 0; kt < nk; ++kt) {
-      const int s = kt % S;
-      if (kt >= S && !wait_bar(&empty[s], ((kt / S) - 1) & 1, abort_flag, p.err)) break;
-      if constexpr (INT4) {
-        uint8_t* dst = smem + L.raw + (size_t)s * BN * 32;
-#pragma unroll
-        for (int i = 0; i < RPL; ++i) {
-          const int r = lane + 32 * i;
-          const bool ok = p.paired || nt * BN + r < p.n_valid;
-          const uint8_t* src = ok ? p.Bq + brow[i] * (p.K / 2) + kt * 32 : p.Bq;
-          cp_async16_zfill(dst + r * 32, src, ok);
-          cp_async16_zfill(dst + r * 32 + 16, src + (ok ? 16 : 0), ok);
-        }
-      } else {
-        uint8_t* dst = smem + L.b + (size_t)s * BN * 128;
-#pragma unroll
-        for (int i = 0; i < RPL; ++i) {
-          const int r = lane + 32 * i;
-          const bool ok = p.paired || nt * BN + r < p.n_valid;
-          const uint16_t* src = ok ? p.Bh + brow[i] * p.K + kt * kBK : p.Bh;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) cp_async16_zfill(dst + sw128_chunk(r, j), src + (ok ? j * 8 : 0), ok);
+  if (warp <= 1) {
+    // ---- A producers
+    if (c.a_tma) {
+      if (warp == 0 && lane == 0) {
+        int g = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+          const GemmTile t = load_tile(p, it / nN, tile_rows);
+          const int msub = t.mcount > 128 ? 2 : 1;
+                    for (int kt = 0; kt < nk; ++kt, ++g) {
+            const int s = g % SA, kx = kt;
+            if (g >= SA && !wait_bar(&emptyA[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+            uint8_t* dst = smem + c.a + (size_t)s * MT * 16384;
+            mbar_expect_tx(&fullA[s], (uint32_t)msub * 16384u);
+            for (int m = 0; m < msub; ++m) tma_load_2d(dst + m * 16384, &tmA, kx * kBK, t.m0 + m * 128, &fullA[s]);
+          }
         }
       }
-      cp_async_arrive_noinc(&fullB[s]);
+    } else {
+      // gathered rows: lane l of the 64 fetches 16-byte chunk l % 8 of rows l / 8 + 8 i (i < 16 MT), so that each
+      // warp instruction covers four whole 128-byte rows
+      const int t64 = threadIdx.x, ch = t64 & 7, r0 = t64 >> 3;
+      int g = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const GemmTile t = load_tile(p, it / nN, tile_rows);
+        int soff[32];  // element offset of the source row of rows r0 + 8 i, or -1
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int r = r0 + 8 * i;
+          soff[i] = -1;
+          if (i < 16 * MT && r < t.mcount) {
+            int src = p.a_rows ? __ldg(p.a_rows + min(t.m0 + r, p.list_len - 1)) / p.a_div : t.m0 + r;
+            src = min(max(src, 0), p.a_nrows - 1);
+            soff[i] = (int)((int64_t)src * p.lda) + ch * 8;
+          }
+        }
+                for (int kt = 0; kt < nk; ++kt, ++g) {
+          const int s = g % SA, kx = kt;
+          if (g >= SA && !wait_bar(&emptyA[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+          uint8_t* dst = smem + c.a + (size_t)s * MT * 16384;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            // rows past the tile are never loaded nor stored: their stale values are harmless
+            if (soff[i] < 0) continue;
+            const int r = r0 + 8 * i;
+            cp_async_n(dst + (r >> 7) * 16384 + sw128_chunk(r & 127, ch), p.A + soff[i] + kx * kBK, 16);
+          }
+          cp_async_arrive_noinc(&fullA[s]);
+        }
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == 2) {
+    // ---- B producer: lane 0 issues the TMA tiles; all lanes copy scales when their rows are under 16 bytes
+    constexpr int HB = BN / 2;
+    int g = 0, j = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
+      const GemmTile t = load_tile(p, it / nN, tile_rows);
+      const int nt = it % nN;
+      // first B row of the item (and of its up half when paired)
+      const int y0 = (int)((int64_t)t.e * p.b_rows_per_e + (p.paired ? nt * HB : nt * BN));
+      const int y1 = (int)((int64_t)t.e * p.b_rows_per_e + p.pair_off + nt * HB);
+      if constexpr (INT4) {
+        const int sb = j & 1;
+        int freed = 1;  // one lane waits, the warp follows its verdict (no divergent exits before the shuffles)
+        if (lane == 0 && j >= 2) freed = wait_bar(&sc_free[sb], ((j >> 1) - 1) & 1, abort_flag, p.err) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, freed, 0)) break;
+        uint8_t* sdst = smem + c.sc + (size_t)sb * BN * c.sstride;
+        if (c.s_tma) {
+          if (lane == 0) {
+            mbar_expect_tx(&sc_full[sb], (uint32_t)(BN * c.sstride));
+            tma_load_2d(sdst, &tmS, 0, y0, &sc_full[sb]);
+            if (p.paired) tma_load_2d(sdst + HB * c.sstride, &tmS, 0, y1, &sc_full[sb]);
+          }
+        } else {
+          const int rb = c.sstride;  // 2, 4 or 8 bytes per row
+          for (int r = lane; r < BN; r += 32) {
+            if (!p.paired && nt * BN + r >= p.n_valid) continue;
+            const int64_t row = p.paired ? (r < HB ? y0 + r : y1 + r - HB) : (int64_t)y0 + r;
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(p.Bs) + row * rb;
+            if (rb >= 4) cp_async_n(sdst + r * rb, src, rb);
+            else *reinterpret_cast<uint16_t*>(sdst + r * rb) = __ldg(reinterpret_cast<const uint16_t*>(src));
+          }
+          if (rb >= 4) cp_async_arrive_noinc(&sc_full[sb]);
+          else mbar_arrive(&sc_full[sb]);
+        }
+        if (lane == 0) {
+          // one raw stage = rk k-steps: 32 * rk contiguous bytes of each of the BN rows
+          const int RB = 32 * c.rk;
+          for (int kt = 0; kt < nk; kt += c.rk, g += c.rk) {
+            const int gr = g / c.rk, s = gr % SR, kx = kt;
+            if (gr >= SR && !wait_bar(&freeR[s], ((gr / SR) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+            uint8_t* dst = smem + c.raw + (size_t)s * BN * RB;
+            mbar_expect_tx(&fullR[s], (uint32_t)(BN * RB));
+            tma_load_2d(dst, &tmB, kx * 32, y0, &fullR[s]);
+            if (p.paired) tma_load_2d(dst + HB * RB, &tmB, kx * 32, y1, &fullR[s]);
+          }
+        }
+        g = __shfl_sync(0xffffffffu, g, 0);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      } else {
+        if (lane == 0) {
+                    for (int kt = 0; kt < nk; ++kt, ++g) {
+            const int s = g % SB, kx = kt;
+            if (g >= SB && !wait_bar(&emptyB[s], ((g / SB) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+            uint8_t* dst = smem + c.b + (size_t)s * BN * 128;
+            mbar_expect_tx(&fullB[s], (uint32_t)(BN * 128));
+            tma_load_2d(dst, &tmB, kx * kBK, y0, &fullB[s]);
+            if (p.paired) tma_load_2d(dst + HB * 128, &tmB, kx * kBK, y1, &fullB[s]);
+          }
+        }
+        g = __shfl_sync(0xffffffffu, g, 0);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == 3) {
     // ---- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
+      constexpr uint32_t idesc = idesc_bf16_f32(128, BN);
+      int g = 0, j = 0;
       bool ok = true;
-      for (int kt = 0; kt < nk && ok; ++kt) {
-        const int s = kt % S;
-        const uint32_t par = (kt / S) & 1;
-        ok = wait_bar(&fullA[s], par, abort_flag, p.err) &&
-             wait_bar(INT4 ? &deq[s] : &fullB[s], par, abort_flag, p.err);
-        if (!ok) break;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
+        const GemmTile t = load_tile(p, it / nN, tile_rows);
+        const int ab = j & 1;
+        if (j >= 2 && !wait_bar(&acc_empty[ab], ((j >> 1) - 1) & 1, abort_flag, p.err)) break;
         fence_after_sync();
-        const uint32_t a_addr = smem_u32(smem + L.a + (size_t)s * kBM * 128);
-        const uint32_t b_addr = smem_u32(smem + L.b + (size_t)s * BN * 128);
+        const int msub = t.mcount > 128 ? 2 : 1;
+        for (int kt = 0; kt < nk; ++kt, ++g) {
+          const int sa = g % SA, sb = g % SB;
+          ok = wait_bar(&fullA[sa], (g / SA) & 1, abort_flag, p.err) &&
+               wait_bar(&fullB[sb], (g / SB) & 1, abort_flag, p.err);
+          if (!ok) break;
+          fence_after_sync();
+          const uint32_t b_addr = smem_u32(smem + c.b + (size_t)sb * BN * 128);
+          for (int m = 0; m < msub; ++m) {
+            const uint32_t a_addr = smem_u32(smem + c.a + ((size_t)sa * MT + m) * 16384);
+            const uint32_t d = tmem + (uint32_t)((ab * MT + m) * BN);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)
-          mma_bf16(tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc, (kt | kk) != 0);
-        mma_commit(&empty[s]);
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              mma_bf16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc, (kt | kk) != 0);
+          }
+          mma_commit(&emptyA[sa]);
+          mma_commit(&emptyB[sb]);
+        }
+        if (ok) mma_commit(&acc_full[ab]);
       }
-      if (ok) mma_commit(acc_full);
     }
     __syncwarp();
-  } else if (warp == 3) {
-    // ---- scale loader (INT4): all K/G scales of the tile's BN rows
-    if constexpr (INT4) {
-      uint16_t* sc = reinterpret_cast<uint16_t*>(smem + L.sc);
-      for (int r = lane; r < BN; r += 32) {
-        if (!p.paired && nt * BN + r >= p.n_valid) continue;  // zero rows: any scale gives 0
-        const uint16_t* src = p.Bs + b_row<BN>(p, t.e, nt, r) * ksc;
-        if ((ksc & 7) == 0) {
-          for (int g = 0; g < ksc; g += 8)
-            *reinterpret_cast<uint4*>(sc + r * ksc + g) = __ldg(reinterpret_cast<const uint4*>(src + g));
+  } else if (warp < kDeqWarp0) {
+    // ---- epilogue: warp (w % 4) reads TMEM lanes 32 (w % 4) .. + 31 of each 128-row sub-tile
+    const int q = warp & 3;
+    int j = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++j) {
+      const GemmTile t = load_tile(p, it / nN, tile_rows);
+      const int nt = it % nN, ab = j & 1;
+      if (!wait_bar(&acc_full[ab], (j >> 1) & 1, abort_flag, p.err)) break;
+      fence_after_sync();
+      const int msub = t.mcount > 128 ? 2 : 1;
+      for (int m = 0; m < msub; ++m) {
+        const int r = m * 128 + q * 32 + lane;
+        const bool valid = r < t.mcount;
+        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((ab * MT + m) * BN);
+        int64_t orow = t.m0 + r;
+        float rs = 1.f;
+        if constexpr (EPI == EPI_SLOT) {
+          orow = valid ? (int64_t)__ldg(p.out_rows + min(t.m0 + r, p.list_len - 1)) : 0;
+          orow = min(max(orow, (int64_t)0), (int64_t)p.out_nrows - 1);
+          rs = valid ? __ldg(p.row_scale + orow) : 0.f;
         } else {
-          for (int g = 0; g < ksc; ++g) sc[r * ksc + g] = __ldg(src + g);
+          orow = min(orow, (int64_t)p.out_nrows - 1);
+        }
+        if constexpr (EPI == EPI_SILU_TILE || EPI == EPI_SILU_ROUND) {
+          uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * (BN / 2);
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+            float gv[16], uv[16];
+            tmem_ld16(tb + c0, gv);
+            tmem_ld16(tb + BN / 2 + c0, uv);
+            if (valid) {
+              uint32_t o[8];
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                float a0, a1;
+                if constexpr (EPI == EPI_SILU_TILE) {
+                  a0 = silu(gv[2 * jj]) * uv[2 * jj];
+                  a1 = silu(gv[2 * jj + 1]) * uv[2 * jj + 1];
+                } else {
+                  a0 = silu(bf2f(f2bf(gv[2 * jj]))) * bf2f(f2bf(uv[2 * jj]));
+                  a1 = silu(bf2f(f2bf(gv[2 * jj + 1]))) * bf2f(f2bf(uv[2 * jj + 1]));
+                }
+                o[jj] = (uint32_t)f2bf(a0) | ((uint32_t)f2bf(a1) << 16);
+              }
+              reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+              reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+          }
+        } else if constexpr (EPI == EPI_BF16) {
+          uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * BN;
+          const int ncol = min(BN, p.n_valid - nt * BN);
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            tmem_ld16(tb + c0, v);
+            if (valid && c0 + 16 <= ncol) {
+              uint32_t o[8];
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) o[jj] = (uint32_t)f2bf(v[2 * jj]) | ((uint32_t)f2bf(v[2 * jj + 1]) << 16);
+              reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+              reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            } else if (valid) {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                if (c0 + jj < ncol) out[c0 + jj] = f2bf(v[jj]);
+            }
+          }
+        } else {  // EPI_F32, EPI_SLOT
+          float* out = static_cast<float*>(p.out) + orow * p.ldo + nt * BN;
+          const int ncol = min(BN, p.n_valid - nt * BN);
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            tmem_ld16(tb + c0, v);
+            if (valid && c0 + 16 <= ncol) {
+#pragma unroll
+              for (int jj = 0; jj < 16; jj += 4)
+                *reinterpret_cast<float4*>(out + c0 + jj) =
+                    make_float4(v[jj] * rs, v[jj + 1] * rs, v[jj + 2] * rs, v[jj + 3] * rs);
+            } else if (valid) {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                if (c0 + jj < ncol) out[c0 + jj] = v[jj] * rs;
+            }
+          }
         }
       }
-      mbar_arrive(sc_full);
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
-  }
-
-  if (warp >= 4) {
-    const int td = threadIdx.x - 128;
-    if constexpr (INT4) {
-      // ---- dequantization
-      const Nib8Magic M = nib8_magic();
-      const uint16_t* sc = reinterpret_cast<const uint16_t*>(smem + L.sc);
-      bool ok = wait_bar(sc_full, 0, abort_flag, p.err);
-      for (int kt = 0; kt < nk && ok; ++kt) {
-        const int s = kt % S;
-        if (!wait_bar(&fullB[s], (kt / S) & 1, abort_flag, p.err)) break;
-        const uint8_t* raw = smem + L.raw + (size_t)s * BN * 32;
-        uint8_t* bdst = smem + L.b + (size_t)s * BN * 128;
-#pragma unroll
-        for (int jb = 0; jb < (BN * 2) / 128; ++jb) {
-          const int job = td + 128 * jb;
-          const int r = job >> 1, h = job & 1;
-          const uint4 w = *reinterpret_cast<const uint4*>(raw + r * 32 + h * 16);
-          const float sv = h2f(sc[r * ksc + (kt * kBK + h * 32) / p.G]);
+  } else if constexpr (INT4) {
+    // ---- dequantization: thread td takes B row td / 2, K half td % 2 (32 nibbles) of every step
+    const int td = threadIdx.x - kDeqWarp0 * 32;
+    const bool active = td < BN * 2;
+    const int r = td >> 1, h = td & 1;
+    const Nib8Magic M = nib8_magic();
+    int g = 0, j = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
+      const int sbuf = j & 1;
+      if (!wait_bar(&sc_full[sbuf], (j >> 1) & 1, abort_flag, p.err)) break;
+      const uint8_t* scrow = smem + c.sc + (size_t)sbuf * BN * c.sstride + r * c.sstride;
+      const int RB = 32 * c.rk;
+      for (int kt = 0; kt < nk; ++kt, ++g) {
+        const int gr = g / c.rk, sr = gr % SR, sb = g % SB, sub = g % c.rk, kx = kt;
+        ok = wait_bar(&fullR[sr], (gr / SR) & 1, abort_flag, p.err) &&
+             (g < SB || wait_bar(&emptyB[sb], ((g / SB) - 1) & 1, abort_flag, p.err));
+        if (!ok) break;
+        if (active) {
+          const uint4 w =
+              *reinterpret_cast<const uint4*>(smem + c.raw + (size_t)sr * BN * RB + r * RB + sub * 32 + h * 16);
+          const float sv = h2f(*reinterpret_cast<const uint16_t*>(scrow + 2 * ((kx * kBK + h * 32) / p.G)));
           const u64 s01 = pack2f(sv, sv * 0.0625f), s23 = pack2f(sv * (1.f / 256.f), sv * (1.f / 4096.f));
           const u64 s45 = pack2f(sv * (1.f / 65536.f), sv * (1.f / 256.f));
           const u64 s67 = pack2f(sv * (1.f / 4096.f), sv * (1.f / 65536.f));
+          uint8_t* bdst = smem + c.b + (size_t)sb * BN * 128;
           const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(bdst + sw128_chunk(r, h * 4 + q)) = dequant8_bf16(ww[q], s01, s23, s45, s67, M);
+          for (int qq = 0; qq < 4; ++qq)
+            *reinterpret_cast<uint4*>(bdst + sw128_chunk(r, h * 4 + qq)) = dequant8_bf16(ww[qq], s01, s23, s45, s67, M);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&deq[s]);
-      }
-    }
-    // ---- epilogue: warp (w % 4) reads TMEM lanes 32 (w % 4) .. + 31 = tile rows
-    if (wait_bar(acc_full, 0, abort_flag, p.err)) {
-      fence_after_sync();
-      const int q = warp & 3, r = q * 32 + lane;
-      const bool valid = r < t.mcount;
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
-      int64_t orow = t.m0 + r;
-      float rs = 1.f;
-      if constexpr (EPI == EPI_SLOT) {
-        orow = valid ? (int64_t)__ldg(p.out_rows + min(t.m0 + r, p.list_len - 1)) : 0;
-        orow = min(max(orow, (int64_t)0), (int64_t)p.out_nrows - 1);
-        rs = valid ? __ldg(p.row_scale + orow) : 0.f;
-      } else {
-        orow = min(orow, (int64_t)p.out_nrows - 1);
-      }
-      if constexpr (EPI == EPI_SILU_TILE || EPI == EPI_SILU_ROUND) {
-        uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * (BN / 2);
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN / 2; c0 += 16) {
-          float g[16], u[16];
-          tmem_ld16(tbase + c0, g);
-          tmem_ld16(tbase + BN / 2 + c0, u);
-          if (valid) {
-            uint32_t o[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float a0, a1;
-              if constexpr (EPI == EPI_SILU_TILE) {
-                a0 = silu(g[2 * j]) * u[2 * j];
-                a1 = silu(g[2 * j + 1]) * u[2 * j + 1];
-              } else {
-                a0 = silu(bf2f(f2bf(g[2 * j]))) * bf2f(f2bf(u[2 * j]));
-                a1 = silu(bf2f(f2bf(g[2 * j + 1]))) * bf2f(f2bf(u[2 * j + 1]));
-              }
-              o[j] = (uint32_t)f2bf(a0) | ((uint32_t)f2bf(a1) << 16);
-            }
-            reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
-          }
-        }
-      } else if constexpr (EPI == EPI_BF16) {
-        uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * BN;
-        const int ncol = min(BN, p.n_valid - nt * BN);
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          float v[16];
-          tmem_ld16(tbase + c0, v);
-          if (valid && c0 + 16 > ncol) {
-            for (int j = 0; j < 16 && c0 + j < ncol; ++j) out[c0 + j] = f2bf(v[j]);
-          } else if (valid) {
-            uint32_t o[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = (uint32_t)f2bf(v[2 * j]) | ((uint32_t)f2bf(v[2 * j + 1]) << 16);
-            reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
-          }
-        }
-      } else {  // EPI_F32, EPI_SLOT
-        float* out = static_cast<float*>(p.out) + orow * p.ldo + nt * BN;
-        const int ncol = min(BN, p.n_valid - nt * BN);
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          float v[16];
-          tmem_ld16(tbase + c0, v);
-          if (valid && c0 + 16 <= ncol) {
-#pragma unroll
-            for (int j = 0; j < 16; j += 4)
-              *reinterpret_cast<float4*>(out + c0 + j) = make_float4(v[j] * rs, v[j + 1] * rs, v[j + 2] * rs,
-                                                                     v[j + 3] * rs);
-          } else if (valid) {
-            for (int j = 0; j < 16 && c0 + j < ncol; ++j) out[c0 + j] = v[j] * rs;
-          }
+        __syncwarp();
+        if (lane == 0) {
+          if (sub == c.rk - 1) mbar_arrive(&freeR[sr]);  // the raw stage's last k-step
+          mbar_arrive(&fullB[sb]);
         }
       }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&sc_free[sbuf]);
     }
   }
 
   fence_before_sync();
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 3) {
     fence_after_sync();
-    tmem_dealloc(tmem, kCols);
+    tmem_dealloc(tmem, cols);
   }
 }
 
 // ------------------------------------------------------------------ host side
 
-static int smem_optin() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (n <= 0) n = 227 * 1024;
+static int dev_attr(cudaDeviceAttr a, int fallback) {
+  int dev = 0, v = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&v, a, dev) != cudaSuccess || v <= 0) v = fallback;
+  return v;
+}
+
+static bool pick_cfg(int bn, int mt, bool int4, int K, int G, GemmCfg* out) {
+  static int optin = 0;
+  if (!optin) optin = dev_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin, 227 * 1024);
+  // deepest rings that fit: the raw INT4 ring first (its loads come from HBM), then A, then the bf16 B ring
+  const int sr_c[] = {4, 3, 2}, sa_c[] = {4, 3, 2}, sb_c[] = {4, 3, 2};
+  for (int sr : sr_c) {
+    for (int sa : sa_c)
+      for (int sb : sb_c) {
+        if (int4 && sb == 4) continue;
+        const GemmCfg c = gemm_cfg(bn, mt, int4, sa, sb, sr, K, G);
+        if ((int)c.total <= optin) {
+          *out = c;
+          return true;
+        }
+      }
+    if (!int4) break;
   }
-  return n;
+  return false;
 }
 
-static int pick_stages(int bn, bool int4, int K, int G) {
-  for (int s = 4; s >= 2; --s)
-    if ((int)gemm_smem(bn, int4, s, K, G).total <= smem_optin()) return s;
-  return 0;
-}
-
-size_t gemm_smem_bytes(int bn, bool int4, int K, int G) {
-  const int s = pick_stages(bn, int4, K, G);
-  return s ? gemm_smem(bn, int4, s, K, G).total : 0;
+// 2D tensor map over a row-major [outer][inner] array; rows are row_bytes apart. Out-of-range box elements read 0.
+static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  memset(m, 0, sizeof *m);
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return cuTensorMapEncodeTiled(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int BN, bool INT4, int EPI>
-static cudaError_t launch_t(const GemmParams& p, int max_tiles, cudaStream_t st) {
-  const int S = pick_stages(BN, INT4, p.K, p.G);
-  if (!S) return cudaErrorInvalidValue;
-  const size_t smem = gemm_smem(BN, INT4, S, p.K, p.G).total;
-  static size_t granted = 0;
-  if (smem > granted) {
-    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<BN, INT4, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    granted = smem;
+static cudaError_t launch_t(const GemmParams& p, int tile_rows, int max_tiles, bool pdl, cudaStream_t st) {
+  GemmCfg c;
+  if (!pick_cfg(BN, tile_rows / 128, INT4, p.K, p.G, &c)) return cudaErrorInvalidValue;
+  c.a_tma = p.a_rows ? 0 : 1;
+  CUtensorMap tmA, tmB, tmS;
+  memset(&tmA, 0, sizeof tmA);
+  memset(&tmS, 0, sizeof tmS);
+  const int rows_box = p.paired ? BN / 2 : BN;
+  if (c.a_tma && !make_map(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.A, (uint64_t)p.K, (uint64_t)p.a_nrows,
+                           (uint64_t)p.lda * 2, kBK, 128, true))
+    return cudaErrorInvalidValue;
+  if (INT4) {
+    const uint64_t rows = (uint64_t)p.E * p.b_rows_per_e;
+    if (!make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.Bq, (uint64_t)p.K / 2, rows, (uint64_t)p.K / 2,
+                  (uint32_t)(32 * c.rk), rows_box, false))
+      return cudaErrorInvalidValue;
+    if (c.s_tma && !make_map(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.Bs, (uint64_t)c.ksc, rows, (uint64_t)c.sstride,
+                             c.ksc, rows_box, false))
+      return cudaErrorInvalidValue;
+  } else {
+    const uint64_t rows = p.paired ? (uint64_t)p.N : (uint64_t)p.n_valid;
+    if (!make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.Bh, (uint64_t)p.K, rows, (uint64_t)p.K * 2, kBK,
+                  rows_box, true))
+      return cudaErrorInvalidValue;
   }
-  const int64_t grid = (int64_t)max_tiles * (p.N / BN);
-  if (grid <= 0) return cudaSuccess;
-  if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-  moe_gemm_kernel<BN, INT4, EPI><<<(unsigned)grid, kGThreads, smem, st>>>(p, S);
-  return cudaGetLastError();
+  static size_t granted = 0;
+  if (c.total > granted) {
+    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<BN, INT4, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)c.total);
+    if (e != cudaSuccess) return e;
+    granted = c.total;
+  }
+  static int sms = 0;
+  if (!sms) sms = dev_attr(cudaDevAttrMultiProcessorCount, 148);
+  const int64_t items = (int64_t)max_tiles * (p.N / BN);
+  if (items <= 0) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::min<int64_t>(items, sms));
+  cfg.blockDim = dim3(kGThreads);
+  cfg.dynamicSmemBytes = c.total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, moe_gemm_kernel<BN, INT4, EPI>, p, tmA, tmB, tmS, c);
 }
 
 template <int BN, bool INT4>
-static cudaError_t launch_epi(const GemmParams& p, int epi, int max_tiles, cudaStream_t st) {
+static cudaError_t launch_epi(const GemmParams& p, int epi, int tile_rows, int max_tiles, bool pdl, cudaStream_t st) {
   switch (epi) {
-    case EPI_F32: return launch_t<BN, INT4, EPI_F32>(p, max_tiles, st);
-    case EPI_BF16: return launch_t<BN, INT4, EPI_BF16>(p, max_tiles, st);
-    case EPI_SILU_TILE: return launch_t<BN, INT4, EPI_SILU_TILE>(p, max_tiles, st);
-    case EPI_SILU_ROUND: return launch_t<BN, INT4, EPI_SILU_ROUND>(p, max_tiles, st);
-    case EPI_SLOT: return launch_t<BN, INT4, EPI_SLOT>(p, max_tiles, st);
+    case EPI_F32: return launch_t<BN, INT4, EPI_F32>(p, tile_rows, max_tiles, pdl, st);
+    case EPI_BF16: return launch_t<BN, INT4, EPI_BF16>(p, tile_rows, max_tiles, pdl, st);
+    case EPI_SILU_TILE: return launch_t<BN, INT4, EPI_SILU_TILE>(p, tile_rows, max_tiles, pdl, st);
+    case EPI_SILU_ROUND: return launch_t<BN, INT4, EPI_SILU_ROUND>(p, tile_rows, max_tiles, pdl, st);
+    case EPI_SLOT: return launch_t<BN, INT4, EPI_SLOT>(p, tile_rows, max_tiles, pdl, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, bool int4, int max_tiles, cudaStream_t st) {
+cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, int tile_rows, bool int4, int max_tiles, bool pdl,
+                        cudaStream_t st) {
   if (p.K <= 0 || p.K % kBK || p.N <= 0 || p.N % bn || p.lda % 8 || p.ldo % 8 || !p.A || !p.out) return cudaErrorInvalidValue;
+  if (tile_rows != 128 && tile_rows != 256) return cudaErrorInvalidValue;
   if (p.n_valid <= 0 || p.n_valid > p.N || (p.paired && p.n_valid != p.N)) return cudaErrorInvalidValue;
   const void* ptrs[5] = {p.A, p.Bh, p.Bq, p.Bs, p.out};
   for (const void* q : ptrs)
@@ -503,9 +693,12 @@ cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, bool int4, int max
     return cudaErrorInvalidValue;
   }
   switch (bn) {
-    case 64: return int4 ? launch_epi<64, true>(p, epi, max_tiles, st) : launch_epi<64, false>(p, epi, max_tiles, st);
-    case 128: return int4 ? launch_epi<128, true>(p, epi, max_tiles, st) : launch_epi<128, false>(p, epi, max_tiles, st);
-    case 256: return int4 ? launch_epi<256, true>(p, epi, max_tiles, st) : launch_epi<256, false>(p, epi, max_tiles, st);
+    case 64:
+      return int4 ? launch_epi<64, true>(p, epi, tile_rows, max_tiles, pdl, st)
+                  : launch_epi<64, false>(p, epi, tile_rows, max_tiles, pdl, st);
+    case 128:
+      return int4 ? launch_epi<128, true>(p, epi, tile_rows, max_tiles, pdl, st)
+                  : launch_epi<128, false>(p, epi, tile_rows, max_tiles, pdl, st);
     default: return cudaErrorInvalidValue;
   }
 }

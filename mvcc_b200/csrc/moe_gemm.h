@@ -1,7 +1,7 @@
 // moe_gemm.h -- host interface of the tcgen05 tile GEMM (moe_gemm.cu) behind the prefill path.
 //
-// D[m][n] = sum_k A[row(m)][k] * B[row(n)][k] over 128-row tiles of A and BN-row tiles of B, both K-major bf16
-// in shared memory (B optionally dequantized there from INT4), fp32 accumulators in TMEM, one of five epilogues.
+// D[m][n] = sum_k A[row(m)][k] * B[row(n)][k] over tiles of up to 256 A rows and BN B rows, both K-major bf16 in
+// shared memory (B optionally dequantized there from INT4), fp32 accumulators in TMEM, one of five epilogues.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -16,7 +16,8 @@ enum GemmEpi {
   EPI_SLOT = 4,        // out fp32 [pair][n] = acc * row_scale[pair]        (routed down -> slot partials)
 };
 
-// One M tile of the grouped problem: B matrix (expert) e, first A row m0 (in the tile-row space), rows mcount.
+// One M tile of the grouped problem: B matrix (expert) e, first A row m0 (in the tile-row space), rows mcount
+// (at most the launch's tile rows, 128 or 256).
 struct GemmTile {
   int e, m0, mcount, pad;
 };
@@ -52,11 +53,12 @@ struct GemmParams {
   uint32_t* err;             // error word (bounded waits)
 };
 
-// Launches the GEMM over max_tiles x (N / BN) CTAs (tiles beyond *ntiles exit at once). bn in {64, 128, 256};
-// int4 selects the INT4 B path. Returns cudaErrorInvalidValue for unsupported parameters.
-cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, bool int4, int max_tiles, cudaStream_t s);
-
-// Dynamic shared memory the launch uses (0 if the configuration is unsupported).
-size_t gemm_smem_bytes(int bn, bool int4, int K, int G);
+// Persistent launch over min(SMs, max_tiles x N/BN) CTAs; work item i = (tile i / (N/BN), n-tile i % (N/BN)),
+// items past *ntiles x N/BN are skipped. bn in {64, 128}; tile_rows in {128, 256} (rows of A per tile, the row
+// count the tile list was built with); int4 selects the INT4 B path. pdl: launched as a programmatic dependent
+// of the previous kernel on the stream (its prologue overlaps that kernel's tail). Returns cudaErrorInvalidValue
+// for unsupported parameters.
+cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, int tile_rows, bool int4, int max_tiles, bool pdl,
+                        cudaStream_t s);
 
 }  // namespace moe

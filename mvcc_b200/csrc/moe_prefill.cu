@@ -9,7 +9,7 @@
 //   topk        the reference's top-k rule per token (router_topk_kernel, kernels.cuh:774-809); marks bit p of
 //               expert e's bitmap for every pair p = t * TOPK + slot
 //   scan        per expert: popcounts and word prefixes of its bitmap; the last CTA turns the counts into the
-//               expert offsets and the grouped-GEMM tile list (128 pairs per tile)
+//               expert offsets and the grouped-GEMM tile list (kTileRows = 256 pairs per tile)
 //   scatter     pair p of expert e goes to offsets[e] + (pairs of e before p): a stable counting sort by pair
 //               index, bit-exact and deterministic (moe_sort_kernel, kernels.cuh:906-923, orders ties arbitrarily)
 //   gate_up     grouped INT4 GEMM, A rows gathered per sorted pair, epilogue bf16(silu(g) * u) -> inter (sorted)
@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(kPT) prefill_scan_kernel(const BlockArgs a) {
   const int cnt = tid < E ? __ldcg(a.counts + tid) : 0;
   int npairs;
   const int off = block_excl_scan(cnt, sm, &npairs);
-  const int nt = (cnt + 127) / 128;
+  const int nt = (cnt + kTileRows - 1) / kTileRows;
   int ntiles;
   const int tbase = block_excl_scan(nt, sm, &ntiles);
   GemmTile* tiles = static_cast<GemmTile*>(a.tiles);
@@ -169,8 +169,8 @@ __global__ void __launch_bounds__(kPT) prefill_scan_kernel(const BlockArgs a) {
     for (int j = 0; j < nt && tbase + j < a.max_tiles; ++j) {
       GemmTile g;
       g.e = tid;
-      g.m0 = off + 128 * j;
-      g.mcount = min(128, cnt - 128 * j);
+      g.m0 = off + kTileRows * j;
+      g.mcount = min(kTileRows, cnt - kTileRows * j);
       g.pad = 0;
       tiles[tbase + j] = g;
     }
@@ -292,7 +292,7 @@ static cudaError_t run_router(const BlockArgs& a, cudaStream_t s) {
   p.out = a.logits;
   p.ldo = a.w.E;
   p.out_nrows = a.T;
-  return launch_gemm(p, EPI_F32, 64, false, (a.T + 127) / 128, s);
+  return launch_gemm(p, EPI_F32, 64, 128, false, (a.T + 127) / 128, false, s);
 }
 
 static cudaError_t run_sort(const BlockArgs& a, bool from_topk, cudaStream_t s) {
@@ -335,7 +335,7 @@ static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s) {
   g.out = a.inter;
   g.ldo = a.w.I;
   g.out_nrows = P;
-  cudaError_t e = launch_gemm(g, EPI_SILU_TILE, 256, true, a.max_tiles, s);
+  cudaError_t e = launch_gemm(g, EPI_SILU_TILE, 128, kTileRows, true, a.max_tiles, false, s);
   if (e != cudaSuccess) return e;
   // down: A = inter rows in sorted order, B = expert down rows; epilogue weights by w[pair] into slot[pair]
   GemmParams d = base_params(a);
@@ -357,7 +357,7 @@ static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s) {
   d.list_len = P;
   d.row_scale = a.wts;
   d.out_nrows = P;
-  return launch_gemm(d, EPI_SLOT, 256, true, a.max_tiles, s);
+  return launch_gemm(d, EPI_SLOT, 128, kTileRows, true, a.max_tiles, false, s);
 }
 
 cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s) {
@@ -375,7 +375,7 @@ cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s) {
   g.out = a.sinter;
   g.ldo = a.w.Is;
   g.out_nrows = a.T;
-  cudaError_t e = launch_gemm(g, EPI_SILU_ROUND, 256, false, (a.T + 127) / 128, s);
+  cudaError_t e = launch_gemm(g, EPI_SILU_ROUND, 128, 256, false, (a.T + 255) / 256, false, s);
   if (e != cudaSuccess) return e;
   GemmParams d = base_params(a);
   d.A = a.sinter;
@@ -389,7 +389,7 @@ cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s) {
   d.out = a.sout;
   d.ldo = a.w.H;
   d.out_nrows = a.T;
-  return launch_gemm(d, EPI_BF16, 256, false, (a.T + 127) / 128, s);
+  return launch_gemm(d, EPI_BF16, 128, 256, false, (a.T + 255) / 256, false, s);
 }
 
 static cudaError_t clear_bits(const BlockArgs& a, cudaStream_t s) {
