@@ -145,7 +145,7 @@ constexpr int kPrefillMinT = 8;
 
 // Rows (sorted pairs of one expert) per grouped-GEMM tile, and the upper bound of the tiles for P pairs over E
 // experts: sum_e ceil(n_e / kTileRows).
-constexpr int kTileRows = 256;
+constexpr int kTileRows = 128;
 __host__ __device__ inline int prefill_max_tiles(int P, int E) { return P / kTileRows + (E < P ? E : P) + 1; }
 
 __host__ __device__ inline size_t ws_align(size_t x) { return (x + 255) & ~(size_t)255; }

@@ -2,30 +2,38 @@
 // shared-expert GEMMs (dense(), qwen.cu:298-319) and the grouped INT4 expert GEMMs (moe_gate_up_tile_kernel,
 // moe_down_tile_kernel, kernels.cuh:942-1057).
 //
-// One CTA per SM walks work items (tile of up to 256 A rows) x (n-tile of BN B rows), K in steps of 64, through
-// three shared-memory rings; 16 warps:
+// One CTA per SM walks work items (tile of up to 128 A rows) x (n-tile of BN B rows), K in steps of 64. Stage s
+// of the ring holds one step's A rows and bf16 B rows; full[s] completes when both are in, empty[s] when the MMAs
+// that read them are done -- one wait and one commit per step for the issuing thread, whose shared-memory round
+// trips (a few hundred cycles per barrier operation) must stay under a step's MMA time (512 cycles at N = 256).
+// 16 warps:
 //   warps 0-1   A producers: contiguous A rows come in as one 2D TMA tile (box 64 x 128, 128-byte swizzle) per
-//               128-row sub-tile and step; gathered rows (one per (token, slot) pair of the sorted pair list) come
-//               in by cp.async, eight lanes per row so that each row is one 128-byte line request, into the same
-//               swizzled K-major layout (cp.async.mbarrier.arrive.noinc on fullA[s]);
-//   warp 2      B producer, one lane: TMA tiles of bf16 B rows straight into the B ring (fullB), or of INT4 rows
-//               (box 32 bytes x BN rows) into the raw ring (fullR) plus, once per item, the item's fp16 group
+//               step; gathered rows (one per (token, slot) pair of the sorted pair list) come in by cp.async,
+//               eight lanes per row so that each row is one 128-byte line request, into the same swizzled K-major
+//               layout (cp.async.mbarrier.arrive.noinc on full[s]);
+//   warp 2      B producer, one lane: TMA tiles of the step's bf16 B rows into stage s, or of INT4 rows (rk
+//               k-steps of each row per box) into the raw ring (fullR) and, once per item, of the item's fp16 group
 //               scales; completion by transaction count (mbarrier expect_tx). No load uses cluster multicast;
-//   warp 3      allocates TMEM (two accumulator buffers of (rows / 128) x BN fp32 columns) and, from one lane,
-//               issues the tcgen05.mma of each step (M=128 per 128-row sub-tile, N=BN, K=16 x 4), committing to
-//               emptyA / emptyB (stage free) and, after an item's last step, to acc_full[buffer];
+//   warp 3      allocates TMEM (two accumulator buffers of BN fp32 columns) and, from one lane, issues the
+//               tcgen05.mma of each step (M=128, N=BN, K=16 x 4), committing to empty[s] and, after an item's last
+//               step, to acc_full[buffer];
 //   warps 4-7   epilogue: wait acc_full, tcgen05.ld the accumulator rows of their TMEM lane quarter, apply the
 //               epilogue, store, release the buffer (acc_empty) -- overlapping the next item's main loop;
-//   warps 8-15  INT4 only: dequantize raw[r] into bf16 B[s] as dequant32_bf16 does (kernels.cuh:925-940:
-//               bf16((q - 8) * scale), one rounding), fence the writes to the async proxy, arrive on fullB.
+//   warps 8-15  INT4 only: each thread owns (row, K half) jobs of the tile (two at BN = 256) and converts their
+//               32 nibbles per step from the raw ring into the swizzled bf16 B of stage s as dequant32_bf16 does
+//               (kernels.cuh:925-940: bf16((q - 8) * scale), one rounding), fences the writes to the async proxy and
+//               arrives on full[s]. Raw bytes and scales come by TMA: loading them through the load/store unit
+//               costs about as many cycles as the conversion itself.
 // Every wait is bounded: kWaitNs after its first miss a waiting thread records MOE_ERR_TIMEOUT in the error word,
 // raises the CTA's abort flag (other waits poll it) and leaves its loop; the CTA then drains its copies, frees TMEM
 // and exits.
 //
-// Exact dequantization without a conversion instruction per nibble: a nibble q at bit position 4p of a word,
-// OR-ed into 0x4B000000, is the float 2^23 + q * 2^(4p); subtracting 2^23 + 8 * 2^(4p) leaves (q - 8) * 2^(4p)
-// exactly, and multiplying by scale * 2^(-4p) gives (q - 8) * scale exactly (at most 15 significant bits); one
-// cvt.rn.bf16x2.f32 rounds two such values to bf16, the reference's single rounding.
+// Exact dequantization with one FMA per pair of weights: a nibble q at bit position 4p of a word, OR-ed into
+// 0x4B000000, is the float f = 2^23 + q * 2^(4p). For p in {2, 3, 4} the product M_p * s of the offset
+// M_p = 2^23 + 8 * 2^(4p) with an fp16 scale s fits in 24 bits, so fma(f, s * 2^(-4p), -M_p * s * 2^(-4p))
+// yields (q - 8) * s exactly (15 significant bits); every nibble of a word reaches one of those positions in the
+// word itself, the word shifted left by 8 or shifted right by 12. One cvt.rn.bf16x2.f32 then rounds two values to
+// bf16: the reference's single rounding.
 #include <cuda.h>
 
 #include <algorithm>
@@ -39,35 +47,38 @@ namespace moe {
 
 using namespace tc;
 
-constexpr int kBK = 64;
+constexpr int kBK = 64, kTileM = 128;
 constexpr int kGWarps = 16, kGThreads = kGWarps * 32;
 constexpr int kDeqWarp0 = 8, kDeqThreads = 256;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far beyond any item's main loop
 
 struct GemmCfg {
-  int bn, mt, sa, sb, sr, ksc, sstride;  // BN, 128-row sub-tiles per tile, ring depths, scales per row, row stride
-  int rk;                                // k-steps per raw INT4 stage (a row's 32 * rk contiguous bytes per load)
-  int a_tma, s_tma;                      // A by TMA tiles (contiguous rows), scales by TMA (rows >= 16 bytes)
+  int bn, sa;            // BN, A + B ring depth
+  int sr, rk;            // INT4: raw ring depth, k-steps per raw stage (a row's 32 * rk bytes per box)
+  int ksc, sstride;      // INT4: scales per B row, their bytes per row in shared memory
+  int a_tma, s_tma;      // A by TMA tiles (contiguous rows); scales by TMA (rows of at least 16 bytes)
   size_t a, b, raw, sc, bar, total;
 };
 
-__host__ __device__ inline size_t g_align(size_t x, size_t a) { return (x + a - 1) / a * a; }
-
-__host__ __device__ inline GemmCfg gemm_cfg(int bn, int mt, bool int4, int sa, int sb, int sr, int K, int G) {
+__host__ __device__ inline GemmCfg gemm_cfg(int bn, bool int4, int sa, int sr, int rk, int K, int G) {
   GemmCfg c;
-  c.bn = bn; c.mt = mt; c.sa = sa; c.sb = sb; c.sr = int4 ? sr : 0;
+  c.bn = bn;
+  c.sa = sa;
   const int nk = K / kBK;
-  c.rk = nk % 4 == 0 ? 4 : (nk % 2 == 0 ? 2 : 1);
+  while (rk > 1 && nk % rk) rk >>= 1;
+  c.rk = rk;
+  c.sr = int4 ? sr : 0;
   c.ksc = int4 ? K / G : 0;
   c.sstride = c.ksc * 2;
   c.a_tma = 0;
   c.s_tma = int4 && c.sstride >= 16;
   size_t o = 0;
-  c.a = o;   o += (size_t)sa * mt * 128 * 128;  // 16 KiB per 128-row sub-tile and stage (1024-byte aligned)
-  c.b = o;   o += (size_t)sb * bn * 128;
-  c.raw = o; o += (size_t)c.sr * bn * 32 * c.rk;
-  c.sc = o;  o = g_align(o + (int4 ? 2 * (size_t)bn * c.sstride : 0), 128);
-  c.bar = o; o += 8 * (size_t)(2 * sa + 2 * sb + 2 * c.sr + 8) + 16;
+  c.a = o;   o += (size_t)sa * kTileM * 128;  // 16 KiB per stage (1024-byte aligned)
+  c.b = o;   o += (size_t)sa * bn * 128;
+  c.raw = o; o += (size_t)c.sr * bn * 32 * rk;
+  c.sc = o;  o += int4 ? 2 * (size_t)bn * c.sstride : 0;
+  c.bar = (o + 127) / 128 * 128;
+  o = c.bar + 8 * (size_t)(2 * sa + 2 * c.sr + 8) + 16;
   c.total = o + 1024;  // the dynamic base is aligned up to 1024 bytes at run time
   return c;
 }
@@ -83,11 +94,8 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
       "}" ::"r"(smem_u32(mbar))
       : "memory");
 }
-__device__ __forceinline__ void cp_async_n(void* dst, const void* src, int bytes) {
-  const uint32_t d = smem_u32(dst);
-  if (bytes == 16) asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
-  else if (bytes == 8) asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(src) : "memory");
-  else asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
 // 2D TMA tile load into this CTA's shared memory, completion counted in bytes on mbar (no multicast).
@@ -96,6 +104,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           smem_u32(dst)),
       "l"(map), "r"(x), "r"(y), "r"(smem_u32(mbar))
+      : "memory");
+}
+// 4D variant: a paired gate/up operand, viewed as [expert][half][row][k], comes in as one box of both halves.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(mbar))
       : "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
@@ -145,36 +162,53 @@ __device__ __forceinline__ bool wait_bar(uint64_t* mbar, uint32_t parity, volati
   }
 }
 
-// 8 nibbles of u (k = 8w .. 8w + 7) times the scale -> 8 bf16 (one 16-byte chunk), exact products, RNE.
-// sc01 = (s, s/16), sc23 = (s/256, s/4096), sc45 = (s/65536, s/256), sc67 = (s/4096, s/65536).
-__device__ __forceinline__ uint4 dequant8_bf16(uint32_t u, u64 sc01, u64 sc23, u64 sc45, u64 sc67,
-                                               const Nib8Magic& M) {
+// Per-scale constants of dequant8_bf16: (scale * 2^(-4p), -M_p * scale * 2^(-4p)) packed for the position pairs
+// (p2, p3), (p4, p2), (p3, p4).
+struct DqConst {
+  u64 s23, c23, s42, c42, s34, c34;
+};
+__device__ __forceinline__ u64 pack2f(float lo, float hi) {
+  return ((u64)__float_as_uint(hi) << 32) | (u64)__float_as_uint(lo);
+}
+__device__ __forceinline__ DqConst dq_const(float s) {
+  const float s2 = s * (1.f / 256.f), s3 = s * (1.f / 4096.f), s4 = s * (1.f / 65536.f);
+  const float c2 = -32776.f * s, c3 = -2056.f * s, c4 = -136.f * s;  // -(2^15 + 8) s, -(2^11 + 8) s, -(2^7 + 8) s
+  DqConst d;
+  d.s23 = pack2f(s2, s3);
+  d.c23 = pack2f(c2, c3);
+  d.s42 = pack2f(s4, s2);
+  d.c42 = pack2f(c4, c2);
+  d.s34 = pack2f(s3, s4);
+  d.c34 = pack2f(c3, c4);
+  return d;
+}
+
+// 8 nibbles of u (k = 8w .. 8w + 7, nibble i at bits 4i) -> 8 bf16 (one 16-byte chunk), exact products, RNE.
+//   nibbles 0, 1: u << 8 at p = 2, 3;  nibbles 2, 3, 4: u at p = 2, 3, 4;  nibbles 5, 6, 7: u >> 12 at p = 2, 3, 4.
+__device__ __forceinline__ uint4 dequant8_bf16(uint32_t u, const DqConst& d) {
   uint4 o;
   asm("{\n\t"
-      ".reg .b32 v, f0, f1, f2, f3, f4, f5, f6, f7;\n\t"
+      ".reg .b32 v0, v1, f0, f1, f2, f3, f4, f5, f6, f7;\n\t"
       ".reg .b64 p01, p23, p45, p67;\n\t"
       ".reg .f32 a0, a1, a2, a3, a4, a5, a6, a7;\n\t"
-      "shr.b32 v, %4, 12;\n\t"
-      "lop3.b32 f0, %4, 0xF, 0x4B000000, 0xEA;\n\t"
-      "lop3.b32 f1, %4, 0xF0, 0x4B000000, 0xEA;\n\t"
+      "shl.b32 v0, %4, 8;\n\t"
+      "shr.b32 v1, %4, 12;\n\t"
+      "lop3.b32 f0, v0, 0xF00, 0x4B000000, 0xEA;\n\t"
+      "lop3.b32 f1, v0, 0xF000, 0x4B000000, 0xEA;\n\t"
       "lop3.b32 f2, %4, 0xF00, 0x4B000000, 0xEA;\n\t"
       "lop3.b32 f3, %4, 0xF000, 0x4B000000, 0xEA;\n\t"
       "lop3.b32 f4, %4, 0xF0000, 0x4B000000, 0xEA;\n\t"
-      "lop3.b32 f5, v, 0xF00, 0x4B000000, 0xEA;\n\t"
-      "lop3.b32 f6, v, 0xF000, 0x4B000000, 0xEA;\n\t"
-      "lop3.b32 f7, v, 0xF0000, 0x4B000000, 0xEA;\n\t"
+      "lop3.b32 f5, v1, 0xF00, 0x4B000000, 0xEA;\n\t"
+      "lop3.b32 f6, v1, 0xF000, 0x4B000000, 0xEA;\n\t"
+      "lop3.b32 f7, v1, 0xF0000, 0x4B000000, 0xEA;\n\t"
       "mov.b64 p01, {f0, f1};\n\t"
       "mov.b64 p23, {f2, f3};\n\t"
       "mov.b64 p45, {f4, f5};\n\t"
       "mov.b64 p67, {f6, f7};\n\t"
-      "add.rn.f32x2 p01, p01, %9;\n\t"
-      "add.rn.f32x2 p23, p23, %10;\n\t"
-      "add.rn.f32x2 p45, p45, %11;\n\t"
-      "add.rn.f32x2 p67, p67, %12;\n\t"
-      "mul.rn.f32x2 p01, p01, %5;\n\t"
-      "mul.rn.f32x2 p23, p23, %6;\n\t"
-      "mul.rn.f32x2 p45, p45, %7;\n\t"
-      "mul.rn.f32x2 p67, p67, %8;\n\t"
+      "fma.rn.f32x2 p01, p01, %5, %6;\n\t"
+      "fma.rn.f32x2 p23, p23, %5, %6;\n\t"
+      "fma.rn.f32x2 p45, p45, %7, %8;\n\t"
+      "fma.rn.f32x2 p67, p67, %9, %10;\n\t"
       "mov.b64 {a0, a1}, p01;\n\t"
       "mov.b64 {a2, a3}, p23;\n\t"
       "mov.b64 {a4, a5}, p45;\n\t"
@@ -185,12 +219,17 @@ __device__ __forceinline__ uint4 dequant8_bf16(uint32_t u, u64 sc01, u64 sc23, u
       "cvt.rn.bf16x2.f32 %3, a7, a6;\n\t"
       "}"
       : "=r"(o.x), "=r"(o.y), "=r"(o.z), "=r"(o.w)
-      : "r"(u), "l"(sc01), "l"(sc23), "l"(sc45), "l"(sc67), "l"(M.m01), "l"(M.m23), "l"(M.m45), "l"(M.m67));
+      : "r"(u), "l"(d.s23), "l"(d.c23), "l"(d.s42), "l"(d.c42), "l"(d.s34), "l"(d.c34));
   return o;
 }
 
-__device__ __forceinline__ u64 pack2f(float lo, float hi) {
-  return ((u64)__float_as_uint(hi) << 32) | (u64)__float_as_uint(lo);
+// 16-byte streaming load that bypasses L1 allocation (each weight byte is used by one thread once).
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
 }
 
 template <int BN>
@@ -201,17 +240,17 @@ __device__ __forceinline__ int64_t b_row(const GemmParams& p, int e, int nt, int
   return (int64_t)e * p.b_rows_per_e + row;
 }
 
-__device__ __forceinline__ GemmTile load_tile(const GemmParams& p, int ti, int tile_rows) {
+__device__ __forceinline__ GemmTile load_tile(const GemmParams& p, int ti) {
   GemmTile t;
   if (p.tiles) {
     t = p.tiles[ti];
   } else {
     t.e = 0;
-    t.m0 = ti * tile_rows;
+    t.m0 = ti * kTileM;
     t.mcount = p.M - t.m0;
   }
   t.e = min(max(t.e, 0), p.E - 1);
-  t.mcount = max(0, min(t.mcount, tile_rows));
+  t.mcount = max(0, min(t.mcount, kTileM));
   if (t.m0 < 0) t.mcount = 0;
   return t;
 }
@@ -223,15 +262,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int MT = c.mt, tile_rows = 128 * MT, SA = c.sa, SB = c.sb, SR = c.sr;
+  const int SA = c.sa, SR = c.sr;
   const int nN = p.N / BN, nk = p.K / kBK;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + c.bar);
-  uint64_t* fullA = bars;
-  uint64_t* emptyA = fullA + SA;
-  uint64_t* fullB = emptyA + SA;
-  uint64_t* emptyB = fullB + SB;
-  uint64_t* fullR = emptyB + SB;
+  uint64_t* full = bars;
+  uint64_t* empty = full + SA;
+  uint64_t* fullR = empty + SA;
   uint64_t* freeR = fullR + SR;
   uint64_t* sc_full = freeR + SR;      // [2]
   uint64_t* sc_free = sc_full + 2;     // [2]
@@ -239,16 +276,12 @@ __global__ void __launch_bounds__(kGThreads, 1)
   uint64_t* acc_empty = acc_full + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  const uint32_t cols = 2u * MT * BN;  // 128, 256 or 512
+  constexpr uint32_t cols = 2u * BN;  // 128, 256 or 512
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
-      mbar_init(&fullA[s], c.a_tma ? 1 : 64);
-      mbar_init(&emptyA[s], 1);
-    }
-    for (int s = 0; s < SB; ++s) {
-      mbar_init(&fullB[s], INT4 ? kDeqThreads / 32 : 1);
-      mbar_init(&emptyB[s], 1);
+      mbar_init(&full[s], (c.a_tma ? 1 : 64) + (INT4 ? kDeqThreads / 32 : 1));
+      mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < SR; ++s) {
       mbar_init(&fullR[s], 1);
@@ -265,7 +298,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
   }
   // everything above touches only this CTA's shared memory: it overlaps the previous kernel under PDL
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int ntiles = p.tiles ? min(*p.ntiles, 1 << 20) : (p.M + tile_rows - 1) / tile_rows;
+  const int ntiles = p.tiles ? min(*p.ntiles, 1 << 20) : (p.M + kTileM - 1) / kTileM;
   const int n_items = ntiles * nN;
   if ((int)blockIdx.x >= n_items) return;  // uniform for the CTA, before any TMEM is held
   if (warp == 3) tmem_alloc(tmem_slot, cols);
@@ -281,48 +314,45 @@ __global__ void __launch_bounds__(kGThreads, 1)
         int g = 0;
         bool ok = true;
         for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-          const GemmTile t = load_tile(p, it / nN, tile_rows);
-          const int msub = t.mcount > 128 ? 2 : 1;
-                    for (int kt = 0; kt < nk; ++kt, ++g) {
-            const int s = g % SA, kx = kt;
-            if (g >= SA && !wait_bar(&emptyA[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
-            uint8_t* dst = smem + c.a + (size_t)s * MT * 16384;
-            mbar_expect_tx(&fullA[s], (uint32_t)msub * 16384u);
-            for (int m = 0; m < msub; ++m) tma_load_2d(dst + m * 16384, &tmA, kx * kBK, t.m0 + m * 128, &fullA[s]);
+          const GemmTile t = load_tile(p, it / nN);
+          for (int kt = 0; kt < nk; ++kt, ++g) {
+            const int s = g % SA;
+            if (g >= SA && !wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+            mbar_expect_tx(&full[s], 16384u);
+            tma_load_2d(smem + c.a + (size_t)s * 16384, &tmA, kt * kBK, t.m0, &full[s]);
           }
         }
       }
     } else {
-      // gathered rows: lane l of the 64 fetches 16-byte chunk l % 8 of rows l / 8 + 8 i (i < 16 MT), so that each
+      // gathered rows: lane l of the 64 fetches 16-byte chunk l % 8 of rows l / 8 + 8 i (i < 16), so that each
       // warp instruction covers four whole 128-byte rows
       const int t64 = threadIdx.x, ch = t64 & 7, r0 = t64 >> 3;
       int g = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-        const GemmTile t = load_tile(p, it / nN, tile_rows);
-        int soff[32];  // element offset of the source row of rows r0 + 8 i, or -1
+        const GemmTile t = load_tile(p, it / nN);
+        int soff[16];  // element offset of the source row of rows r0 + 8 i, or -1
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 16; ++i) {
           const int r = r0 + 8 * i;
           soff[i] = -1;
-          if (i < 16 * MT && r < t.mcount) {
+          if (r < t.mcount) {
             int src = p.a_rows ? __ldg(p.a_rows + min(t.m0 + r, p.list_len - 1)) / p.a_div : t.m0 + r;
             src = min(max(src, 0), p.a_nrows - 1);
             soff[i] = (int)((int64_t)src * p.lda) + ch * 8;
           }
         }
-                for (int kt = 0; kt < nk; ++kt, ++g) {
-          const int s = g % SA, kx = kt;
-          if (g >= SA && !wait_bar(&emptyA[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
-          uint8_t* dst = smem + c.a + (size_t)s * MT * 16384;
+        for (int kt = 0; kt < nk; ++kt, ++g) {
+          const int s = g % SA;
+          if (g >= SA && !wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+          uint8_t* dst = smem + c.a + (size_t)s * 16384;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = 0; i < 16; ++i) {
             // rows past the tile are never loaded nor stored: their stale values are harmless
             if (soff[i] < 0) continue;
-            const int r = r0 + 8 * i;
-            cp_async_n(dst + (r >> 7) * 16384 + sw128_chunk(r & 127, ch), p.A + soff[i] + kx * kBK, 16);
+            cp_async16(dst + sw128_chunk(r0 + 8 * i, ch), p.A + soff[i] + kt * kBK);
           }
-          cp_async_arrive_noinc(&fullA[s]);
+          cp_async_arrive_noinc(&full[s]);
         }
       }
       asm volatile("cp.async.wait_all;" ::: "memory");
@@ -333,182 +363,173 @@ __global__ void __launch_bounds__(kGThreads, 1)
     int g = 0, j = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
-      const GemmTile t = load_tile(p, it / nN, tile_rows);
+      const GemmTile t = load_tile(p, it / nN);
       const int nt = it % nN;
-      // first B row of the item (and of its up half when paired)
-      const int y0 = (int)((int64_t)t.e * p.b_rows_per_e + (p.paired ? nt * HB : nt * BN));
-      const int y1 = (int)((int64_t)t.e * p.b_rows_per_e + p.pair_off + nt * HB);
+      const int y0 = (int)((int64_t)t.e * p.b_rows_per_e + nt * BN);
       if constexpr (INT4) {
         const int sb = j & 1;
-        int freed = 1;  // one lane waits, the warp follows its verdict (no divergent exits before the shuffles)
+        int freed = 1;  // one lane waits, the warp follows its verdict
         if (lane == 0 && j >= 2) freed = wait_bar(&sc_free[sb], ((j >> 1) - 1) & 1, abort_flag, p.err) ? 1 : 0;
         if (!__shfl_sync(0xffffffffu, freed, 0)) break;
         uint8_t* sdst = smem + c.sc + (size_t)sb * BN * c.sstride;
         if (c.s_tma) {
           if (lane == 0) {
             mbar_expect_tx(&sc_full[sb], (uint32_t)(BN * c.sstride));
-            tma_load_2d(sdst, &tmS, 0, y0, &sc_full[sb]);
-            if (p.paired) tma_load_2d(sdst + HB * c.sstride, &tmS, 0, y1, &sc_full[sb]);
+            if (p.paired) tma_load_4d(sdst, &tmS, 0, nt * HB, 0, t.e, &sc_full[sb]);
+            else tma_load_2d(sdst, &tmS, 0, y0, &sc_full[sb]);
           }
         } else {
           const int rb = c.sstride;  // 2, 4 or 8 bytes per row
           for (int r = lane; r < BN; r += 32) {
             if (!p.paired && nt * BN + r >= p.n_valid) continue;
-            const int64_t row = p.paired ? (r < HB ? y0 + r : y1 + r - HB) : (int64_t)y0 + r;
+            const int64_t row = b_row<BN>(p, t.e, nt, r);
             const uint8_t* src = reinterpret_cast<const uint8_t*>(p.Bs) + row * rb;
-            if (rb >= 4) cp_async_n(sdst + r * rb, src, rb);
-            else *reinterpret_cast<uint16_t*>(sdst + r * rb) = __ldg(reinterpret_cast<const uint16_t*>(src));
+            if (rb >= 4) {
+              const uint32_t d = smem_u32(sdst + r * rb);
+              if (rb == 8) asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(src) : "memory");
+              else asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+            } else {
+              *reinterpret_cast<uint16_t*>(sdst + r * rb) = __ldg(reinterpret_cast<const uint16_t*>(src));
+            }
           }
           if (rb >= 4) cp_async_arrive_noinc(&sc_full[sb]);
           else mbar_arrive(&sc_full[sb]);
         }
         if (lane == 0) {
-          // one raw stage = rk k-steps: 32 * rk contiguous bytes of each of the BN rows
           const int RB = 32 * c.rk;
           for (int kt = 0; kt < nk; kt += c.rk, g += c.rk) {
-            const int gr = g / c.rk, s = gr % SR, kx = kt;
+            const int gr = g / c.rk, s = gr % SR;
             if (gr >= SR && !wait_bar(&freeR[s], ((gr / SR) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
             uint8_t* dst = smem + c.raw + (size_t)s * BN * RB;
             mbar_expect_tx(&fullR[s], (uint32_t)(BN * RB));
-            tma_load_2d(dst, &tmB, kx * 32, y0, &fullR[s]);
-            if (p.paired) tma_load_2d(dst + HB * RB, &tmB, kx * 32, y1, &fullR[s]);
+            if (p.paired) tma_load_4d(dst, &tmB, kt * 32, nt * HB, 0, t.e, &fullR[s]);
+            else tma_load_2d(dst, &tmB, kt * 32, y0, &fullR[s]);
           }
         }
-        g = __shfl_sync(0xffffffffu, g, 0);
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       } else {
         if (lane == 0) {
-                    for (int kt = 0; kt < nk; ++kt, ++g) {
-            const int s = g % SB, kx = kt;
-            if (g >= SB && !wait_bar(&emptyB[s], ((g / SB) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+          for (int kt = 0; kt < nk; ++kt, ++g) {
+            const int s = g % SA;
+            if (g >= SA && !wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
             uint8_t* dst = smem + c.b + (size_t)s * BN * 128;
-            mbar_expect_tx(&fullB[s], (uint32_t)(BN * 128));
-            tma_load_2d(dst, &tmB, kx * kBK, y0, &fullB[s]);
-            if (p.paired) tma_load_2d(dst + HB * 128, &tmB, kx * kBK, y1, &fullB[s]);
+            mbar_expect_tx(&full[s], (uint32_t)(BN * 128));
+            if (p.paired) tma_load_4d(dst, &tmB, kt * kBK, nt * HB, 0, t.e, &full[s]);
+            else tma_load_2d(dst, &tmB, kt * kBK, y0, &full[s]);
           }
         }
-        g = __shfl_sync(0xffffffffu, g, 0);
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       }
+      g = __shfl_sync(0xffffffffu, g, 0);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == 3) {
     // ---- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(128, BN);
+      constexpr uint32_t idesc = idesc_bf16_f32(kTileM, BN);
       int g = 0, j = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
-        const GemmTile t = load_tile(p, it / nN, tile_rows);
         const int ab = j & 1;
         if (j >= 2 && !wait_bar(&acc_empty[ab], ((j >> 1) - 1) & 1, abort_flag, p.err)) break;
         fence_after_sync();
-        const int msub = t.mcount > 128 ? 2 : 1;
+        const uint32_t d = tmem + (uint32_t)(ab * BN);
         for (int kt = 0; kt < nk; ++kt, ++g) {
-          const int sa = g % SA, sb = g % SB;
-          ok = wait_bar(&fullA[sa], (g / SA) & 1, abort_flag, p.err) &&
-               wait_bar(&fullB[sb], (g / SB) & 1, abort_flag, p.err);
+          const int s = g % SA;
+          ok = wait_bar(&full[s], (g / SA) & 1, abort_flag, p.err);
           if (!ok) break;
           fence_after_sync();
-          const uint32_t b_addr = smem_u32(smem + c.b + (size_t)sb * BN * 128);
-          for (int m = 0; m < msub; ++m) {
-            const uint32_t a_addr = smem_u32(smem + c.a + ((size_t)sa * MT + m) * 16384);
-            const uint32_t d = tmem + (uint32_t)((ab * MT + m) * BN);
+          const uint32_t a_addr = smem_u32(smem + c.a + (size_t)s * 16384);
+          const uint32_t b_addr = smem_u32(smem + c.b + (size_t)s * BN * 128);
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              mma_bf16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc, (kt | kk) != 0);
-          }
-          mma_commit(&emptyA[sa]);
-          mma_commit(&emptyB[sb]);
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc, (kt | kk) != 0);
+          mma_commit(&empty[s]);
         }
         if (ok) mma_commit(&acc_full[ab]);
       }
     }
     __syncwarp();
   } else if (warp < kDeqWarp0) {
-    // ---- epilogue: warp (w % 4) reads TMEM lanes 32 (w % 4) .. + 31 of each 128-row sub-tile
+    // ---- epilogue: warp (w % 4) reads TMEM lanes 32 (w % 4) .. + 31 = tile rows
     const int q = warp & 3;
     int j = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++j) {
-      const GemmTile t = load_tile(p, it / nN, tile_rows);
+      const GemmTile t = load_tile(p, it / nN);
       const int nt = it % nN, ab = j & 1;
       if (!wait_bar(&acc_full[ab], (j >> 1) & 1, abort_flag, p.err)) break;
       fence_after_sync();
-      const int msub = t.mcount > 128 ? 2 : 1;
-      for (int m = 0; m < msub; ++m) {
-        const int r = m * 128 + q * 32 + lane;
-        const bool valid = r < t.mcount;
-        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((ab * MT + m) * BN);
-        int64_t orow = t.m0 + r;
-        float rs = 1.f;
-        if constexpr (EPI == EPI_SLOT) {
-          orow = valid ? (int64_t)__ldg(p.out_rows + min(t.m0 + r, p.list_len - 1)) : 0;
-          orow = min(max(orow, (int64_t)0), (int64_t)p.out_nrows - 1);
-          rs = valid ? __ldg(p.row_scale + orow) : 0.f;
-        } else {
-          orow = min(orow, (int64_t)p.out_nrows - 1);
-        }
-        if constexpr (EPI == EPI_SILU_TILE || EPI == EPI_SILU_ROUND) {
-          uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * (BN / 2);
+      const int r = q * 32 + lane;
+      const bool valid = r < t.mcount;
+      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+      int64_t orow = t.m0 + r;
+      float rs = 1.f;
+      if constexpr (EPI == EPI_SLOT) {
+        orow = valid ? (int64_t)__ldg(p.out_rows + min(t.m0 + r, p.list_len - 1)) : 0;
+        orow = min(max(orow, (int64_t)0), (int64_t)p.out_nrows - 1);
+        rs = valid ? __ldg(p.row_scale + orow) : 0.f;
+      } else {
+        orow = min(orow, (int64_t)p.out_nrows - 1);
+      }
+      if constexpr (EPI == EPI_SILU_TILE || EPI == EPI_SILU_ROUND) {
+        uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * (BN / 2);
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN / 2; c0 += 16) {
-            float gv[16], uv[16];
-            tmem_ld16(tb + c0, gv);
-            tmem_ld16(tb + BN / 2 + c0, uv);
-            if (valid) {
-              uint32_t o[8];
+        for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+          float gv[16], uv[16];
+          tmem_ld16(tb + c0, gv);
+          tmem_ld16(tb + BN / 2 + c0, uv);
+          if (valid) {
+            uint32_t o[8];
 #pragma unroll
-              for (int jj = 0; jj < 8; ++jj) {
-                float a0, a1;
-                if constexpr (EPI == EPI_SILU_TILE) {
-                  a0 = silu(gv[2 * jj]) * uv[2 * jj];
-                  a1 = silu(gv[2 * jj + 1]) * uv[2 * jj + 1];
-                } else {
-                  a0 = silu(bf2f(f2bf(gv[2 * jj]))) * bf2f(f2bf(uv[2 * jj]));
-                  a1 = silu(bf2f(f2bf(gv[2 * jj + 1]))) * bf2f(f2bf(uv[2 * jj + 1]));
-                }
-                o[jj] = (uint32_t)f2bf(a0) | ((uint32_t)f2bf(a1) << 16);
+            for (int jj = 0; jj < 8; ++jj) {
+              float a0, a1;
+              if constexpr (EPI == EPI_SILU_TILE) {
+                a0 = silu(gv[2 * jj]) * uv[2 * jj];
+                a1 = silu(gv[2 * jj + 1]) * uv[2 * jj + 1];
+              } else {
+                a0 = silu(bf2f(f2bf(gv[2 * jj]))) * bf2f(f2bf(uv[2 * jj]));
+                a1 = silu(bf2f(f2bf(gv[2 * jj + 1]))) * bf2f(f2bf(uv[2 * jj + 1]));
               }
-              reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-              reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+              o[jj] = (uint32_t)f2bf(a0) | ((uint32_t)f2bf(a1) << 16);
             }
+            reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
           }
-        } else if constexpr (EPI == EPI_BF16) {
-          uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * BN;
-          const int ncol = min(BN, p.n_valid - nt * BN);
+        }
+      } else if constexpr (EPI == EPI_BF16) {
+        uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * BN;
+        const int ncol = min(BN, p.n_valid - nt * BN);
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 16) {
-            float v[16];
-            tmem_ld16(tb + c0, v);
-            if (valid && c0 + 16 <= ncol) {
-              uint32_t o[8];
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(tb + c0, v);
+          if (valid && c0 + 16 <= ncol) {
+            uint32_t o[8];
 #pragma unroll
-              for (int jj = 0; jj < 8; ++jj) o[jj] = (uint32_t)f2bf(v[2 * jj]) | ((uint32_t)f2bf(v[2 * jj + 1]) << 16);
-              reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-              reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
-            } else if (valid) {
+            for (int jj = 0; jj < 8; ++jj) o[jj] = (uint32_t)f2bf(v[2 * jj]) | ((uint32_t)f2bf(v[2 * jj + 1]) << 16);
+            reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          } else if (valid) {
 #pragma unroll
-              for (int jj = 0; jj < 16; ++jj)
-                if (c0 + jj < ncol) out[c0 + jj] = f2bf(v[jj]);
-            }
+            for (int jj = 0; jj < 16; ++jj)
+              if (c0 + jj < ncol) out[c0 + jj] = f2bf(v[jj]);
           }
-        } else {  // EPI_F32, EPI_SLOT
-          float* out = static_cast<float*>(p.out) + orow * p.ldo + nt * BN;
-          const int ncol = min(BN, p.n_valid - nt * BN);
+        }
+      } else {  // EPI_F32, EPI_SLOT
+        float* out = static_cast<float*>(p.out) + orow * p.ldo + nt * BN;
+        const int ncol = min(BN, p.n_valid - nt * BN);
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 16) {
-            float v[16];
-            tmem_ld16(tb + c0, v);
-            if (valid && c0 + 16 <= ncol) {
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(tb + c0, v);
+          if (valid && c0 + 16 <= ncol) {
 #pragma unroll
-              for (int jj = 0; jj < 16; jj += 4)
-                *reinterpret_cast<float4*>(out + c0 + jj) =
-                    make_float4(v[jj] * rs, v[jj + 1] * rs, v[jj + 2] * rs, v[jj + 3] * rs);
-            } else if (valid) {
+            for (int jj = 0; jj < 16; jj += 4)
+              *reinterpret_cast<float4*>(out + c0 + jj) =
+                  make_float4(v[jj] * rs, v[jj + 1] * rs, v[jj + 2] * rs, v[jj + 3] * rs);
+          } else if (valid) {
 #pragma unroll
-              for (int jj = 0; jj < 16; ++jj)
-                if (c0 + jj < ncol) out[c0 + jj] = v[jj] * rs;
-            }
+            for (int jj = 0; jj < 16; ++jj)
+              if (c0 + jj < ncol) out[c0 + jj] = v[jj] * rs;
           }
         }
       }
@@ -517,41 +538,41 @@ __global__ void __launch_bounds__(kGThreads, 1)
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
   } else if constexpr (INT4) {
-    // ---- dequantization: thread td takes B row td / 2, K half td % 2 (32 nibbles) of every step
+    // ---- dequantization: job (row r, K half h) covers 32 nibbles of row r per step; thread td owns jobs
+    // td + kDeqThreads * j
+    constexpr int J = (BN * 2 + kDeqThreads - 1) / kDeqThreads;  // jobs per thread (2 at BN = 256)
     const int td = threadIdx.x - kDeqWarp0 * 32;
-    const bool active = td < BN * 2;
-    const int r = td >> 1, h = td & 1;
-    const Nib8Magic M = nib8_magic();
+    const int RB = 32 * c.rk;
     int g = 0, j = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
       const int sbuf = j & 1;
       if (!wait_bar(&sc_full[sbuf], (j >> 1) & 1, abort_flag, p.err)) break;
-      const uint8_t* scrow = smem + c.sc + (size_t)sbuf * BN * c.sstride + r * c.sstride;
-      const int RB = 32 * c.rk;
+      const uint8_t* scb = smem + c.sc + (size_t)sbuf * BN * c.sstride;
       for (int kt = 0; kt < nk; ++kt, ++g) {
-        const int gr = g / c.rk, sr = gr % SR, sb = g % SB, sub = g % c.rk, kx = kt;
-        ok = wait_bar(&fullR[sr], (gr / SR) & 1, abort_flag, p.err) &&
-             (g < SB || wait_bar(&emptyB[sb], ((g / SB) - 1) & 1, abort_flag, p.err));
+        const int gr = g / c.rk, sr = gr % SR, sub = g - gr * c.rk, s = g % SA;
+        ok = wait_bar(&fullR[sr], (gr / SR) & 1, abort_flag, p.err);
+        ok = ok && (g < SA || wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err));
         if (!ok) break;
-        if (active) {
-          const uint4 w =
-              *reinterpret_cast<const uint4*>(smem + c.raw + (size_t)sr * BN * RB + r * RB + sub * 32 + h * 16);
-          const float sv = h2f(*reinterpret_cast<const uint16_t*>(scrow + 2 * ((kx * kBK + h * 32) / p.G)));
-          const u64 s01 = pack2f(sv, sv * 0.0625f), s23 = pack2f(sv * (1.f / 256.f), sv * (1.f / 4096.f));
-          const u64 s45 = pack2f(sv * (1.f / 65536.f), sv * (1.f / 256.f));
-          const u64 s67 = pack2f(sv * (1.f / 4096.f), sv * (1.f / 65536.f));
-          uint8_t* bdst = smem + c.b + (size_t)sb * BN * 128;
+        const uint8_t* rawp = smem + c.raw + (size_t)sr * BN * RB + sub * 32;
+        uint8_t* bdst = smem + c.b + (size_t)s * BN * 128;
+#pragma unroll
+        for (int jj = 0; jj < J; ++jj) {
+          const int job = td + kDeqThreads * jj, r = job >> 1, h = job & 1;
+          if (job >= BN * 2) continue;
+          const uint4 w = *reinterpret_cast<const uint4*>(rawp + r * RB + h * 16);
+          const float sv = h2f(*reinterpret_cast<const uint16_t*>(scb + r * c.sstride + 2 * ((kt * kBK + h * 32) / p.G)));
+          const DqConst dc = dq_const(sv);
           const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq)
-            *reinterpret_cast<uint4*>(bdst + sw128_chunk(r, h * 4 + qq)) = dequant8_bf16(ww[qq], s01, s23, s45, s67, M);
+            *reinterpret_cast<uint4*>(bdst + sw128_chunk(r, h * 4 + qq)) = dequant8_bf16(ww[qq], dc);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
           if (sub == c.rk - 1) mbar_arrive(&freeR[sr]);  // the raw stage's last k-step
-          mbar_arrive(&fullB[sb]);
+          mbar_arrive(&full[s]);
         }
       }
       __syncwarp();
@@ -576,24 +597,37 @@ static int dev_attr(cudaDeviceAttr a, int fallback) {
   return v;
 }
 
-static bool pick_cfg(int bn, int mt, bool int4, int K, int G, GemmCfg* out) {
+static bool pick_cfg(int bn, bool int4, int K, int G, GemmCfg* out) {
   static int optin = 0;
   if (!optin) optin = dev_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin, 227 * 1024);
-  // deepest rings that fit: the raw INT4 ring first (its loads come from HBM), then A, then the bf16 B ring
-  const int sr_c[] = {4, 3, 2}, sa_c[] = {4, 3, 2}, sb_c[] = {4, 3, 2};
-  for (int sr : sr_c) {
-    for (int sa : sa_c)
-      for (int sb : sb_c) {
-        if (int4 && sb == 4) continue;
-        const GemmCfg c = gemm_cfg(bn, mt, int4, sa, sb, sr, K, G);
-        if ((int)c.total <= optin) {
+  // first fit in order of preference: 3+ A + B stages, then wide raw boxes, then raw ring depth
+  const int sa_c[] = {4, 3, 2}, rk_c[] = {4, 2, 1}, sr_c[] = {3, 2};
+  for (int sa : sa_c)
+    for (int rk : rk_c)
+      for (int sr : sr_c) {
+        const GemmCfg c = gemm_cfg(bn, int4, sa, sr, rk, K, G);
+        if ((int)c.total <= optin && (sa >= 3 || rk == 1)) {
           *out = c;
           return true;
         }
+        if (!int4) break;
       }
-    if (!int4) break;
-  }
   return false;
+}
+
+// 4D tensor map of a paired operand: [E][2][half_rows][inner], halves half_rows rows apart, experts e_rows apart.
+static bool make_map_pair(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t half_rows,
+                          uint64_t experts, uint64_t e_rows, uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows,
+                          bool swizzle128) {
+  memset(m, 0, sizeof *m);
+  const cuuint64_t dims[4] = {inner, half_rows, 2, experts};
+  const cuuint64_t strides[3] = {row_bytes, half_rows * row_bytes, (e_rows ? e_rows : 2 * half_rows) * row_bytes};
+  const cuuint32_t box[4] = {box_inner, box_rows, 2, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return cuTensorMapEncodeTiled(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // 2D tensor map over a row-major [outer][inner] array; rows are row_bytes apart. Out-of-range box elements read 0.
@@ -611,30 +645,39 @@ static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
 }
 
 template <int BN, bool INT4, int EPI>
-static cudaError_t launch_t(const GemmParams& p, int tile_rows, int max_tiles, bool pdl, cudaStream_t st) {
+static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaStream_t st) {
   GemmCfg c;
-  if (!pick_cfg(BN, tile_rows / 128, INT4, p.K, p.G, &c)) return cudaErrorInvalidValue;
+  if (!pick_cfg(BN, INT4, p.K, p.G, &c)) return cudaErrorInvalidValue;
   c.a_tma = p.a_rows ? 0 : 1;
   CUtensorMap tmA, tmB, tmS;
   memset(&tmA, 0, sizeof tmA);
+  memset(&tmB, 0, sizeof tmB);
   memset(&tmS, 0, sizeof tmS);
-  const int rows_box = p.paired ? BN / 2 : BN;
   if (c.a_tma && !make_map(&tmA, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.A, (uint64_t)p.K, (uint64_t)p.a_nrows,
-                           (uint64_t)p.lda * 2, kBK, 128, true))
+                           (uint64_t)p.lda * 2, kBK, kTileM, true))
     return cudaErrorInvalidValue;
+  const uint32_t rows_box = p.paired ? BN / 2 : BN;
+  const uint64_t hr = (uint64_t)p.pair_off, ne = (uint64_t)p.E, er = (uint64_t)p.b_rows_per_e;
   if (INT4) {
-    const uint64_t rows = (uint64_t)p.E * p.b_rows_per_e;
-    if (!make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.Bq, (uint64_t)p.K / 2, rows, (uint64_t)p.K / 2,
-                  (uint32_t)(32 * c.rk), rows_box, false))
-      return cudaErrorInvalidValue;
-    if (c.s_tma && !make_map(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.Bs, (uint64_t)c.ksc, rows, (uint64_t)c.sstride,
-                             c.ksc, rows_box, false))
-      return cudaErrorInvalidValue;
+    const uint64_t rows = ne * er;
+    const bool okb = p.paired ? make_map_pair(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.Bq, (uint64_t)p.K / 2, hr, ne, er,
+                                              (uint64_t)p.K / 2, (uint32_t)(32 * c.rk), rows_box, false)
+                              : make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.Bq, (uint64_t)p.K / 2, rows,
+                                         (uint64_t)p.K / 2, (uint32_t)(32 * c.rk), rows_box, false);
+    if (!okb) return cudaErrorInvalidValue;
+    if (c.s_tma) {
+      const bool oks = p.paired ? make_map_pair(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.Bs, (uint64_t)c.ksc, hr, ne, er,
+                                                (uint64_t)c.sstride, (uint32_t)c.ksc, rows_box, false)
+                                : make_map(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, p.Bs, (uint64_t)c.ksc, rows,
+                                           (uint64_t)c.sstride, (uint32_t)c.ksc, rows_box, false);
+      if (!oks) return cudaErrorInvalidValue;
+    }
   } else {
-    const uint64_t rows = p.paired ? (uint64_t)p.N : (uint64_t)p.n_valid;
-    if (!make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.Bh, (uint64_t)p.K, rows, (uint64_t)p.K * 2, kBK,
-                  rows_box, true))
-      return cudaErrorInvalidValue;
+    const bool okb = p.paired ? make_map_pair(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.Bh, (uint64_t)p.K, hr, 1, 0,
+                                              (uint64_t)p.K * 2, kBK, rows_box, true)
+                              : make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p.Bh, (uint64_t)p.K,
+                                         (uint64_t)p.n_valid, (uint64_t)p.K * 2, kBK, rows_box, true);
+    if (!okb) return cudaErrorInvalidValue;
   }
   static size_t granted = 0;
   if (c.total > granted) {
@@ -661,13 +704,13 @@ static cudaError_t launch_t(const GemmParams& p, int tile_rows, int max_tiles, b
 }
 
 template <int BN, bool INT4>
-static cudaError_t launch_epi(const GemmParams& p, int epi, int tile_rows, int max_tiles, bool pdl, cudaStream_t st) {
+static cudaError_t launch_epi(const GemmParams& p, int epi, int max_tiles, bool pdl, cudaStream_t st) {
   switch (epi) {
-    case EPI_F32: return launch_t<BN, INT4, EPI_F32>(p, tile_rows, max_tiles, pdl, st);
-    case EPI_BF16: return launch_t<BN, INT4, EPI_BF16>(p, tile_rows, max_tiles, pdl, st);
-    case EPI_SILU_TILE: return launch_t<BN, INT4, EPI_SILU_TILE>(p, tile_rows, max_tiles, pdl, st);
-    case EPI_SILU_ROUND: return launch_t<BN, INT4, EPI_SILU_ROUND>(p, tile_rows, max_tiles, pdl, st);
-    case EPI_SLOT: return launch_t<BN, INT4, EPI_SLOT>(p, tile_rows, max_tiles, pdl, st);
+    case EPI_F32: return launch_t<BN, INT4, EPI_F32>(p, max_tiles, pdl, st);
+    case EPI_BF16: return launch_t<BN, INT4, EPI_BF16>(p, max_tiles, pdl, st);
+    case EPI_SILU_TILE: return launch_t<BN, INT4, EPI_SILU_TILE>(p, max_tiles, pdl, st);
+    case EPI_SILU_ROUND: return launch_t<BN, INT4, EPI_SILU_ROUND>(p, max_tiles, pdl, st);
+    case EPI_SLOT: return launch_t<BN, INT4, EPI_SLOT>(p, max_tiles, pdl, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -675,7 +718,7 @@ static cudaError_t launch_epi(const GemmParams& p, int epi, int tile_rows, int m
 cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, int tile_rows, bool int4, int max_tiles, bool pdl,
                         cudaStream_t st) {
   if (p.K <= 0 || p.K % kBK || p.N <= 0 || p.N % bn || p.lda % 8 || p.ldo % 8 || !p.A || !p.out) return cudaErrorInvalidValue;
-  if (tile_rows != 128 && tile_rows != 256) return cudaErrorInvalidValue;
+  if (tile_rows != kTileM) return cudaErrorInvalidValue;
   if (p.n_valid <= 0 || p.n_valid > p.N || (p.paired && p.n_valid != p.N)) return cudaErrorInvalidValue;
   const void* ptrs[5] = {p.A, p.Bh, p.Bq, p.Bs, p.out};
   for (const void* q : ptrs)
@@ -694,11 +737,13 @@ cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, int tile_rows, boo
   }
   switch (bn) {
     case 64:
-      return int4 ? launch_epi<64, true>(p, epi, tile_rows, max_tiles, pdl, st)
-                  : launch_epi<64, false>(p, epi, tile_rows, max_tiles, pdl, st);
+      return int4 ? launch_epi<64, true>(p, epi, max_tiles, pdl, st) : launch_epi<64, false>(p, epi, max_tiles, pdl, st);
     case 128:
-      return int4 ? launch_epi<128, true>(p, epi, tile_rows, max_tiles, pdl, st)
-                  : launch_epi<128, false>(p, epi, tile_rows, max_tiles, pdl, st);
+      return int4 ? launch_epi<128, true>(p, epi, max_tiles, pdl, st)
+                  : launch_epi<128, false>(p, epi, max_tiles, pdl, st);
+    case 256:
+      return int4 ? launch_epi<256, true>(p, epi, max_tiles, pdl, st)
+                  : launch_epi<256, false>(p, epi, max_tiles, pdl, st);
     default: return cudaErrorInvalidValue;
   }
 }

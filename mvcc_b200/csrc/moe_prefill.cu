@@ -9,7 +9,7 @@
 //   topk        the reference's top-k rule per token (router_topk_kernel, kernels.cuh:774-809); marks bit p of
 //               expert e's bitmap for every pair p = t * TOPK + slot
 //   scan        per expert: popcounts and word prefixes of its bitmap; the last CTA turns the counts into the
-//               expert offsets and the grouped-GEMM tile list (kTileRows = 256 pairs per tile)
+//               expert offsets and the grouped-GEMM tile list (kTileRows = 128 pairs per tile)
 //   scatter     pair p of expert e goes to offsets[e] + (pairs of e before p): a stable counting sort by pair
 //               index, bit-exact and deterministic (moe_sort_kernel, kernels.cuh:906-923, orders ties arbitrarily)
 //   gate_up     grouped INT4 GEMM, A rows gathered per sorted pair, epilogue bf16(silu(g) * u) -> inter (sorted)
@@ -269,6 +269,11 @@ __global__ void __launch_bounds__(kPT) prefill_combine_kernel(const BlockArgs a,
 
 bool prefill_supported(const moe_layer_weights& w) { return w.E % 16 == 0; }
 
+// 256 B rows per tile: the most MMA work per pipeline step for the issuing thread's fixed barrier cost.
+static cudaError_t launch_wide(const GemmParams& p, int epi, bool int4, int max_tiles, cudaStream_t s) {
+  return launch_gemm(p, epi, 256, kTileRows, int4, max_tiles, false, s);
+}
+
 static GemmParams base_params(const BlockArgs& a) {
   GemmParams p;
   memset(&p, 0, sizeof p);
@@ -285,14 +290,14 @@ static cudaError_t run_router(const BlockArgs& a, cudaStream_t s) {
   p.a_nrows = a.T;
   p.Bh = a.w.router;
   p.b_rows_per_e = 0;
-  p.N = (a.w.E + 63) / 64 * 64;
+  p.N = (a.w.E + 127) / 128 * 128;
   p.n_valid = a.w.E;
   p.K = a.w.H;
   p.M = a.T;
   p.out = a.logits;
   p.ldo = a.w.E;
   p.out_nrows = a.T;
-  return launch_gemm(p, EPI_F32, 64, 128, false, (a.T + 127) / 128, false, s);
+  return launch_gemm(p, EPI_F32, 128, 128, false, (a.T + 127) / 128, false, s);
 }
 
 static cudaError_t run_sort(const BlockArgs& a, bool from_topk, cudaStream_t s) {
@@ -335,7 +340,7 @@ static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s) {
   g.out = a.inter;
   g.ldo = a.w.I;
   g.out_nrows = P;
-  cudaError_t e = launch_gemm(g, EPI_SILU_TILE, 128, kTileRows, true, a.max_tiles, false, s);
+  cudaError_t e = launch_wide(g, EPI_SILU_TILE, true, a.max_tiles, s);
   if (e != cudaSuccess) return e;
   // down: A = inter rows in sorted order, B = expert down rows; epilogue weights by w[pair] into slot[pair]
   GemmParams d = base_params(a);
@@ -357,7 +362,7 @@ static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s) {
   d.list_len = P;
   d.row_scale = a.wts;
   d.out_nrows = P;
-  return launch_gemm(d, EPI_SLOT, 128, kTileRows, true, a.max_tiles, false, s);
+  return launch_wide(d, EPI_SLOT, true, a.max_tiles, s);
 }
 
 cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s) {
@@ -375,7 +380,7 @@ cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s) {
   g.out = a.sinter;
   g.ldo = a.w.Is;
   g.out_nrows = a.T;
-  cudaError_t e = launch_gemm(g, EPI_SILU_ROUND, 128, 256, false, (a.T + 255) / 256, false, s);
+  cudaError_t e = launch_wide(g, EPI_SILU_ROUND, false, (a.T + 127) / 128, s);
   if (e != cudaSuccess) return e;
   GemmParams d = base_params(a);
   d.A = a.sinter;
@@ -389,7 +394,7 @@ cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s) {
   d.out = a.sout;
   d.ldo = a.w.H;
   d.out_nrows = a.T;
-  return launch_gemm(d, EPI_BF16, 128, 256, false, (a.T + 255) / 256, false, s);
+  return launch_wide(d, EPI_BF16, false, (a.T + 127) / 128, s);
 }
 
 static cudaError_t clear_bits(const BlockArgs& a, cudaStream_t s) {
