@@ -59,7 +59,7 @@ def build(verbose=False, force=False):
             if verbose and log:
                 sys.stderr.write(log)
     if todo or not os.path.exists(LIB):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -35,8 +35,10 @@
 // word itself, the word shifted left by 8 or shifted right by 12. One cvt.rn.bf16x2.f32 then rounds two values to
 // bf16: the reference's single rounding.
 #include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <mutex>
 #include <cstring>
 
 #include "moe_common.cuh"
@@ -615,16 +617,33 @@ static bool pick_cfg(int bn, bool int4, int K, int G, GemmCfg* out) {
   return false;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point: the library links no driver library, so it
+// loads on machines without a GPU driver (where only its host-side checks run).
+static PFN_cuTensorMapEncodeTiled encode_fn() {
+  static PFN_cuTensorMapEncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(f);
+  });
+  return fn;
+}
+
 // 4D tensor map of a paired operand: [E][2][half_rows][inner], halves half_rows rows apart, experts e_rows apart.
 static bool make_map_pair(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t half_rows,
                           uint64_t experts, uint64_t e_rows, uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows,
                           bool swizzle128) {
   memset(m, 0, sizeof *m);
+  const PFN_cuTensorMapEncodeTiled enc = encode_fn();
+  if (!enc) return false;
   const cuuint64_t dims[4] = {inner, half_rows, 2, experts};
   const cuuint64_t strides[3] = {row_bytes, half_rows * row_bytes, (e_rows ? e_rows : 2 * half_rows) * row_bytes};
   const cuuint32_t box[4] = {box_inner, box_rows, 2, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
-  return cuTensorMapEncodeTiled(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+  return enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
                                 CU_TENSOR_MAP_INTERLEAVE_NONE,
                                 swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -634,11 +653,13 @@ static bool make_map_pair(CUtensorMap* m, CUtensorMapDataType dt, const void* ba
 static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
                      uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
   memset(m, 0, sizeof *m);
+  const PFN_cuTensorMapEncodeTiled enc = encode_fn();
+  if (!enc) return false;
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  return cuTensorMapEncodeTiled(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                                 CU_TENSOR_MAP_INTERLEAVE_NONE,
                                 swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
