@@ -1,22 +1,31 @@
 #!/usr/bin/env python3
-"""bench.py -- throughput of the B200 MoE block on BASELINE config 2 (int4 MoE decode).
+"""bench.py -- throughput of the B200 MoE block on BASELINE configs 2 (int4 decode) and 4 (Zipf-skewed prefill).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference] [--quick]
 
-One step is one pass of the MoE block (qwen.cu:429-448: RMSNorm, router + top-8, routed int4 experts, shared
-expert, gated combine) over one decode batch of B tokens (default 1) for one layer, through the C ABI
-(libmoe_b200.so). Weights (H=2048, E=256, top-8, I=Is=512, INT4 group 64) are generated on the device from a
-seeded generator; each step uses the next of 32 distinct layer copies (13.7 GB), so no step reads weights a recent
-step left in the 126 MB L2 (no flush needed). Steps are captured in CUDA graphs and timed with CUDA events on the
-launching stream, bracketed by barrier + synchronize, max over ranks. Under torchrun (N > 1) every rank runs its
-own replica (the decode block does not shard; expert-parallel prefill is the multi-GPU path).
+Headline (`value`): one step is one pass of the MoE block (qwen.cu:429-448: residual RMSNorm,
+router + top-8, routed int4 experts, shared expert, gated combine) over one decode batch of B tokens (default 1)
+for one layer, through the C ABI (libmoe_b200.so). Weights (H=2048, E=256, top-8, I=Is=512, INT4 group 64, scales
+absmax/7 of N(0, 0.02) weights) come from a seeded device generator; step i uses layer copy i mod 32 (13.7 GB in
+all), so no step finds its weights in the 126 MB L2 (inputs larger than L2; no flush). Steps are captured in CUDA
+graphs and timed with CUDA events on the launching stream, bracketed by barrier + synchronize, max over ranks.
 
-`value`: tokens/s with weights and activations resident in HBM. `e2e`: the same steps with each step's input
-(hidden fp32, attn_out bf16) copied from pinned host memory and its outputs (hidden, normed) copied back inside
-the timed region. `roofline`: the dominant kernel (routed + shared gate/up), algorithmic bytes per launch over
-its mean duration from graph-captured events. `cpu_baseline`: the C oracle (test infrastructure) on the host
-cores, N=1 rank 0 only. `--impl reference` times the reference arm: the reference has no CPU implementation of
-the block, so it is the oracle's restatement of the reference kernels, with every host thread.
+Further objects on the same line:
+  roofline        the dominant kernel of the headline step (the fused decode kernel: the whole block is one launch
+                  for B < 8), algorithmic block bytes per launch over its mean duration from graph-captured events;
+  decode_batches  the other batch sizes of config 2 (1, 4, 16) on the default path selection;
+  prefill         BASELINE config 4: 4096 tokens through one layer with the per-expert Zipf(1.1) router bias:
+                  tok/s, the tensor-pipe roofline of its dominant kernel (the routed gate/up grouped GEMM) and of
+                  the whole block, its own e2e and clocks, and the C oracle on a bounded token sample;
+  e2e             the headline steps with each step's input (hidden fp32, attn_out bf16) copied from pinned host
+                  memory and its outputs (hidden, normed) copied back inside the timed region;
+  cpu_baseline    the C oracle (test infrastructure) of the decode block on the host cores, N=1 rank 0 only.
+Under torchrun (N > 1) every rank runs its own replica of these single-GPU workloads (`scaling` weak: the decode
+block does not shard).
+
+`--impl reference` times the reference arm: the reference implements the block only as GPU kernels
+(examples/qwen/kernels.cuh) and has no CPU code for it, so the arm is the oracle's restatement of those kernels on
+every host thread; under torchrun only rank 0 runs it.
 """
 import argparse
 import datetime
@@ -37,6 +46,11 @@ sys.path.insert(0, ROOT)
 METRIC = "int4 MoE decode tok/s + expert-GEMV HBM GB/s vs peak; EP prefill tok/s 1/2/4/8"
 LAYER_COPIES = 32
 GRAPH_STEPS = 256
+PREFILL_T = 4096
+PREFILL_COPIES = 2
+DTYPE = "int4/bf16 weights, bf16 activations, fp32 accumulate"
+DATA = ("synthetic (seeded device generator: bf16 N(0,0.02) weights, INT4 absmax/7 group-64 experts, "
+        "activations N(0,1))")
 
 
 def load_peaks():
@@ -44,8 +58,9 @@ def load_peaks():
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return {"hbm": float(d["hbm_gbs"]), "tf_burst": float(d["bf16_tflops"]),
+                "tf_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "kind": "measured"}
+    return {"hbm": 6650.0, "tf_burst": 1590.0, "tf_sustained": 1400.0, "kind": "fallback"}
 
 
 # ------------------------------------------------------------------ distributed plumbing
@@ -96,6 +111,7 @@ class ClockSampler:
             self.proc = None
             return
         threading.Thread(target=self._read, daemon=True).start()
+        time.sleep(0.3)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -133,25 +149,32 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(win), "window": where}
 
 
-# ------------------------------------------------------------------ B200 arm
+# ------------------------------------------------------------------ algorithmic work
 
-def algorithmic_bytes(shape, U, B):
-    """Bytes the block must move per step (the reference's decode_weight_bytes terms, qwen.cu:463-477):
-    router, U unique experts (gate/up + down weights and fp16 group scales), shared expert, norms, activations."""
-    s = shape
+def decode_bytes(s, U, B):
+    """Bytes the block must move per decode step (the reference's decode_weight_bytes terms, qwen.cu:463-477):
+    router, U unique experts (gate/up + down INT4 weights and fp16 group scales), shared expert, norm vectors,
+    activations (hidden fp32 + attn_out bf16 in, hidden fp32 + normed bf16 out)."""
     gu_exp = 2 * s.I * s.H // 2 + 2 * 2 * s.I * (s.H // s.G)
     dn_exp = s.H * s.I // 2 + 2 * s.H * (s.I // s.G)
-    shared_gu = 2 * s.Is * s.H * 2
-    shared_dn = s.H * s.Is * 2
-    act = B * s.H * (4 + 2) + B * s.H * (4 + 2)  # hidden + attn_out in, hidden + normed out
-    return {
-        "route": s.E * s.H * 2 + 2 * s.H * 2 + B * s.H * 6,
-        "gate_up": U * gu_exp + shared_gu,
-        "down": U * dn_exp + shared_dn + B * s.H * 4 * 2,
-        "experts": U * (gu_exp + dn_exp),
-        "block": s.E * s.H * 2 + U * (gu_exp + dn_exp) + shared_gu + shared_dn + 2 * s.H * 2 + act,
-    }
+    shared = 2 * s.Is * s.H * 2 + s.H * s.Is * 2
+    act = B * s.H * (4 + 2) * 2
+    return {"experts": U * (gu_exp + dn_exp),
+            "block": s.E * s.H * 2 + U * (gu_exp + dn_exp) + shared + 2 * s.H * 2 + act}
 
+
+def prefill_flops(s, T):
+    """Multiply-add FLOPs of the block for T tokens: router, TOPK routed experts (gate/up, down) and the shared
+    expert per token."""
+    router = 2 * T * s.H * s.E
+    gate_up = 2 * T * s.TOPK * s.H * 2 * s.I
+    down = 2 * T * s.TOPK * s.I * s.H
+    shared = 2 * T * s.H * 2 * s.Is + 2 * T * s.Is * s.H
+    return {"router": router, "gate_up": gate_up, "down": down, "shared": shared,
+            "block": router + gate_up + down + shared}
+
+
+# ------------------------------------------------------------------ graph timing helpers
 
 def capture(fn, steps, stream):
     g = torch.cuda.CUDAGraph()
@@ -161,57 +184,28 @@ def capture(fn, steps, stream):
     return g
 
 
-def run_graphs(graphs_counts, stream):
+def run_graphs(plan, stream):
     """Replays on `stream` (CUDAGraph.replay launches on the current stream)."""
     with torch.cuda.stream(stream):
-        for g, n in graphs_counts:
+        for g, n in plan:
             for _ in range(n):
                 g.replay()
 
 
-def b200_arm(args, rank, world, local):
-    import mvcc_b200 as m
-    dev = torch.device("cuda", local)
-    shape = m.MoeShape()
-    B = args.batch
-    K, W = args.steps, args.warmup
-    stream = torch.cuda.Stream(device=dev)
-    with torch.cuda.stream(stream):
-        layers = [m.synth_layer(shape, seed=1000 + 97 * rank + i, stream=stream) for i in range(LAYER_COPIES)]
-        blocks = [m.MoeBlock(l, B) for l in layers]
-        hidden, attn = m.synth_activations(shape, B, seed=7 + rank, stream=stream)
-        hidden0 = hidden.clone()
-        normed = torch.zeros(B, shape.H, dtype=torch.int16, device=dev)
-    torch.cuda.synchronize()
-
-    def step(i):
-        blocks[i % LAYER_COPIES].forward(hidden, attn, normed, stream=stream)
-
-    # warm-up: W eager steps
-    with torch.cuda.stream(stream):
-        for i in range(W):
-            step(i)
-    torch.cuda.synchronize()
-    # unique experts per step (B = 1: always TOPK), from the routing of one pass over the layer copies
-    uniq = []
-    for i in range(LAYER_COPIES):
-        step(i)
-        torch.cuda.synchronize()
-        uniq.append(len(np.unique(blocks[i].trace(B)["idx"].cpu().numpy())))
-    U = float(np.mean(uniq))
-    hidden.copy_(hidden0)
-
+def graph_plan(step, K, stream):
     S = min(K, GRAPH_STEPS)
-    g_main = capture(step, S, stream)
+    g = capture(step, S, stream)
     rem = K % S
-    g_rem = capture(step, rem, stream) if rem else None
-    plan = [(g_main, K // S)] + ([(g_rem, 1)] if g_rem else [])
-    run_graphs([(g_main, 1)], stream)  # graph upload, untimed
+    plan = [(g, K // S)] + ([(capture(step, rem, stream), 1)] if rem else [])
+    run_graphs([(g, 1)], stream)  # upload, untimed
     torch.cuda.synchronize()
+    return plan
 
-    clocks = ClockSampler(dev)
-    clocks.start()
-    time.sleep(0.3)
+
+def timed(plan, stream, world, clocks=None):
+    """Device time (ms) of the plan, barrier + synchronize on both sides, max over ranks; clocks sampled inside."""
+    if clocks is not None:
+        clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
@@ -222,60 +216,185 @@ def b200_arm(args, rank, world, local):
     torch.cuda.synchronize()
     t1 = time.time()
     barrier(world)
-    clocks.stop()
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
-    value = world * B * K / (ms / 1e3)
+    clk = None
+    if clocks is not None:
+        clocks.stop()
+        clk = clocks.summary(t0, t1)
+    return max_over_ranks(e0.elapsed_time(e1), world), clk
 
-    # per-kernel durations from graph-captured events over the same steps
+
+def stage_times(m, fwd_events, S, reps, stream):
+    """Mean per-stage durations (us) over S graph-captured steps replayed `reps` times: the four events the library
+    records around one block (start, after routing, after gate/up, end)."""
     evs = [[m.Event() for _ in range(4)] for _ in range(S)]
-    g_ev = capture(lambda i: blocks[i % LAYER_COPIES].forward_events(hidden, attn, normed, evs[i], stream=stream),
-                   S, stream)
-    run_graphs([(g_ev, 1)], stream)
+    g = capture(lambda i: fwd_events(i, evs[i]), S, stream)
+    run_graphs([(g, 1)], stream)
     torch.cuda.synchronize()
-    reps = max(1, min(K // S, 8))
     acc = np.zeros(3)
     for _ in range(reps):
-        run_graphs([(g_ev, 1)], stream)
+        run_graphs([(g, 1)], stream)
         torch.cuda.synchronize()
         for e in evs:
             acc += [e[0].elapsed_ms(e[1]), e[1].elapsed_ms(e[2]), e[2].elapsed_ms(e[3])]
-    stage_us = acc * 1e3 / (reps * S)
+    return acc * 1e3 / (reps * S)
 
-    # e2e: host-resident inputs and outputs copied inside the timed region
-    h_in = hidden0.cpu().pin_memory()
+
+def e2e_time(block_at, hidden, attn, normed, K, stream, world):
+    """The same steps fed from pinned host memory: H2D of hidden + attn_out and D2H of hidden + normed per step
+    inside the timed region."""
+    h_in = hidden.cpu().pin_memory()
     a_in = attn.cpu().pin_memory()
     h_out = torch.empty_like(h_in).pin_memory()
     n_out = torch.empty(normed.shape, dtype=normed.dtype).pin_memory()
 
-    def e2e_step(i):
+    def step(i):
         hidden.copy_(h_in, non_blocking=True)
         attn.copy_(a_in, non_blocking=True)
-        blocks[i % LAYER_COPIES].forward(hidden, attn, normed, stream=stream)
+        block_at(i).forward(hidden, attn, normed, stream=stream)
         h_out.copy_(hidden, non_blocking=True)
         n_out.copy_(normed, non_blocking=True)
 
-    ge = capture(e2e_step, S, stream)
-    ge_rem = capture(e2e_step, rem, stream) if rem else None
-    plan_e = [(ge, K // S)] + ([(ge_rem, 1)] if ge_rem else [])
-    run_graphs([(ge, 1)], stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
-    e0.record(stream)
-    run_graphs(plan_e, stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    ms_e2e = max_over_ranks(e0.elapsed_time(e1), world)
+    ms, _ = timed(graph_plan(step, K, stream), stream, world)
+    return ms, h_in.numel() * 4 + a_in.numel() * 2, h_out.numel() * 4 + n_out.numel() * 2
 
-    peak, peak_kind = load_peaks()
-    ab = algorithmic_bytes(shape, U, B)
-    gu_gbs = ab["gate_up"] / (stage_us[1] * 1e-6) / 1e9
-    exp_gbs = (ab["gate_up"] + ab["down"]) / ((stage_us[1] + stage_us[2]) * 1e-6) / 1e9
-    blk_gbs = ab["block"] / (ms / K * 1e-3) / 1e9
+
+def launches_per_step(T, fused_max=7, prefill_min=8, chunk=16):
+    """Kernels of this library one block launches: the fused decode kernel (T < 8), three per decode chunk, or the
+    prefill sequence (norm, router GEMM, top-k, sort scan, sort scatter, gate/up GEMM, down GEMM, two shared-expert
+    GEMMs, combine)."""
+    if T >= prefill_min:
+        return 10
+    if T <= fused_max:
+        return 1
+    return 3 * ((T + chunk - 1) // chunk)
+
+
+# ------------------------------------------------------------------ B200 arm
+
+def decode_case(m, shape, blocks, B, K, W, stream, world, dev, clocks=None):
+    hidden, attn = m.synth_activations(shape, B, seed=7, stream=stream)
+    normed = torch.zeros(B, shape.H, dtype=torch.int16, device=dev)
+    torch.cuda.synchronize()
+    blk = [m.MoeBlock(b.layer, B) for b in blocks] if blocks[0].max_T < B else blocks
+    step = lambda i: blk[i % len(blk)].forward(hidden, attn, normed, stream=stream)  # noqa: E731
+    with torch.cuda.stream(stream):
+        for i in range(W):
+            step(i)
+    torch.cuda.synchronize()
+    uniq = []
+    for i in range(len(blk)):
+        step(i)
+        torch.cuda.synchronize()
+        uniq.append(len(np.unique(blk[i].trace(B)["idx"].cpu().numpy())))
+    U = float(np.mean(uniq))
+    hidden0 = hidden.clone()
+    ms, clk = timed(graph_plan(step, K, stream), stream, world, clocks)
+    S = min(K, GRAPH_STEPS)
+    st = stage_times(m, lambda i, ev: blk[i % len(blk)].forward_events(hidden, attn, normed, ev, stream=stream),
+                     S, max(1, min(K // S, 8)), stream)
+    hidden.copy_(hidden0)
+    ms_e2e, hb, db = e2e_time(lambda i: blk[i % len(blk)], hidden, attn, normed, K, stream, world)
+    return {"ms": ms, "U": U, "stage_us": st, "clocks": clk, "ms_e2e": ms_e2e, "h2d": hb, "d2h": db}
+
+
+def prefill_case(m, shape, K, W, stream, world, dev, peaks, cpu_seconds, do_cpu):
+    T = PREFILL_T
+    bias = torch.from_numpy(m.zipf_bias(shape.E, seed=0)).to(dev)
+    layers = []
+    for c in range(PREFILL_COPIES):
+        base = m.synth_layer(shape, seed=2000 + c, stream=stream)
+        t = dict(base.t)
+        t["router_bias"] = bias
+        layers.append(m.MoeLayer(shape, t))
+    blocks = [m.MoeBlock(l, T) for l in layers]
+    hidden, attn = m.synth_activations(shape, T, seed=17, stream=stream)
+    normed = torch.zeros(T, shape.H, dtype=torch.int16, device=dev)
+    torch.cuda.synchronize()
+    hidden0 = hidden.clone()
+    step = lambda i: blocks[i % PREFILL_COPIES].forward(hidden, attn, normed, stream=stream)  # noqa: E731
+    with torch.cuda.stream(stream):
+        for i in range(W):
+            step(i)
+    torch.cuda.synchronize()
+    tr = blocks[(W - 1) % PREFILL_COPIES].trace(T)
+    idx = tr["idx"].cpu().numpy()
+    load = np.bincount(idx.ravel(), minlength=shape.E)
+    err = blocks[0].error_word() | blocks[1 % PREFILL_COPIES].error_word()
+    ms, clk = timed(graph_plan(step, K, stream), stream, world, ClockSampler(dev))
+    st = stage_times(m, lambda i, ev: blocks[i % PREFILL_COPIES].forward_events(hidden, attn, normed, ev,
+                                                                                  stream=stream),
+                     min(K, 16), 2, stream)
+    hidden.copy_(hidden0)
+    ms_e2e, hb, db = e2e_time(lambda i: blocks[i % PREFILL_COPIES], hidden, attn, normed, K, stream, world)
+    fl = prefill_flops(shape, T)
+    step_us = ms / K * 1e3
+    gu_tf = fl["gate_up"] / (st[1] * 1e-6) / 1e12
+    blk_tf = fl["block"] / (step_us * 1e-6) / 1e12
+    out = {
+        "workload": f"BASELINE config 4: prefill of {T} tokens through one int4 G=64 MoE layer, router logits + "
+                    f"per-expert Zipf(1.1) bias b_e = -1.1 ln(1 + pi(e)), pi a seed-0 permutation",
+        "tokens": T, "value": world * T * K / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / K, "steps": K,
+        "layer_copies": PREFILL_COPIES,
+        "l2": f"inputs larger than L2: steps alternate over {PREFILL_COPIES} layer copies (428 MB of weights each); "
+              "no flush",
+        "expert_load": {"max_pairs": int(load.max()), "mean_pairs": float(load.mean()),
+                        "top8_share": float(np.sort(load)[::-1][:8].sum() / load.sum()),
+                        "experts_used": int((load > 0).sum())},
+        "stages_us": {"route_sort": st[0], "gate_up_gemm": st[1], "down_shared_combine": st[2]},
+        "roofline": {"kernel": "moe_gemm_kernel<256, INT4, EPI_SILU_TILE> (routed gate/up grouped GEMM + SiLU)",
+                     "bound": "tensor", "achieved": gu_tf, "peak": peaks["tf_sustained"], "unit": "TFLOP/s",
+                     "frac": gu_tf / peaks["tf_sustained"],
+                     "peak_kind": f"{peaks['kind']} bf16 sustained",
+                     "flops_per_launch": fl["gate_up"], "us_per_launch": st[1], "traffic": None},
+        "block_tflops": {"achieved": blk_tf, "frac": blk_tf / peaks["tf_sustained"], "flops_per_step": fl["block"]},
+        "e2e": {"value": world * T * K / (ms_e2e / 1e3), "unit": "tok/s", "h2d_bytes_per_step": hb,
+                "d2h_bytes_per_step": db},
+        "gpu_launches": launches_per_step(T) * K,
+        "error_word": err,
+        "clocks": clk,
+    }
+    if do_cpu:
+        out["cpu_baseline"] = cpu_prefill(layers[0], shape, bias.cpu().numpy(), cpu_seconds)
+    return out
+
+
+def b200_arm(args, rank, world, local):
+    import mvcc_b200 as m
+    dev = torch.device("cuda", local)
+    shape = m.MoeShape()
+    B = args.batch
+    K, W = args.steps, args.warmup
+    peaks = load_peaks()
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        layers = [m.synth_layer(shape, seed=1000 + 97 * rank + i, stream=stream) for i in range(args.layer_copies)]
+    blocks = [m.MoeBlock(l, max(B, 16)) for l in layers]
+    torch.cuda.synchronize()
+
+    head = decode_case(m, shape, blocks, B, K, W, stream, world, dev, ClockSampler(dev))
+    ms = head["ms"]
+    st = head["stage_us"]
+    ab = decode_bytes(shape, head["U"], B)
+    step_us = ms / K * 1e3
+    fused = B < 8
+    if fused:
+        achieved = ab["block"] / (st[0] * 1e-6) / 1e9
+        roof = {"kernel": "moe_fused_decode_kernel (the whole block in one cooperative launch)",
+                "bound": "hbm", "achieved": achieved, "peak": peaks["hbm"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm"], "peak_kind": peaks["kind"], "bytes_per_launch": ab["block"],
+                "us_per_launch": st[0], "traffic": None}
+    else:
+        fl = prefill_flops(shape, B)
+        achieved = fl["gate_up"] / (st[1] * 1e-6) / 1e12
+        roof = {"kernel": "moe_gemm_kernel (routed gate/up grouped GEMM)", "bound": "tensor", "achieved": achieved,
+                "peak": peaks["tf_sustained"], "unit": "TFLOP/s", "frac": achieved / peaks["tf_sustained"],
+                "peak_kind": peaks["kind"], "flops_per_launch": fl["gate_up"], "us_per_launch": st[1],
+                "traffic": None}
+    exp_gbs = ab["experts"] / (step_us * 1e-6) / 1e9
+    blk_gbs = ab["block"] / (step_us * 1e-6) / 1e9
     result = {
         "metric": METRIC,
-        "value": value,
+        "value": world * B * K / (ms / 1e3),
         "unit": "tok/s",
         "n_gpus": world,
         "steps": K,
@@ -284,56 +403,87 @@ def b200_arm(args, rank, world, local):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "fp32",
-        "data": "synthetic (seeded device generator; bf16 N(0,0.02) weights, INT4 absmax/7 group-64 experts)",
+        "dtype": DTYPE,
+        "data": DATA,
         "config": {
             "workload": f"BASELINE config 2: one MoE layer, int4 G=64 experts, decode batch {B}",
             "H": shape.H, "E": shape.E, "topk": shape.TOPK, "I": shape.I, "Is": shape.Is, "G": shape.G,
-            "batch": B, "layer_copies": LAYER_COPIES,
-            "l2": f"inputs larger than L2: consecutive steps cycle over {LAYER_COPIES} layer copies "
-                  f"({LAYER_COPIES * 428 / 1000:.1f} GB of weights); no flush",
-            "parallelism": "replicas" if world > 1 else "single",
-            "graph_steps": S,
+            "batch": B, "layer_copies": args.layer_copies,
+            "l2": f"inputs larger than L2: consecutive steps cycle over {args.layer_copies} layer copies "
+                  f"({args.layer_copies * 0.428:.1f} GB of weights); no flush",
+            "parallelism": f"replicas x{world}" if world > 1 else "single",
+            "graph_steps": min(K, GRAPH_STEPS),
         },
-        "roofline": {
-            "kernel": "gate_up_kernel (routed int4 gate/up + SiLU for the unique experts, shared gate/up)",
-            "bound": "hbm", "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
-            "peak_kind": peak_kind, "bytes_per_launch": ab["gate_up"], "us_per_launch": stage_us[1],
-            "traffic": None,
-        },
-        "expert_gemv": {"bytes_per_step": ab["gate_up"] + ab["down"], "us": stage_us[1] + stage_us[2],
-                        "gbs": exp_gbs, "frac": exp_gbs / peak, "unique_experts": U},
-        "block": {"bytes_per_step": ab["block"], "gbs": blk_gbs, "frac": blk_gbs / peak},
-        "kernels_us": {"route": stage_us[0], "gate_up": stage_us[1], "down_combine": stage_us[2]},
-        "e2e": {"value": world * B * K / (ms_e2e / 1e3), "unit": "tok/s",
-                "h2d_bytes_per_step": B * shape.H * (4 + 2), "d2h_bytes_per_step": B * shape.H * (4 + 2)},
-        "gpu_launches": 3 * K,
-        "clocks": clocks.summary(t0, t1),
+        "roofline": roof,
+        "expert_gemv": {"bytes_per_step": ab["experts"], "unique_experts": head["U"], "gbs_over_step": exp_gbs,
+                        "frac_over_step": exp_gbs / peaks["hbm"],
+                        "note": "expert weight + scale bytes over the whole step time (router, shared expert and "
+                                "norms included in the time)"},
+        "block": {"bytes_per_step": ab["block"], "gbs": blk_gbs, "frac": blk_gbs / peaks["hbm"], "us": step_us},
+        "kernels_us": {"fused_block": st[0]} if fused else
+                      {"route": st[0], "gate_up": st[1], "down_combine": st[2]},
+        "e2e": {"value": world * B * K / (head["ms_e2e"] / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"]},
+        "gpu_launches": launches_per_step(B) * K,
+        "clocks": head["clocks"],
     }
+    if not args.quick:
+        extra = {}
+        for b in (1, 4, 16):
+            if b == B:
+                continue
+            kb = min(K, 4096)
+            r = decode_case(m, shape, blocks, b, kb, W, stream, world, dev)
+            u = r["ms"] / kb * 1e3
+            bb = decode_bytes(shape, r["U"], b)
+            extra[str(b)] = {"tok_s": world * b * kb / (r["ms"] / 1e3), "us_per_step": u, "steps": kb,
+                             "unique_experts": r["U"], "block_gbs": bb["block"] / (u * 1e-6) / 1e9,
+                             "block_frac": bb["block"] / (u * 1e-6) / 1e9 / peaks["hbm"],
+                             "path": "fused decode kernel" if b < 8 else "prefill (tile GEMMs)",
+                             "stages_us": list(r["stage_us"]),
+                             "e2e_tok_s": world * b * kb / (r["ms_e2e"] / 1e3)}
+        result["decode_batches"] = extra
+    del blocks, layers
+    torch.cuda.empty_cache()
+    if not args.no_prefill:
+        do_cpu = world == 1 and rank == 0 and not args.no_cpu
+        result["prefill"] = prefill_case(m, shape, args.prefill_steps, W, stream, world, dev, peaks,
+                                         args.cpu_seconds / 2, do_cpu)
     if world == 1 and rank == 0 and not args.no_cpu:
-        result["cpu_baseline"] = cpu_baseline(layers[0], shape, B, args.cpu_seconds)
+        with torch.cuda.stream(stream):
+            l0 = m.synth_layer(shape, seed=1000, stream=stream)
+        torch.cuda.synchronize()
+        result["cpu_baseline"] = cpu_baseline(l0, shape, B, args.cpu_seconds)
     return result
 
 
 # ------------------------------------------------------------------ CPU oracle (baseline / reference arm)
 
 def host_layer(layer):
-    return {n: (v.cpu().numpy() if v.dtype == torch.uint8 else v.cpu().numpy().view(np.uint16))
-            for n, v in layer.t.items()}
+    out = {}
+    for n, v in layer.t.items():
+        a = v.cpu().numpy()
+        out[n] = a.view(np.uint16) if v.dtype == torch.int16 else a
+    return out
 
 
-def time_oracle(L, shape, B, seconds, max_steps=None):
+def oracle_shape(shape):
+    from oracle import oracle as O
+    return O.Shape(H=shape.H, E=shape.E, TOPK=shape.TOPK, I=shape.I, Is=shape.Is, G=shape.G, eps=shape.eps)
+
+
+def time_oracle(L, shape, B, seconds, mode=0, max_steps=None):
     from oracle import oracle as O
     orc = O.Oracle()
     n = orc.max_threads()
     orc.set_threads(n)
-    s = O.Shape(H=shape.H, E=shape.E, TOPK=shape.TOPK, I=shape.I, Is=shape.Is, G=shape.G, eps=shape.eps)
+    s = oracle_shape(shape)
     hidden, attn = O.make_activations(s, B, 3)
-    orc.block_forward(s, L, hidden, attn, mode=0)  # warm
+    orc.block_forward(s, L, hidden, attn, mode=mode)  # warm
     steps = 0
     t0 = time.perf_counter()
     while True:
-        orc.block_forward(s, L, hidden, attn, mode=0)
+        orc.block_forward(s, L, hidden, attn, mode=mode)
         steps += 1
         el = time.perf_counter() - t0
         if el >= seconds or (max_steps and steps >= max_steps):
@@ -349,6 +499,15 @@ def cpu_baseline(layer, shape, B, seconds):
                       f"layer, {el:.1f} s, {n} threads ({os.cpu_count()} logical CPUs)"}
 
 
+def cpu_prefill(layer, shape, bias, seconds, tokens=64):
+    L = host_layer(layer)
+    L["router_bias"] = bias
+    steps, el, n = time_oracle(L, shape, tokens, seconds, mode=1)
+    return {"value": steps * tokens / el, "unit": "tok/s", "cores": n, "kind": "port",
+            "sample": f"{steps} calls of {tokens} tokens through the C oracle of the block (tile numerics, Zipf "
+                      f"bias) on one layer, {el:.1f} s, {n} threads ({os.cpu_count()} logical CPUs)"}
+
+
 def reference_arm(args, rank, world, local):
     if rank != 0:
         return None
@@ -362,7 +521,7 @@ def reference_arm(args, rank, world, local):
     from oracle import oracle as O
     orc = O.Oracle()
     orc.set_threads(orc.max_threads())
-    s = O.Shape()
+    s = oracle_shape(shape)
     hidden, attn = O.make_activations(s, B, 3)
     for _ in range(min(args.warmup, 3)):
         orc.block_forward(s, L, hidden, attn, mode=0)
@@ -373,13 +532,13 @@ def reference_arm(args, rank, world, local):
     return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": el / steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": DTYPE, "data": DATA,
         "config": {"workload": f"BASELINE config 2: one MoE layer, int4 G=64 experts, decode batch {B}",
                    "H": shape.H, "E": shape.E, "topk": shape.TOPK, "I": shape.I, "Is": shape.Is, "G": shape.G,
                    "batch": B},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": n, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference implements the block only as CUDA kernels (examples/qwen/kernels.cuh); its CPU "
+        "note": "the reference implements the block only as GPU kernels (examples/qwen/kernels.cuh); its CPU "
                 "arm is the oracle's scalar restatement of those kernels",
     }
 
@@ -391,9 +550,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--layer-copies", type=int, default=LAYER_COPIES,
+                    help="decode layer copies cycled over (each 428 MB; the default keeps steps out of L2)")
+    ap.add_argument("--prefill-steps", type=int, default=40)
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
+    ap.add_argument("--quick", action="store_true", help="headline batch only (no decode_batches sweep)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

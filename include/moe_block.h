@@ -46,6 +46,10 @@ typedef struct moe_layer_weights {
   const uint16_t* shared_gate;    /* bf16 [H]           L{i}.shared.gate */
   int32_t H, E, TOPK, I, Is, G;
   float eps;
+  /* Optional (NULL = none): fp32 [E] added to the router logits as they are produced, before the top-k, so the
+   * logits, indices and weights all carry it. No reference counterpart: it expresses the skewed expert load of
+   * the prefill benchmark (router logits plus a per-expert Zipf bias). */
+  const float* router_bias;
 } moe_layer_weights;
 
 /* Shapes the kernels accept: H % 256 == 0 and H <= 4096, I % 128 == 0 and I <= 2048, Is % 128 == 0 and
@@ -80,9 +84,11 @@ MOE_API int moe_block_forward(const moe_layer_weights* w, void* workspace, size_
                       const uint16_t* attn_out, uint16_t* normed, const uint16_t* next_rms1, int T,
                       moe_stream_t stream);
 
-/* moe_block_forward that also records events[0..3] (cudaEvent_t) on `stream` before the first launch and after
- * each of its three kernels (routing, gate/up, down + combine); inside stream capture the records become graph
- * nodes. Profiling hook with no reference counterpart (the reference times whole launches, qwen.cu:486-498). */
+/* moe_block_forward that also records events[0..3] (cudaEvent_t) on `stream`: events[0] before the first launch,
+ * events[1] after the routing stage (norm, router, top-k; on the prefill path also the expert sort), events[2] after
+ * the routed gate/up launch, events[3] at the end (down, shared expert, combine). The fused decode kernel (T < 8) is
+ * one launch: events[1..3] all follow it. Inside stream capture the records become graph nodes. Profiling hook with
+ * no reference counterpart (the reference times whole launches, qwen.cu:486-498). */
 MOE_API int moe_block_forward_events(const moe_layer_weights* w, void* workspace, size_t workspace_bytes,
                                      float* hidden, const uint16_t* attn_out, uint16_t* normed,
                                      const uint16_t* next_rms1, int T, void* const* events, moe_stream_t stream);

@@ -41,6 +41,7 @@ class MoeLayerWeights(ctypes.Structure):
         ("Is", ctypes.c_int32),
         ("G", ctypes.c_int32),
         ("eps", ctypes.c_float),
+        ("router_bias", ctypes.c_void_p),
     ]
 
 
@@ -164,8 +165,13 @@ class MoeLayer:
             v = self.t[n]
             if tuple(v.shape) != shp or v.dtype != dt or not v.is_contiguous() or not v.is_cuda:
                 raise ValueError(f"{n}: expected contiguous cuda {dt} {shp}, got {v.dtype} {tuple(v.shape)}")
+        bias = self.t.get("router_bias")
+        if bias is not None and (tuple(bias.shape) != (s.E,) or bias.dtype != torch.float32 or not bias.is_cuda
+                                 or not bias.is_contiguous()):
+            raise ValueError(f"router_bias: expected contiguous cuda float32 ({s.E},)")
         self.c = MoeLayerWeights(*[ctypes.c_void_p(self.t[n].data_ptr()) for n in self.NAMES],
-                                 s.H, s.E, s.TOPK, s.I, s.Is, s.G, s.eps)
+                                 s.H, s.E, s.TOPK, s.I, s.Is, s.G, s.eps,
+                                 None if bias is None else ctypes.c_void_p(bias.data_ptr()))
         _check(_lib.moe_check_shape(ctypes.byref(self.c)), "moe_check_shape")
 
 
@@ -288,6 +294,14 @@ def synth_layer(shape: MoeShape, seed: int, device="cuda", std=0.02, stream=None
     _check(_lib.moe_synth_int4_rows(_ptr(t["exp_dn_q"]), _ptr(t["exp_dn_s"]), s.E * s.H, s.I, s.G, seed, 7, std, st),
            "moe_synth_int4_rows")
     return MoeLayer(shape, t)
+
+
+def zipf_bias(E: int, seed: int = 0, s: float = 1.1):
+    """Per-expert router bias b_e = -s * ln(1 + pi(e)), pi a seeded permutation of 0..E-1: the Zipf(s) expert-load
+    skew of the prefill benchmark (fp32 numpy array, host)."""
+    import numpy as np
+    perm = np.random.default_rng(seed).permutation(E)
+    return (-s * np.log1p(perm.astype(np.float64))).astype(np.float32)
 
 
 def synth_activations(shape: MoeShape, T: int, seed: int, device="cuda", stream=None):

@@ -133,17 +133,6 @@ int moe_workspace_error(void* workspace, size_t workspace_bytes, moe_stream_t st
 }
 
 namespace {
-// Records `ev` on `s`; inside stream capture the record becomes a graph node that timestamps every replay.
-cudaError_t record_event(void* ev, cudaStream_t s) {
-  if (!ev) return cudaSuccess;
-  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
-  cudaError_t e = cudaStreamIsCapturing(s, &st);
-  if (e != cudaSuccess) return e;
-  if (st == cudaStreamCaptureStatusActive)
-    return cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev), s, cudaEventRecordExternal);
-  return cudaEventRecord(static_cast<cudaEvent_t>(ev), s);
-}
-
 // The fused single-launch decode kernel serves T <= kFusedMaxT unless the environment sets MOE_B200_FUSED=0
 // (read once per process), which selects the three-kernel path.
 bool fused_enabled() {
@@ -168,8 +157,7 @@ int block_forward_impl(const moe_layer_weights* w, void* workspace, size_t works
     a.normed = normed;
     a.next_rms1 = next_rms1;
     cudaError_t e = events ? record_event(events[0], s) : cudaSuccess;
-    if (e == cudaSuccess) e = prefill_block(a, s);
-    for (int k = 1; k < 4 && events && e == cudaSuccess; ++k) e = record_event(events[k], s);
+    if (e == cudaSuccess) e = prefill_block(a, s, events);
     return (int)e;
   }
   int fs = 0, frows = 0;

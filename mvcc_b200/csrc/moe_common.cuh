@@ -148,6 +148,18 @@ constexpr int kPrefillMinT = 8;
 constexpr int kTileRows = 128;
 __host__ __device__ inline int prefill_max_tiles(int P, int E) { return P / kTileRows + (E < P ? E : P) + 1; }
 
+// Records the cudaEvent_t `ev` (nullable) on `s`; inside stream capture the record becomes a graph node that
+// timestamps every replay.
+inline cudaError_t record_event(void* ev, cudaStream_t s) {
+  if (!ev) return cudaSuccess;
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(s, &st);
+  if (e != cudaSuccess) return e;
+  if (st == cudaStreamCaptureStatusActive)
+    return cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev), s, cudaEventRecordExternal);
+  return cudaEventRecord(static_cast<cudaEvent_t>(ev), s);
+}
+
 __host__ __device__ inline size_t ws_align(size_t x) { return (x + 255) & ~(size_t)255; }
 
 __host__ __device__ inline WsLayout ws_layout(int H, int E, int TOPK, int I, int Is, int maxT) {

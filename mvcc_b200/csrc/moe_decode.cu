@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(256) route_kernel(BlockArgs a, int flags) {
       }
       acc = warp_sum(acc);
       if (lane == 0) {
-        if (e < E) a.logits[(int64_t)t * E + e] = acc;
+        if (e < E) a.logits[(int64_t)t * E + e] = a.w.router_bias ? acc + a.w.router_bias[e] : acc;
         else a.gate[t] = sigmoid(acc);
       }
     }

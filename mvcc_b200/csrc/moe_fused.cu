@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
         }
         acc = warp_sum(acc);
         if (lane == 0) {
-          if (row < E) a.logits[(int64_t)t * E + row] = acc;
+          if (row < E) a.logits[(int64_t)t * E + row] = a.w.router_bias ? acc + a.w.router_bias[row] : acc;
           else a.gate[t] = sigmoid(acc);
         }
       }

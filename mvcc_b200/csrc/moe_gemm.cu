@@ -523,6 +523,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           tmem_ld16(tb + c0, v);
+          if constexpr (EPI == EPI_F32) {
+            if (p.col_bias) {  // fp32 add after the dot product (the router's per-expert bias)
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                v[jj] += (c0 + jj < ncol) ? __ldg(p.col_bias + nt * BN + c0 + jj) : 0.f;
+            }
+          }
           if (valid && c0 + 16 <= ncol) {
 #pragma unroll
             for (int jj = 0; jj < 16; jj += 4)

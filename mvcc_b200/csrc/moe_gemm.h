@@ -49,6 +49,7 @@ struct GemmParams {
   int64_t ldo;               // elements
   const int32_t* out_rows;   // EPI_SLOT: out row = out_rows[m0 + r]
   const float* row_scale;    // EPI_SLOT: scale = row_scale[out row]
+  const float* col_bias;     // EPI_F32 (nullable): out = acc + col_bias[column]
   int out_nrows;             // bound of out rows (clamp)
   uint32_t* err;             // error word (bounded waits)
 };

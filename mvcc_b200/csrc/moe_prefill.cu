@@ -295,6 +295,7 @@ static cudaError_t run_router(const BlockArgs& a, cudaStream_t s) {
   p.K = a.w.H;
   p.M = a.T;
   p.out = a.logits;
+  p.col_bias = a.w.router_bias;
   p.ldo = a.w.E;
   p.out_nrows = a.T;
   return launch_gemm(p, EPI_F32, 128, 128, false, (a.T + 127) / 128, false, s);
@@ -315,7 +316,7 @@ static cudaError_t run_sort(const BlockArgs& a, bool from_topk, cudaStream_t s) 
   return cudaGetLastError();
 }
 
-static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s) {
+static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s, void* mark = nullptr) {
   const int P = a.T * a.w.TOPK;
   const GemmTile* tiles = static_cast<const GemmTile*>(a.tiles);
   // gate/up: A = normed rows of the sorted pairs' tokens, B = expert gate rows i and up rows I + i
@@ -341,6 +342,7 @@ static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s) {
   g.ldo = a.w.I;
   g.out_nrows = P;
   cudaError_t e = launch_wide(g, EPI_SILU_TILE, true, a.max_tiles, s);
+  if (e == cudaSuccess) e = record_event(mark, s);
   if (e != cudaSuccess) return e;
   // down: A = inter rows in sorted order, B = expert down rows; epilogue weights by w[pair] into slot[pair]
   GemmParams d = base_params(a);
@@ -420,17 +422,19 @@ cudaError_t prefill_routed(const BlockArgs& a, uint16_t* inter_out, cudaStream_t
   return cudaGetLastError();
 }
 
-cudaError_t prefill_block(const BlockArgs& a, cudaStream_t s) {
+cudaError_t prefill_block(const BlockArgs& a, cudaStream_t s, void* const* marks) {
   cudaError_t e = clear_bits(a, s);
   if (e != cudaSuccess) return e;
   prefill_norm_kernel<<<a.T, kPT, 0, s>>>(a);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if ((e = run_router(a, s)) != cudaSuccess) return e;
   if ((e = run_sort(a, true, s)) != cudaSuccess) return e;
-  if ((e = run_experts(a, s)) != cudaSuccess) return e;
+  if (marks && (e = record_event(marks[1], s)) != cudaSuccess) return e;
+  if ((e = run_experts(a, s, marks ? marks[2] : nullptr)) != cudaSuccess) return e;
   if ((e = prefill_shared(a, s)) != cudaSuccess) return e;
   prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 1 | 2);
-  return cudaGetLastError();
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  return marks ? record_event(marks[3], s) : cudaSuccess;
 }
 
 }  // namespace moe

@@ -9,8 +9,10 @@ namespace moe {
 bool prefill_supported(const moe_layer_weights& w);
 
 // Whole block (qwen.cu:429-448 at T >= 8): residual RMSNorm, router GEMM + top-k, stable expert sort, grouped INT4
-// GEMMs, shared-expert GEMMs, slot-order combine (+ the next layer's RMSNorm when a.next_rms1 is set).
-cudaError_t prefill_block(const BlockArgs& a, cudaStream_t s);
+// GEMMs, shared-expert GEMMs, slot-order combine (+ the next layer's RMSNorm when a.next_rms1 is set). marks
+// (nullable, 4 cudaEvent_t of which [1..3] are used) are recorded after the routing stage (norm, router, top-k,
+// sort), after the gate/up GEMM and at the end.
+cudaError_t prefill_block(const BlockArgs& a, cudaStream_t s, void* const* marks = nullptr);
 // Router GEMM + top-k from a.normed into a.logits / a.idx / a.wts.
 cudaError_t prefill_router(const BlockArgs& a, cudaStream_t s);
 // moe() for caller routing a.idx / a.wts: sort, grouped GEMMs, slot-order sum into a.routed; inter_out

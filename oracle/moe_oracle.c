@@ -382,6 +382,8 @@ typedef struct orc_weights {
   const uint16_t* shared_gate;    /* bf16 [H] */
   int32_t H, E, TOPK, I, Is, G;
   float eps;
+  const float* router_bias;       /* fp32 [E] or NULL: added to the logits as they are produced (no reference
+                                   * counterpart; the prefill benchmark's per-expert Zipf skew) */
 } orc_weights;
 
 /* Optional intermediates (every pointer nullable), sized for T tokens. */
@@ -422,6 +424,8 @@ ORC_API int orc_moe_block_forward(const orc_weights* w, float* hidden, const uin
 
   orc_residual_rmsnorm(hidden, attn_out, w->rms2, normed, T, H, w->eps);
   dense_bf16(normed, w->router, logits, 0, T, E, H);
+  if (w->router_bias)
+    for (int64_t i = 0; i < (int64_t)T * E; ++i) logits[i] += w->router_bias[i % E];
   orc_topk(logits, idx, wts, T, E, K);
   if (mode == 0) {
     orc_moe_gate_up_int4(normed, w->exp_gu_q, w->exp_gu_s, idx, inter, T, K, I, H, G);

@@ -145,7 +145,8 @@ def exact_normed(shape, T, seed):
 class _Weights(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in ("rms2", "router", "exp_gu_q", "exp_gu_s", "exp_dn_q", "exp_dn_s",
                                                "shared_gate_up", "shared_down", "shared_gate")] + \
-               [(n, ctypes.c_int32) for n in ("H", "E", "TOPK", "I", "Is", "G")] + [("eps", ctypes.c_float)]
+               [(n, ctypes.c_int32) for n in ("H", "E", "TOPK", "I", "Is", "G")] + [("eps", ctypes.c_float),
+                                                                              ("router_bias", ctypes.c_void_p)]
 
 
 class _Trace(ctypes.Structure):
@@ -198,7 +199,9 @@ class Oracle:
         s = shape
         T = hidden.shape[0]
         keep = [np.ascontiguousarray(layer[n]) for n, _ in _Weights._fields_[:9]]
-        w = _Weights(*[_p(a) for a in keep], s.H, s.E, s.TOPK, s.I, s.Is, s.G, s.eps)
+        bias = layer.get("router_bias")
+        bias = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        w = _Weights(*[_p(a) for a in keep], s.H, s.E, s.TOPK, s.I, s.Is, s.G, s.eps, _p(bias))
         h = np.ascontiguousarray(hidden, dtype=np.float32).copy()
         a = np.ascontiguousarray(attn_out, dtype=np.uint16)
         normed = np.zeros((T, s.H), np.uint16)
@@ -228,6 +231,8 @@ class Oracle:
         x = np.ascontiguousarray(normed, np.uint16)
         r = np.ascontiguousarray(layer["router"])
         self.lib.orc_dense_bf16_f32(_p(x), _p(r), _p(logits), T, s.E, s.H)
+        if layer.get("router_bias") is not None:  # fp32 add after the sum, as the block does
+            logits = (logits + np.asarray(layer["router_bias"], np.float32)[None, :]).astype(np.float32)
         self.lib.orc_topk(_p(logits), _p(idx), _p(wts), T, s.E, s.TOPK)
         return logits, idx, wts
 

@@ -165,3 +165,22 @@ def test_threaded_oracle_is_deterministic(orc, layer_small):
         orc.set_threads(1)
     for k in ("hidden", "routed", "sout", "idx"):
         assert np.array_equal(a[k], b[k])
+
+
+def test_router_bias_is_added_to_fp32_logits(orc):
+    """The optional per-expert bias shifts the oracle's logits exactly (one fp32 add after the sum) and the top-k
+    and weights follow the biased logits, in the router and in the whole block."""
+    s = O.Shape(H=512, E=16, TOPK=4, I=256, Is=256, G=32)
+    L = O.make_layer(s, 3)
+    x = O.f32_to_bf16(O.normal(5, 4, 4 * s.H)).reshape(4, s.H)
+    l0, _, _ = orc.router(s, L, x)
+    Lb = dict(L)
+    Lb["router_bias"] = np.linspace(-1, 1, s.E).astype(np.float32)
+    l1, i1, w1 = orc.router(s, Lb, x)
+    assert np.array_equal(l1, (l0 + Lb["router_bias"][None, :]).astype(np.float32))
+    ic, wc = orc.topk(l1, s.TOPK)
+    assert np.array_equal(ic, i1) and np.array_equal(wc, w1)
+    h, a = O.make_activations(s, 3, 7)
+    rb = orc.block_forward(s, Lb, h, a, mode=0)
+    r0 = orc.block_forward(s, L, h, a, mode=0)
+    assert np.allclose(rb["logits"] - r0["logits"], Lb["router_bias"][None, :], atol=1e-6)
