@@ -74,6 +74,11 @@ _SIGS = {
     "moe_synth_int4_rows": (_I, [_P, _P, ctypes.c_int64, _I, _I, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                  _P]),
     "moe_version": (ctypes.c_char_p, []),
+    # expert-parallel stages (include/moe_ep.h)
+    "moe_ep_record_bytes": (ctypes.c_size_t, [_W]),
+    "moe_ep_dispatch": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
+    "moe_ep_experts": (_I, [_W, _P, ctypes.c_size_t, _P, _I, _P, _P]),
+    "moe_ep_combine": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(_lib, _name)

@@ -12,7 +12,9 @@
 #include <cstdlib>
 
 #include "moe_common.cuh"
+#include "../../include/moe_ep.h"
 #include "moe_decode.h"
+#include "moe_ep.h"
 #include "moe_fused.h"
 #include "moe_prefill.h"
 
@@ -338,3 +340,82 @@ int moe_set_prefill_min_tokens(int T) {
 const char* moe_version(void) { return "moe_b200 0.1 sm_100a"; }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ expert-parallel stages (include/moe_ep.h)
+
+namespace {
+bool ep_geometry_ok(const moe_layer_weights* w, int world) {
+  if (!shape_ok(w) || world < 1 || world > kEpMaxWorld || w->E % world) return false;
+  const int El = w->E / world;
+  return El % 16 == 0 && El >= w->TOPK;
+}
+}  // namespace
+
+extern "C" {
+
+size_t moe_ep_record_bytes(const moe_layer_weights* w) {
+  if (!shape_ok(w)) return 0;
+  return (size_t)ep_record_bytes(w->H, w->TOPK);
+}
+
+int moe_ep_dispatch(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const float* hidden,
+                    const uint16_t* attn_out, uint16_t* normed, int T, int world, void* send, int32_t* send_count,
+                    int32_t* tok_pos, moe_stream_t stream) {
+  if (!ep_geometry_ok(w, world) || !workspace || T < 1) return (int)cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < layout_for(w, T).total)
+    return (int)cudaErrorInvalidValue;
+  if (!hidden || !attn_out || !normed || !send || !send_count || !tok_pos || !w->router || !w->rms2 ||
+      !w->shared_gate || reinterpret_cast<uintptr_t>(send) % 16)
+    return (int)cudaErrorInvalidValue;
+  const cudaStream_t s = (cudaStream_t)stream;
+  BlockArgs a = make_args(w, workspace, layout_for(w, T), T);
+  a.hidden = const_cast<float*>(hidden);
+  a.attn_out = attn_out;
+  a.normed = normed;
+  cudaError_t e = prefill_norm(a, s);
+  if (e == cudaSuccess) e = prefill_router(a, s);
+  if (e == cudaSuccess) e = ep_plan_pack(a, world, static_cast<uint8_t*>(send), send_count, tok_pos, s);
+  return (int)e;
+}
+
+int moe_ep_experts(const moe_layer_weights* w_local, void* workspace, size_t workspace_bytes, const void* recv, int R,
+                   float* part, moe_stream_t stream) {
+  if (!shape_ok(w_local) || !prefill_supported(*w_local) || !workspace || R < 0) return (int)cudaErrorInvalidValue;
+  if (!weights_present(w_local, false, true, false)) return (int)cudaErrorInvalidValue;
+  if (R == 0) return 0;
+  const WsLayout L = layout_for(w_local, std::max(R, kPrefillMinT));
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < L.total) return (int)cudaErrorInvalidValue;
+  if (!recv || !part || reinterpret_cast<uintptr_t>(recv) % 16 || reinterpret_cast<uintptr_t>(part) % 16)
+    return (int)cudaErrorInvalidValue;
+  const cudaStream_t s = (cudaStream_t)stream;
+  BlockArgs a = make_args(w_local, workspace, L, R);
+  a.normed = static_cast<uint16_t*>(const_cast<void*>(recv));
+  a.xstride = ep_record_bytes(w_local->H, w_local->TOPK) / 2;
+  a.routed = part;
+  cudaError_t e = prefill_bits_clear(a, s);
+  if (e == cudaSuccess) e = ep_mark(a, static_cast<const uint8_t*>(recv), s);
+  if (e == cudaSuccess) e = prefill_routed_marked(a, s);
+  return (int)e;
+}
+
+int moe_ep_combine(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
+                   const uint16_t* attn_out, const uint16_t* sout, uint16_t* normed, const uint16_t* next_rms1,
+                   int T, int world, const int32_t* tok_pos, const float* ret, moe_stream_t stream) {
+  if (!ep_geometry_ok(w, world) || !workspace || T < 1) return (int)cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < layout_for(w, T).total)
+    return (int)cudaErrorInvalidValue;
+  if (!hidden || !attn_out || !sout || !normed || !tok_pos || !ret) return (int)cudaErrorInvalidValue;
+  BlockArgs a = make_args(w, workspace, layout_for(w, T), T);
+  a.hidden = hidden;
+  a.attn_out = attn_out;
+  a.sout = const_cast<uint16_t*>(sout);
+  a.normed = normed;
+  a.next_rms1 = next_rms1;
+  a.ep_pos = tok_pos;
+  a.ep_ret = ret;
+  a.ep_world = world;
+  return (int)prefill_combine(a, (cudaStream_t)stream);
+}
+
+}  // extern "C"
+

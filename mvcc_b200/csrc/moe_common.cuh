@@ -236,6 +236,13 @@ struct BlockArgs {
   int32_t* sorted;
   float* slot;
   int nwp, max_tiles;
+  // row stride (elements) of `normed` as the routed gate/up operand; 0 = H (expert-parallel records are wider)
+  int xstride;
+  // expert-parallel combine (null otherwise): routed[t] = sum over ranks d < ep_world, ascending, with
+  // ep_pos[t * ep_world + d] >= 0 of the returned partial row ep_ret[ep_pos[...]]
+  const int32_t* ep_pos;
+  const float* ep_ret;
+  int ep_world;
 };
 
 }  // namespace moe

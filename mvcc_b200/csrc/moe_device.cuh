@@ -23,6 +23,34 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // Position of k in the permuted fp32 activation row: k = 32c + 8q + 4h + e -> ((2q + h) * NCH + c) * 4 + e.
+// Exclusive block-wide prefix sum of one int per thread (blockDim.x a multiple of 32, at most 1024); *total
+// receives the block's sum. sm: 32 ints of shared memory.
+__device__ __forceinline__ int block_excl_scan(int v, int* sm, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) sm[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? sm[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) sm[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  const int before = warp ? sm[warp - 1] : 0;
+  *total = sm[nw - 1];
+  return before + x - v;
+}
+
 __device__ __forceinline__ int xperm(int k, int nch) {
   const int c = k >> 5, r = k & 31;
   return (((r >> 3) * 2 + ((r >> 2) & 1)) * nch + c) * 4 + (r & 3);

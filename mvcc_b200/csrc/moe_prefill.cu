@@ -32,32 +32,6 @@ namespace moe {
 
 constexpr int kPT = 256;  // threads of the small prefill kernels
 
-__device__ __forceinline__ int block_excl_scan(int v, int* sm, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  __syncthreads();
-  if (lane == 31) sm[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int w = lane < nw ? sm[lane] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += y;
-    }
-    if (lane < nw) sm[lane] = w;  // inclusive warp totals
-  }
-  __syncthreads();
-  const int before = warp ? sm[warp - 1] : 0;
-  *total = sm[nw - 1];
-  return before + x - v;
-}
-
 // ---- residual RMSNorm + shared-gate logit, one CTA per token
 __global__ void __launch_bounds__(kPT) prefill_norm_kernel(const BlockArgs a) {
   __shared__ float red[32];
@@ -208,12 +182,17 @@ __global__ void __launch_bounds__(kPT) prefill_unsort_kernel(const BlockArgs a, 
 
 // ---- slot-order reduction and gated residual combine, one CTA per token.
 // mode: 1 = write routed, 2 = combine into hidden (+ next-layer RMSNorm when a.next_rms1 is set).
+// The routed sum is over the token's slots with a valid expert, in slot order, or, on the expert-parallel source
+// side (a.ep_pos set), over the partial rows the ranks returned, in rank order.
 __global__ void __launch_bounds__(kPT) prefill_combine_kernel(const BlockArgs a, int mode) {
   __shared__ float red[32];
   const int t = blockIdx.x, tid = threadIdx.x, H = a.w.H, K = a.w.TOPK;
+  const bool ep = a.ep_pos != nullptr;
   int ok[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) ok[k] = k < K && (unsigned)a.idx[(int64_t)t * K + k] < (unsigned)a.w.E;
+  for (int k = 0; k < 8; ++k)
+    ok[k] = ep ? (k < a.ep_world ? a.ep_pos[(int64_t)t * a.ep_world + k] : -1)
+               : (k < K && (unsigned)a.idx[(int64_t)t * K + k] < (unsigned)a.w.E);
   const float g = (mode & 2) ? a.gate[t] : 0.f;
   const bool nn = (mode & 2) && a.next_rms1;
   float4 hv[4];
@@ -225,8 +204,9 @@ __global__ void __launch_bounds__(kPT) prefill_combine_kernel(const BlockArgs a,
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      if (!ok[k]) continue;
-      const float4 v = __ldcs(reinterpret_cast<const float4*>(a.slot + ((int64_t)t * K + k) * H) + i);
+      if (ep ? ok[k] < 0 : !ok[k]) continue;
+      const float* src = ep ? a.ep_ret + (int64_t)ok[k] * H : a.slot + ((int64_t)t * K + k) * H;
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(src) + i);
       acc.x += v.x;
       acc.y += v.y;
       acc.z += v.z;
@@ -301,12 +281,15 @@ static cudaError_t run_router(const BlockArgs& a, cudaStream_t s) {
   return launch_gemm(p, EPI_F32, 128, 128, false, (a.T + 127) / 128, false, s);
 }
 
-static cudaError_t run_sort(const BlockArgs& a, bool from_topk, cudaStream_t s) {
+// Bitmaps from the top-k (SORT_TOPK), from caller routing (SORT_MARK), or already marked by the caller's kernel
+// (SORT_MARKED); then the per-expert scan and the stable scatter.
+enum { SORT_MARK = 0, SORT_TOPK = 1, SORT_MARKED = 2 };
+static cudaError_t run_sort(const BlockArgs& a, int from, cudaStream_t s) {
   const int P = a.T * a.w.TOPK;
   cudaError_t e = cudaSuccess;
-  if (from_topk) {
+  if (from == SORT_TOPK) {
     prefill_topk_kernel<<<(a.T + kPT / 32 - 1) / (kPT / 32), kPT, 0, s>>>(a, 1);
-  } else {
+  } else if (from == SORT_MARK) {
     prefill_mark_kernel<<<(P + kPT - 1) / kPT, kPT, 0, s>>>(a);
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -322,7 +305,7 @@ static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s, void* mark = 
   // gate/up: A = normed rows of the sorted pairs' tokens, B = expert gate rows i and up rows I + i
   GemmParams g = base_params(a);
   g.A = a.normed;
-  g.lda = a.w.H;
+  g.lda = a.xstride ? a.xstride : a.w.H;
   g.a_rows = a.sorted;
   g.a_div = a.w.TOPK;
   g.list_len = P;
@@ -412,7 +395,7 @@ cudaError_t prefill_router(const BlockArgs& a, cudaStream_t s) {
 
 cudaError_t prefill_routed(const BlockArgs& a, uint16_t* inter_out, cudaStream_t s) {
   cudaError_t e = clear_bits(a, s);
-  if (e == cudaSuccess) e = run_sort(a, false, s);
+  if (e == cudaSuccess) e = run_sort(a, SORT_MARK, s);
   if (e == cudaSuccess) e = run_experts(a, s);
   if (e != cudaSuccess) return e;
   prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 1);
@@ -428,13 +411,33 @@ cudaError_t prefill_block(const BlockArgs& a, cudaStream_t s, void* const* marks
   prefill_norm_kernel<<<a.T, kPT, 0, s>>>(a);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if ((e = run_router(a, s)) != cudaSuccess) return e;
-  if ((e = run_sort(a, true, s)) != cudaSuccess) return e;
+  if ((e = run_sort(a, SORT_TOPK, s)) != cudaSuccess) return e;
   if (marks && (e = record_event(marks[1], s)) != cudaSuccess) return e;
   if ((e = run_experts(a, s, marks ? marks[2] : nullptr)) != cudaSuccess) return e;
   if ((e = prefill_shared(a, s)) != cudaSuccess) return e;
   prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 1 | 2);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   return marks ? record_event(marks[3], s) : cudaSuccess;
+}
+
+cudaError_t prefill_norm(const BlockArgs& a, cudaStream_t s) {
+  prefill_norm_kernel<<<a.T, kPT, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t prefill_bits_clear(const BlockArgs& a, cudaStream_t s) { return clear_bits(a, s); }
+
+cudaError_t prefill_routed_marked(const BlockArgs& a, cudaStream_t s) {
+  cudaError_t e = run_sort(a, SORT_MARKED, s);
+  if (e == cudaSuccess) e = run_experts(a, s);
+  if (e != cudaSuccess) return e;
+  prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 1);
+  return cudaGetLastError();
+}
+
+cudaError_t prefill_combine(const BlockArgs& a, cudaStream_t s) {
+  prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 2);
+  return cudaGetLastError();
 }
 
 }  // namespace moe

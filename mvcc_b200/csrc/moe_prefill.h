@@ -21,4 +21,15 @@ cudaError_t prefill_routed(const BlockArgs& a, uint16_t* inter_out, cudaStream_t
 // Shared expert from a.normed into a.sout.
 cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s);
 
+// Pieces the expert-parallel entry points compose (moe_ep.cu):
+// residual RMSNorm of a.hidden + a.attn_out into a.normed, shared-gate sigmoid into a.gate;
+cudaError_t prefill_norm(const BlockArgs& a, cudaStream_t s);
+// zeroing of the pair bitmaps (before a kernel of the caller marks them);
+cudaError_t prefill_bits_clear(const BlockArgs& a, cudaStream_t s);
+// moe() on pair bitmaps, a.idx and a.wts the caller's kernel already wrote: scan, scatter, grouped GEMMs, slot-order
+// sum into a.routed (slots with an index outside [0, E) contribute nothing);
+cudaError_t prefill_routed_marked(const BlockArgs& a, cudaStream_t s);
+// gated residual combine into a.hidden (+ next RMSNorm); routed rows from a.ep_pos / a.ep_ret when set.
+cudaError_t prefill_combine(const BlockArgs& a, cudaStream_t s);
+
 }  // namespace moe

@@ -1,0 +1,201 @@
+"""Expert-parallel MoE layer: the block of `MoeBlock` with its routed experts sharded over the GPUs of one node.
+
+Rank d of `world` holds experts [d * E / world, (d + 1) * E / world) and the replicated router, norm and shared
+expert. One step on each rank (include/moe_ep.h):
+
+  1. moe_ep_dispatch: residual RMSNorm, router + top-k, one dispatch record per (token, rank owning >= 1 of its
+     experts), grouped by destination;
+  2. the shared expert of the rank's own tokens on a side stream, overlapping 3-5;
+  3. all-to-all of the per-destination record counts, read back to the host (the one host synchronisation of a step:
+     the record exchange needs its split sizes);
+  4. all-to-all of the records; moe_ep_experts on the received records -> one fp32 partial row per record;
+  5. all-to-all of the partial rows back, reverse splits;
+  6. moe_ep_combine: per token the partials in rank order + gated shared expert into hidden.
+
+`ep_step` runs one rank's step with its exchanges through `NcclExchange` (all_to_all_single over a torch.distributed
+process group: NCCL on GPUs); `emulated_step` runs every rank's stages in one process on one GPU, the exchanges as
+device copies, for single-GPU parity tests of the multi-rank numerics. The reference runs the block on one GPU only
+(qwen.cu:429-448); the split has no counterpart there.
+"""
+import contextlib
+import ctypes
+import dataclasses
+
+import torch
+
+from . import (MoeBlock, MoeLayer, MoeLayerWeights, MoeShape, _check, _lib, _ptr, _stream)
+
+
+class ExpertShard:
+    """Rank `rank`'s routed experts of `layer` (tensors of the shard only; E = E / world) as a moe_layer_weights
+    whose router and shared-expert pointers are NULL: moe_ep_experts reads the expert tensors alone."""
+
+    def __init__(self, layer: MoeLayer, rank: int, world: int, copy=True):
+        s = layer.shape
+        if world < 1 or s.E % world:
+            raise ValueError(f"E={s.E} does not split over {world} ranks")
+        El = s.E // world
+        self.shape = dataclasses.replace(s, E=El)
+        self.rank, self.world, self.first = rank, world, rank * El
+        self.t = {}
+        for n in ("exp_gu_q", "exp_gu_s", "exp_dn_q", "exp_dn_s"):
+            v = layer.t[n][rank * El:(rank + 1) * El]
+            self.t[n] = v.clone() if copy else v
+        null = ctypes.c_void_p()
+        self.c = MoeLayerWeights(null, null, *[ctypes.c_void_p(self.t[n].data_ptr()) for n in
+                                               ("exp_gu_q", "exp_gu_s", "exp_dn_q", "exp_dn_s")],
+                                 null, null, null, s.H, El, s.TOPK, s.I, s.Is, s.G, s.eps, None)
+
+
+class EpRank:
+    """One rank's state and stages: buffers sized for up to `max_tokens` tokens on every rank."""
+
+    def __init__(self, layer: MoeLayer, rank: int, world: int, max_tokens: int, device=None, copy_shard=True):
+        s = layer.shape
+        self.layer, self.shape = layer, s
+        self.rank, self.world, self.max_tokens = rank, world, max_tokens
+        self.device = layer.t["router"].device if device is None else torch.device(device)
+        self.shard = ExpertShard(layer, rank, world, copy=copy_shard)
+        self.src = MoeBlock(layer, max_tokens)      # dispatch + combine workspace
+        self.sh = MoeBlock(layer, max_tokens)       # shared-expert workspace (side stream)
+        cap = max_tokens * world                    # records a rank can send or receive
+        self.rec_bytes = _lib.moe_ep_record_bytes(ctypes.byref(layer.c))
+        xb = _lib.moe_workspace_bytes(ctypes.byref(self.shard.c), max(8, cap))
+        if self.rec_bytes == 0 or xb == 0:
+            raise ValueError("moe_ep: unsupported geometry")
+        dev = self.device
+        self.xws_bytes = xb
+        self.xws = torch.empty(xb, dtype=torch.uint8, device=dev)
+        _check(_lib.moe_workspace_init(_ptr(self.xws), xb, _stream(None)), "moe_workspace_init")
+        self.send = torch.empty(cap, self.rec_bytes, dtype=torch.uint8, device=dev)
+        self.recv = torch.empty(cap, self.rec_bytes, dtype=torch.uint8, device=dev)
+        self.send_count = torch.zeros(world, dtype=torch.int32, device=dev)
+        self.recv_count = torch.zeros(world, dtype=torch.int32, device=dev)
+        self.tok_pos = torch.empty(max_tokens, world, dtype=torch.int32, device=dev)
+        self.part = torch.empty(cap, s.H, dtype=torch.float32, device=dev)
+        self.ret = torch.empty(cap, s.H, dtype=torch.float32, device=dev)
+        self.sout = torch.empty(max_tokens, s.H, dtype=torch.int16, device=dev)
+        self.side = torch.cuda.Stream(device=dev)
+        self._shared_done = None
+        torch.cuda.current_stream(dev).synchronize()
+
+    # -- stages (all asynchronous on `stream`)
+    def dispatch(self, hidden, attn_out, normed, stream):
+        T = hidden.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > max_tokens {self.max_tokens}")
+        _check(_lib.moe_ep_dispatch(ctypes.byref(self.layer.c), _ptr(self.src.ws), self.src.ws_bytes, _ptr(hidden),
+                                    _ptr(attn_out), _ptr(normed), T, self.world, _ptr(self.send),
+                                    _ptr(self.send_count), _ptr(self.tok_pos), _stream(stream)), "moe_ep_dispatch")
+        # the shared expert needs normed only: run it beside the exchange
+        self.side.wait_stream(stream)
+        _check(_lib.moe_shared_expert(ctypes.byref(self.layer.c), _ptr(self.sh.ws), self.sh.ws_bytes, _ptr(normed),
+                                      _ptr(self.sout), T, _stream(self.side)), "moe_shared_expert")
+        self._shared_done = torch.cuda.Event()
+        self._shared_done.record(self.side)
+
+    def experts(self, R, stream):
+        _check(_lib.moe_ep_experts(ctypes.byref(self.shard.c), _ptr(self.xws), self.xws_bytes, _ptr(self.recv), R,
+                                   _ptr(self.part), _stream(stream)), "moe_ep_experts")
+
+    def combine(self, hidden, attn_out, normed, next_rms1, stream):
+        T = hidden.shape[0]
+        stream.wait_event(self._shared_done)
+        _check(_lib.moe_ep_combine(ctypes.byref(self.layer.c), _ptr(self.src.ws), self.src.ws_bytes, _ptr(hidden),
+                                   _ptr(attn_out), _ptr(self.sout), _ptr(normed), _ptr(next_rms1), T, self.world,
+                                   _ptr(self.tok_pos), _ptr(self.ret), _stream(stream)), "moe_ep_combine")
+
+    def error_word(self):
+        """Error bits recorded by this rank's kernels since the last read (the three workspaces)."""
+        w = self.src.error_word() | self.sh.error_word()
+        rc = _lib.moe_workspace_error(_ptr(self.xws), self.xws_bytes, _stream(None))
+        if rc < 0:
+            raise RuntimeError(f"moe_workspace_error failed: cudaError {-rc}")
+        return w | rc
+
+
+class NcclExchange:
+    """The exchanges of one rank over a torch.distributed process group (NCCL on GPUs, gloo in the CPU tests)."""
+
+    def __init__(self, group=None):
+        self.group = group
+
+    def counts(self, rank_state):
+        """Per-destination record counts out, per-source counts in; both as host lists (one synchronisation)."""
+        import torch.distributed as dist
+        dist.all_to_all_single(rank_state.recv_count, rank_state.send_count, group=self.group)
+        both = torch.stack([rank_state.send_count, rank_state.recv_count]).cpu()
+        return both[0].tolist(), both[1].tolist()
+
+    def a2a(self, out, inp, out_splits, in_splits):
+        import torch.distributed as dist
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+
+def ep_step(rank_state, exchange, hidden, attn_out, normed, next_rms1=None, stream=None):
+    """One expert-parallel step of one rank (every rank of the group calls it with its own tokens):
+    hidden (fp32 [T,H], in/out), attn_out (bf16 bits [T,H]), normed (out), as MoeBlock.forward."""
+    if rank_state.device.type == "cuda":
+        st = torch.cuda.current_stream(rank_state.device) if stream is None else stream
+        ctx = torch.cuda.stream(st)
+    else:  # host-side doubles of the stages (CPU tests over gloo)
+        st, ctx = None, contextlib.nullcontext()
+    with ctx:
+        rank_state.dispatch(hidden, attn_out, normed, st)
+        sc, rc = exchange.counts(rank_state)
+        S, R = sum(sc), sum(rc)
+        exchange.a2a(rank_state.recv[:R], rank_state.send[:S], rc, sc)
+        rank_state.experts(R, st)
+        exchange.a2a(rank_state.ret[:S], rank_state.part[:R], sc, rc)
+        rank_state.combine(hidden, attn_out, normed, next_rms1, st)
+    return S, R
+
+
+class ExpertParallelMoe:
+    """The expert-parallel MoE layer of one rank: `forward` is MoeBlock.forward for this rank's tokens, with the
+    routed experts sharded over the process group."""
+
+    def __init__(self, layer: MoeLayer, max_tokens: int, group=None, rank=None, world=None):
+        import torch.distributed as dist
+        self.rank = dist.get_rank(group) if rank is None else rank
+        self.world = dist.get_world_size(group) if world is None else world
+        self.state = EpRank(layer, self.rank, self.world, max_tokens)
+        self.exchange = NcclExchange(group)
+
+    def forward(self, hidden, attn_out, normed, next_rms1=None, stream=None):
+        return ep_step(self.state, self.exchange, hidden, attn_out, normed, next_rms1, stream)
+
+    def error_word(self):
+        return self.state.error_word()
+
+
+def emulated_step(ranks, hiddens, attn_outs, normeds, next_rms1=None, stream=None):
+    """All ranks of an expert-parallel step in one process (every EpRank on one device, exchanges as device copies
+    in the order the all-to-alls define): the multi-rank numerics on a single GPU."""
+    W = len(ranks)
+    st = torch.cuda.current_stream() if stream is None else stream
+    with torch.cuda.stream(st):
+        for r in range(W):
+            ranks[r].dispatch(hiddens[r], attn_outs[r], normeds[r], st)
+        C = torch.stack([r.send_count for r in ranks]).cpu().tolist()  # C[s][d]
+        soff = [[sum(C[s][:d]) for d in range(W)] for s in range(W)]
+        roff = [[sum(C[x][d] for x in range(s)) for s in range(W)] for d in range(W)]  # roff[d][s]
+        R = [sum(C[s][d] for s in range(W)) for d in range(W)]
+        for d in range(W):
+            for s in range(W):
+                n = C[s][d]
+                if n:
+                    ranks[d].recv[roff[d][s]:roff[d][s] + n].copy_(ranks[s].send[soff[s][d]:soff[s][d] + n])
+        for d in range(W):
+            ranks[d].experts(R[d], st)
+        for s in range(W):
+            for d in range(W):
+                n = C[s][d]
+                if n:
+                    ranks[s].ret[soff[s][d]:soff[s][d] + n].copy_(ranks[d].part[roff[d][s]:roff[d][s] + n])
+        for r in range(W):
+            ranks[r].combine(hiddens[r], attn_outs[r], normeds[r], next_rms1, st)
+    return C
+
+
+__all__ = ["ExpertShard", "EpRank", "NcclExchange", "ExpertParallelMoe", "ep_step", "emulated_step", "MoeShape"]

@@ -265,6 +265,70 @@ class Oracle:
             self.lib.orc_moe_slot_reduce(_p(slot), _p(routed), T, s.TOPK, s.H)
         return inter, routed
 
+    def slot_partials(self, shape, layer, normed, idx, wts):
+        """The tile path's per-slot partials (kernels.cuh:942-1057): slot [T, TOPK, H] fp32 = w * down(inter)."""
+        s = shape
+        T = normed.shape[0]
+        x = np.ascontiguousarray(normed, np.uint16)
+        ix = np.ascontiguousarray(idx, np.int32)
+        wt = np.ascontiguousarray(wts, np.float32)
+        inter = np.zeros((T, s.TOPK, s.I), np.uint16)
+        slot = np.zeros((T, s.TOPK, s.H), np.float32)
+        gq, gs, dq, ds = (np.ascontiguousarray(layer[n]) for n in ("exp_gu_q", "exp_gu_s", "exp_dn_q", "exp_dn_s"))
+        self.lib.orc_moe_gate_up_tile(_p(x), _p(gq), _p(gs), _p(ix), _p(inter), T, s.TOPK, s.I, s.H, s.G)
+        self.lib.orc_moe_down_tile(_p(inter), _p(dq), _p(ds), _p(ix), _p(wt), _p(slot), T, s.TOPK, s.H, s.I, s.G)
+        return slot
+
+    def shared_gate_combine(self, shape, layer, hidden_res, routed, sout, normed, next_rms1=None):
+        """shared_gate_combine(_rmsnorm)_kernel (kernels.cuh:1081-1121) on the residual-added hidden: returns
+        (hidden, normed_out, gate)."""
+        s = shape
+        T = hidden_res.shape[0]
+        h = np.ascontiguousarray(hidden_res, np.float32).copy()
+        nout = np.zeros((T, s.H), np.uint16)
+        gate = np.zeros((T,), np.float32)
+        nr = None if next_rms1 is None else np.ascontiguousarray(next_rms1, np.uint16)
+        self.lib.orc_shared_gate_combine(_p(h), _p(np.ascontiguousarray(routed, np.float32)),
+                                         _p(np.ascontiguousarray(sout, np.uint16)),
+                                         _p(np.ascontiguousarray(normed, np.uint16)),
+                                         _p(np.ascontiguousarray(layer["shared_gate"])), _p(nr), _p(nout), _p(gate),
+                                         T, s.H, ctypes.c_float(s.eps))
+        return h, nout, gate
+
+    def ep_routed(self, shape, layer, normed, idx, wts, world):
+        """Routed output of the expert-parallel layer over `world` ranks (rank d owns experts [d*E/world,
+        (d+1)*E/world)): per rank the partial of its slots summed in slot order, then the partials summed in rank
+        order, in fp32 (mvcc_b200/csrc/moe_ep.cu and the source-side combine of moe_prefill.cu)."""
+        s = shape
+        slot = self.slot_partials(shape, layer, normed, idx, wts)
+        El = s.E // world
+        T = normed.shape[0]
+        routed = np.zeros((T, s.H), np.float32)
+        owner = np.asarray(idx) // El
+        for d in range(world):
+            part = np.zeros((T, s.H), np.float32)
+            for k in range(s.TOPK):
+                on = owner[:, k] == d
+                part[on] = part[on] + slot[on, k]
+            sent = (owner == d).any(axis=1)
+            routed[sent] = routed[sent] + part[sent]
+        return routed
+
+    def ep_block_forward(self, shape, layer, hidden, attn_out, world, next_rms1=None):
+        """The block with its routed experts split over `world` ranks (tile numerics otherwise): returns the
+        block_forward dict with routed / hidden / normed of the expert-parallel summation order."""
+        s = shape
+        base = self.block_forward(shape, layer, hidden, attn_out, mode=1)
+        normed0 = base["normed"]
+        routed = self.ep_routed(shape, layer, normed0, base["idx"], base["wts"], world)
+        hres = (np.asarray(hidden, np.float32) + bf16_to_f32(np.asarray(attn_out, np.uint16))).astype(np.float32)
+        h, nout, _ = self.shared_gate_combine(s, layer, hres, routed, base["sout"], normed0, next_rms1)
+        out = dict(base)
+        out["routed"] = routed
+        out["hidden"] = h
+        out["normed"] = nout if next_rms1 is not None else normed0
+        return out
+
     def shared(self, shape, layer, normed):
         """Shared expert: returns (sinter bf16 [T,Is], sout bf16 [T,H])."""
         s = shape

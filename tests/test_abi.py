@@ -1,5 +1,5 @@
-"""CPU tests of the C-ABI library: it loads, exports every entry point include/moe_block.h declares, and its
-host-side shape and workspace checks behave. No kernel is launched here."""
+"""CPU tests of the C-ABI library: it loads, exports every entry point include/*.h declares, and its host-side
+shape and workspace checks behave. No kernel is launched here."""
 import ctypes
 import os
 import re
@@ -7,12 +7,15 @@ import re
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "moe_block.h")
+HEADERS = [os.path.join(ROOT, "include", f) for f in sorted(os.listdir(os.path.join(ROOT, "include")))
+           if f.endswith(".h")]
 
 
 def _declared():
-    text = open(HEADER).read()
-    return sorted(set(re.findall(r"^MOE_API\s+[\w\s\*]+?\b(moe_\w+)\s*\(", text, flags=re.M)))
+    names = set()
+    for h in HEADERS:
+        names |= set(re.findall(r"^MOE_API\s+[\w\s\*]+?\b(moe_\w+)\s*\(", open(h).read(), flags=re.M))
+    return sorted(names)
 
 
 def test_library_exports_every_declared_symbol():

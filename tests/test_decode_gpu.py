@@ -258,3 +258,40 @@ def test_full_size_block_against_oracle(orc, T):
     assert ok.mean() >= 0.5
     assert O.max_rel_err(tr["routed"].cpu().numpy()[ok], ref["routed"][ok]) < TOL_INT4
     assert O.max_rel_err(gh[ok], ref["hidden"][ok]) < TOL_BF16
+
+
+_full = {}
+
+
+@pytest.mark.parametrize("T", [9, 12, 16])
+def test_full_geometry_decode_kernels(orc, T):
+    """BASELINE geometry (H=2048, E=256, top-8, I=Is=512, G=64) on the three decode kernels for batches above the
+    fused kernel's limit. T = 12 asks the routing kernel for exactly 48 KB of dynamic shared memory, which with its
+    static shared memory exceeds the default limit: every decode kernel raises its limit on first launch."""
+    m = mb()
+    ms = m.MoeShape()
+    if "layer" not in _full:
+        layer = m.synth_layer(ms, seed=19)
+        torch.cuda.synchronize()
+        _full["layer"] = layer
+        _full["host"] = {n: (v.cpu().numpy() if v.dtype == torch.uint8 else v.cpu().numpy().view(np.uint16))
+                         for n, v in layer.t.items()}
+    layer, L = _full["layer"], _full["host"]
+    hid, att = m.synth_activations(ms, T, 23 + T)
+    hidden = hid.cpu().numpy()
+    attn = att.cpu().numpy().view(np.uint16)
+    blk = m.MoeBlock(layer, T)
+    normed = torch.zeros(T, ms.H, dtype=torch.int16, device="cuda")
+    blk.forward(hid, att, normed)
+    torch.cuda.synchronize()
+    s = O.Shape()
+    ref = orc.block_forward(s, L, hidden, attn, mode=0)
+    tr = blk.trace(T)
+    gl = tr["logits"].cpu().numpy()
+    check_routing(orc, s, gl, tr["idx"].cpu().numpy(), tr["wts"].cpu().numpy(), ref["logits"], ref["idx"],
+                  ref["wts"], logit_tol=2e-3)
+    ok = stable_rows(s, ref["logits"], gpu_logits=gl)
+    assert ok.mean() >= 0.5
+    assert O.max_rel_err(hid.cpu().numpy()[ok], ref["hidden"][ok]) < TOL_BF16
+    assert O.max_rel_err(O.bf16_to_f32(host16(normed)[ok]), O.bf16_to_f32(ref["normed"][ok])) < TOL_BF16
+    assert blk.error_word() == 0
