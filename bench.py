@@ -19,9 +19,13 @@ Further objects on the same line:
                   the whole block, its own e2e and clocks, and the C oracle on a bounded token sample;
   e2e             the headline steps with each step's input (hidden fp32, attn_out bf16) copied from pinned host
                   memory and its outputs (hidden, normed) copied back inside the timed region;
+  ep_prefill      BASELINE config 5: 16384 tokens per step through one int4 MoE layer, the 256 experts sharded over
+                  the N ranks (N = 1: the single-GPU prefill block; N > 1: mvcc_b200.ep over NCCL all-to-all, each
+                  rank holding 16384 / N of the tokens), tokens/s of the whole job from the max-over-ranks time
+                  (`scaling` strong: the total work is fixed);
   cpu_baseline    the C oracle (test infrastructure) of the decode block on the host cores, N=1 rank 0 only.
-Under torchrun (N > 1) every rank runs its own replica of these single-GPU workloads (`scaling` weak: the decode
-block does not shard).
+Under torchrun (N > 1) every rank runs its own replica of the single-GPU workloads (`value`, decode_batches,
+prefill; `scaling` weak: the decode block does not shard); ep_prefill is the sharded one.
 
 `--impl reference` times the reference arm: the reference implements the block only as GPU kernels
 (examples/qwen/kernels.cuh) and has no CPU code for it, so the arm is the oracle's restatement of those kernels on
@@ -48,6 +52,10 @@ LAYER_COPIES = 32
 GRAPH_STEPS = 256
 PREFILL_T = 4096
 PREFILL_COPIES = 2
+EP_TOKENS = 16384
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch from one ncu capture of the same kernel on the
+# same workload: the fused decode kernel at batch 1, the routed gate/up GEMM at prefill T=4096 with the Zipf bias.
+NCU_TRAFFIC = {"fused_b1": 20826624 + 1024, "gate_up_t4096": 168678656 + 23924480}
 DTYPE = "int4/bf16 weights, bf16 activations, fp32 accumulate"
 DATA = ("synthetic (seeded device generator: bf16 N(0,0.02) weights, INT4 absmax/7 group-64 experts, "
         "activations N(0,1))")
@@ -345,7 +353,8 @@ def prefill_case(m, shape, K, W, stream, world, dev, peaks, cpu_seconds, do_cpu)
                      "bound": "tensor", "achieved": gu_tf, "peak": peaks["tf_sustained"], "unit": "TFLOP/s",
                      "frac": gu_tf / peaks["tf_sustained"],
                      "peak_kind": f"{peaks['kind']} bf16 sustained",
-                     "flops_per_launch": fl["gate_up"], "us_per_launch": st[1], "traffic": None},
+                     "flops_per_launch": fl["gate_up"], "us_per_launch": st[1],
+                     "traffic": NCU_TRAFFIC["gate_up_t4096"]},
         "block_tflops": {"achieved": blk_tf, "frac": blk_tf / peaks["tf_sustained"], "flops_per_step": fl["block"]},
         "e2e": {"value": world * T * K / (ms_e2e / 1e3), "unit": "tok/s", "h2d_bytes_per_step": hb,
                 "d2h_bytes_per_step": db},
@@ -355,6 +364,73 @@ def prefill_case(m, shape, K, W, stream, world, dev, peaks, cpu_seconds, do_cpu)
     }
     if do_cpu:
         out["cpu_baseline"] = cpu_prefill(layers[0], shape, bias.cpu().numpy(), cpu_seconds)
+    return out
+
+
+def ep_case(m, shape, K, W, stream, world, rank, dev, peaks):
+    """Config 5: EP_TOKENS tokens per step over `world` ranks, experts sharded evenly, device time max over ranks."""
+    T = EP_TOKENS // world
+    with torch.cuda.stream(stream):
+        layer = m.synth_layer(shape, seed=3000, stream=stream)  # same weights on every rank; each keeps its shard
+        hidden, attn = m.synth_activations(shape, T, seed=31 + rank, stream=stream)
+    normed = torch.zeros(T, shape.H, dtype=torch.int16, device=dev)
+    torch.cuda.synchronize()
+    hidden0 = hidden.clone()
+    if world == 1:
+        blk = m.MoeBlock(layer, T)
+        step = lambda i: blk.forward(hidden, attn, normed, stream=stream)  # noqa: E731
+        with torch.cuda.stream(stream):
+            for i in range(W):
+                step(i)
+        torch.cuda.synchronize()
+        ms, clk = timed(graph_plan(step, K, stream), stream, world, ClockSampler(dev))
+        how = "single GPU: moe_block_forward prefill path (CUDA graph)"
+        recv = None
+    else:
+        import mvcc_b200.ep as ep
+        st = ep.EpRank(layer, rank, world, T)
+        ex = ep.NcclExchange()
+        sizes = []
+        step = lambda i: sizes.append(ep.ep_step(st, ex, hidden, attn, normed, stream=stream))  # noqa: E731
+        for i in range(W):
+            step(i)
+        torch.cuda.synchronize()
+        sizes.clear()
+        clocks = ClockSampler(dev)
+        clocks.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        t0 = time.time()
+        e0.record(stream)
+        for i in range(K):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t1 = time.time()
+        barrier(world)
+        clocks.stop()
+        clk = clocks.summary(t0, t1)
+        ms = max_over_ranks(e0.elapsed_time(e1), world)
+        how = (f"mvcc_b200.ep: {shape.E // world} experts per rank; records exchanged with NCCL all_to_all_single "
+               "(counts, records, partial rows), one host read of the counts per step; shared expert on a side "
+               "stream")
+        recv = {"records_sent_per_step": float(np.mean([s for s, _ in sizes])),
+                "records_received_per_step": float(np.mean([r for _, r in sizes]))}
+        assert st.error_word() == 0
+    hidden.copy_(hidden0)
+    fl = prefill_flops(shape, EP_TOKENS)
+    tf = fl["block"] / (ms / K * 1e-3) / 1e12
+    out = {"workload": f"BASELINE config 5: {EP_TOKENS} tokens per step through one int4 G=64 MoE layer, experts "
+                       f"sharded over {world} GPU(s), {T} tokens per rank",
+           "value": EP_TOKENS * K / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / K, "steps": K,
+           "n_gpus": world, "scaling": "strong", "how": how,
+           "tflops": {"achieved_job": tf, "per_gpu": tf / world, "frac_per_gpu": tf / world / peaks["tf_sustained"],
+                      "peak_kind": f"{peaks['kind']} bf16 sustained", "flops_per_step": fl["block"]},
+           "gpu_launches_per_step_per_rank": launches_per_step(T) if world == 1 else 14,
+           "clocks": clk}
+    if recv:
+        out["exchange"] = recv
     return out
 
 
@@ -382,7 +458,7 @@ def b200_arm(args, rank, world, local):
         roof = {"kernel": "moe_fused_decode_kernel (the whole block in one cooperative launch)",
                 "bound": "hbm", "achieved": achieved, "peak": peaks["hbm"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm"], "peak_kind": peaks["kind"], "bytes_per_launch": ab["block"],
-                "us_per_launch": st[0], "traffic": None}
+                "us_per_launch": st[0], "traffic": NCU_TRAFFIC["fused_b1"] if B == 1 else None}
     else:
         fl = prefill_flops(shape, B)
         achieved = fl["gate_up"] / (st[1] * 1e-6) / 1e12
@@ -449,6 +525,9 @@ def b200_arm(args, rank, world, local):
         do_cpu = world == 1 and rank == 0 and not args.no_cpu
         result["prefill"] = prefill_case(m, shape, args.prefill_steps, W, stream, world, dev, peaks,
                                          args.cpu_seconds / 2, do_cpu)
+    if not args.no_ep and world <= 8 and shape.E % world == 0:
+        torch.cuda.empty_cache()
+        result["ep_prefill"] = ep_case(m, shape, args.ep_steps, W, stream, world, rank, dev, peaks)
     if world == 1 and rank == 0 and not args.no_cpu:
         with torch.cuda.stream(stream):
             l0 = m.synth_layer(shape, seed=1000, stream=stream)
@@ -554,6 +633,8 @@ def main():
                     help="decode layer copies cycled over (each 428 MB; the default keeps steps out of L2)")
     ap.add_argument("--prefill-steps", type=int, default=40)
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
+    ap.add_argument("--ep-steps", type=int, default=20)
+    ap.add_argument("--no-ep", action="store_true", help="skip the config-5 expert-parallel measurement")
     ap.add_argument("--quick", action="store_true", help="headline batch only (no decode_batches sweep)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)

@@ -13,7 +13,7 @@
 //               layout (cp.async.mbarrier.arrive.noinc on full[s]);
 //   warp 2      B producer, one lane: TMA tiles of the step's bf16 B rows into stage s, or of INT4 rows (rk
 //               k-steps of each row per box) into the raw ring (fullR) and, once per item, of the item's fp16 group
-//               scales; completion by transaction count (mbarrier expect_tx). No load uses cluster multicast;
+//               scales; completion by transaction count (mbarrier expect_tx). Every load targets this CTA's own shared memory only;
 //   warp 3      allocates TMEM (two accumulator buffers of BN fp32 columns) and, from one lane, issues the
 //               tcgen05.mma of each step (M=128, N=BN, K=16 x 4), committing to empty[s] and, after an item's last
 //               step, to acc_full[buffer];
@@ -100,7 +100,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
-// 2D TMA tile load into this CTA's shared memory, completion counted in bytes on mbar (no multicast).
+// 2D TMA tile load into this CTA's shared memory, completion counted in bytes on mbar (this CTA only).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* mbar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
