@@ -22,7 +22,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return warp_sum(t);
 }
 
-// Position of k in the permuted fp32 activation row: k = 32c + 8q + 4h + e -> ((2q + h) * NCH + c) * 4 + e.
 // Exclusive block-wide prefix sum of one int per thread (blockDim.x a multiple of 32, at most 1024); *total
 // receives the block's sum. sm: 32 ints of shared memory.
 __device__ __forceinline__ int block_excl_scan(int v, int* sm, int* total) {
@@ -51,6 +50,7 @@ __device__ __forceinline__ int block_excl_scan(int v, int* sm, int* total) {
   return before + x - v;
 }
 
+// Position of k in the permuted fp32 activation row: k = 32c + 8q + 4h + e -> ((2q + h) * NCH + c) * 4 + e.
 __device__ __forceinline__ int xperm(int k, int nch) {
   const int c = k >> 5, r = k & 31;
   return (((r >> 3) * 2 + ((r >> 2) & 1)) * nch + c) * 4 + (r & 3);

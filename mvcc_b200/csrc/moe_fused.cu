@@ -1,44 +1,60 @@
 // moe_fused.cu -- fused persistent decode kernel of the MoE block for T <= 8 tokens: one cooperative launch does
 // qwen.cu:429-448 end to end.
 //
-// One CTA per SM, 16 warps. The work is partitioned so that every SM streams about the same number of weight
-// bytes, and every byte is requested as soon as its dependency allows:
-//   start     cp.async of the routing-independent weights this CTA owns: router rows (router row r -> CTA r % G,
-//             the shared gate vector is row E), shared-expert gate/up row pairs (pair j -> CTA j % G) and the
-//             shared-expert down rows of the CTA's output rows [h0, h1);
+// One CTA per SM, 16 warps. Weight bytes move with bulk asynchronous copies (cp.async.bulk, completion counted on
+// shared-memory mbarriers) issued by one thread, a few large contiguous copies per CTA, so no warp stalls issuing
+// loads and every byte is requested as soon as its dependency allows:
+//   entry     bulk copies of the routing-independent weights this CTA owns: router rows (router row r -> CTA
+//             r % G; the shared gate vector is row E), shared-expert gate/up row pairs (pair j -> CTA j % G) and
+//             the shared-expert down rows of the CTA's output rows [h0, h1);
 //   phase R   RMSNorm of every token (every CTA, into shared memory), router logits of the CTA's rows -> global;
-//             arrive at grid barrier 1; compute the shared-expert gate/up pairs while the barrier settles; wait;
-//   phase G   every CTA runs the reference's top-k on all logits itself (no second round trip) and builds the
-//             unique-expert table in shared memory; each warp then streams its routed gate/up row pairs and its
-//             down-row batches through a private cp.async ring (loads run ahead of compute, across the barrier);
-//             `inter` -> global; arrive and wait at grid barrier 2;
+//             arrive at grid barrier 1; the shared-expert gate/up pairs while the barrier settles; wait;
+//   phase G   every CTA runs the reference's top-k on all logits itself (one warp per token, warp reductions) and
+//             one warp builds the unique-expert table; the CTA's share of the routed gate/up jobs (contiguous row
+//             ranges of each unique expert) and its down rows (rows [h0, h1) of every unique expert) form a list
+//             of chunks that stream through a ring of shared-memory stages: gate/up chunks are consumed one job
+//             per warp, `inter` -> global; the last warp to finish a stage refills it with the next chunk, so the
+//             down rows arrive while phase G still runs; grid barrier 2;
 //   phase D   stage every pair's `inter` and the shared `sinter`; each warp reduces one output row h over every
 //             unique expert (weighted per pair) and the shared expert, and applies the gated residual combine;
 //             the last CTA to finish (ticket) optionally applies the next layer's RMSNorm.
 // Grid barriers use a monotone 64-bit arrival counter in the workspace (each launch adds exactly 2 x G arrivals,
-// so the targets follow from its value at launch start) and bounded spins: after kSpinLimit polls a CTA records
-// MOE_ERR_BARRIER in the error word, drains its own copies and returns. The launch is cooperative, so all CTAs are
-// co-resident. Reductions and numerics are those of the three-kernel path (moe_decode.cu).
+// so the targets follow from its value at launch start) and bounded spins; stage waits are bounded by the global
+// timer. A wait that gives up records MOE_ERR_BARRIER in the error word; the CTA skips the remaining work, still
+// arrives at the grid barriers, and before returning waits (bounded) for every copy it issued. The launch is
+// cooperative, so all CTAs are co-resident. Per-job reductions and numerics are those of the three-kernel path
+// (moe_decode.cu).
 #include <algorithm>
 #include <cstring>
 
 #include "moe_device.cuh"
 #include "moe_fused.h"
+#include "moe_tc.cuh"
 
 namespace moe {
 
+using tc::fence_proxy_async_smem;
+using tc::mbar_fence_init;
+using tc::mbar_init;
+using tc::smem_u32;
+
 constexpr int kFW = 16;
 constexpr int kFThreads = kFW * 32;
-constexpr int kSgu = 4;                   // shared gate/up pairs per CTA (Is <= 4 x grid)
-constexpr int kRouterRows = 2;            // router rows per CTA (E + 1 <= 2 x grid)
-constexpr long long kSpinLimit = 1 << 21; // barrier polls (x ~100 ns) before giving up
+constexpr int kSgu = 4;                            // shared gate/up pairs per CTA (Is <= 4 x grid)
+constexpr int kRouterRows = 2;                     // router rows per CTA (E + 1 <= 2 x grid)
+constexpr int kMaxStages = 6;                      // ring stages
+constexpr int kMaxChunks = 96;                     // gate/up + down chunks of one CTA
+constexpr long long kSpinLimit = 1 << 21;          // grid-barrier polls (x ~100 ns) before giving up
+constexpr unsigned long long kWaitNs = 1000000000; // stage-barrier wait limit (1 s of global time)
 
 struct FusedArgs {
   BlockArgs a;
   unsigned long long* gbar;  // grid-barrier arrival counter
-  int slot_bytes;            // per-warp ring slot
-  int stages;                // ring slots per warp
-  int rows_per_cta;          // output rows h per CTA
+  int stages;                // ring stages
+  int stage_bytes;           // bytes per stage
+  int cjobs;                 // gate/up jobs (row pairs) per chunk, at most kFW
+  int kd;                    // experts per down chunk
+  int rows_per_cta;          // output rows h per CTA (at most kFW)
   int next_norm;             // apply the next layer's RMSNorm
 };
 
@@ -48,9 +64,10 @@ struct FusedSmem {
 };
 
 __host__ __device__ inline size_t f_align(size_t x) { return (x + 127) & ~(size_t)127; }
+__host__ __device__ inline int a16(int x) { return (x + 15) & ~15; }
 
 __host__ __device__ inline FusedSmem fused_smem(int T, int H, int TOPK, int I, int Is, int rows_per_cta,
-                                                 int slot_bytes, int stages) {
+                                                 int stage_bytes, int stages) {
   FusedSmem L;
   size_t o = 0;
   const size_t xs = (size_t)T * H * 4, inter = (size_t)T * TOPK * inter_stride(I) * 2;
@@ -60,31 +77,76 @@ __host__ __device__ inline FusedSmem fused_smem(int T, int H, int TOPK, int I, i
   L.sgu = o;    o = f_align(o + (size_t)kSgu * 2 * H * 2);
   L.sdn = o;    o = f_align(o + (size_t)rows_per_cta * Is * 2);
   L.acc = o;    o = f_align(o + (size_t)kFW * T * 32 * 4);
-  L.ring = o;   o = f_align(o + (size_t)kFW * stages * slot_bytes);
+  L.ring = o;   o = f_align(o + (size_t)stages * stage_bytes);
   L.total = o;
   return L;
 }
 
-__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gmem_src) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(gmem_src) : "memory");
+// Layout of one stage. Gate/up chunk of n <= C jobs: gate rows [C][H/2], up rows [C][H/2], then the gate and up
+// scale rows, each copied as the 16-byte aligned superset of its [n][H/G] fp16. Down chunk of n <= kd experts: rows
+// [kd][rpc][I/2], then per expert its scale rows [rpc][I/G] fp16 as an aligned superset.
+__host__ __device__ inline int gate_scale_region(int C, int H, int G) { return a16(C * (H / G) * 2) + 32; }
+__host__ __device__ inline int down_scale_region(int rpc, int I, int G) { return a16(rpc * (I / G) * 2) + 32; }
+__host__ __device__ inline int gate_stage_bytes(int C, int H, int G) {
+  return 2 * C * (H / 2) + 2 * gate_scale_region(C, H, G);
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-__device__ __forceinline__ void cp_wait_stages(int stages) {
-  switch (stages) {  // wait until at most stages - 1 groups are pending
-    case 1: cp_wait<0>(); break;
-    case 2: cp_wait<1>(); break;
-    case 3: cp_wait<2>(); break;
-    default: cp_wait<3>(); break;
-  }
+__host__ __device__ inline int down_stage_bytes(int kd, int rpc, int I, int G) {
+  return kd * rpc * (I / 2) + kd * down_scale_region(rpc, I, G);
 }
 
-// Copies `bytes` (a multiple of 16) from global to shared with the calling warp's lanes.
-__device__ __forceinline__ void warp_copy16(uint8_t* dst, const uint8_t* src, int bytes, int lane) {
-  for (int o = lane * 16; o < bytes; o += 32 * 16) cp_async16(dst + o, src + o);
+// ------------------------------------------------------------------ bulk copies and barriers
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(mbar))
+               : "memory");
 }
+__device__ __forceinline__ void expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(mbar)),
+      "r"(bytes)
+      : "memory");
+}
+// Bytes of the 16-byte aligned superset of [src, src + bytes), and the offset of src within it.
+__device__ __forceinline__ uint32_t span_bytes(const void* src, int bytes) {
+  const uintptr_t s = reinterpret_cast<uintptr_t>(src);
+  return (uint32_t)(((s + bytes + 15) & ~(uintptr_t)15) - (s & ~(uintptr_t)15));
+}
+__device__ __forceinline__ int span_delta(const void* src) { return (int)(reinterpret_cast<uintptr_t>(src) & 15); }
+__device__ __forceinline__ void bulk_span(void* dst, const void* src, int bytes, uint64_t* mbar) {
+  const uintptr_t s = reinterpret_cast<uintptr_t>(src);
+  bulk_g2s(dst, reinterpret_cast<const void*>(s & ~(uintptr_t)15), span_bytes(src, bytes), mbar);
+}
+
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Waits for phase `parity` of the mbarrier; false if kWaitNs of global time pass first.
+__device__ __forceinline__ bool bar_wait(uint64_t* mbar, uint32_t parity) {
+  const uint32_t addr = smem_u32(mbar);
+  unsigned long long t0 = 0;
+  for (int i = 0;; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 63) == 0) {
+      const unsigned long long t = gtime();
+      if (i == 0) t0 = t;
+      else if (t - t0 > kWaitNs) return false;
+    }
+  }
+}
+__device__ __forceinline__ int vload(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
   unsigned long long v;
@@ -111,85 +173,164 @@ __device__ __forceinline__ bool grid_wait(const unsigned long long* gbar, unsign
         ok = 0;
         break;
       }
-      __nanosleep(32);
+      __nanosleep(20);
     }
-    __threadfence();
     *ok_s = ok;
   }
   __syncthreads();
   return *ok_s != 0;
 }
 
-// The reference's top-k table built in shared memory (same rule and order as build_unique in moe_decode.cu).
-__device__ void table_smem(const int32_t* idx_s, int P, int E, int* cnt_s, int* start_s, int* uniq_s, int* uoff_s,
-                           int* upairs_s, int* ptok_s, int K, int* nuniq_s) {
-  const int tid = threadIdx.x;
-  for (int e = tid; e < E; e += blockDim.x) cnt_s[e] = 0;
-  __syncthreads();
-  for (int p = tid; p < P; p += blockDim.x) {
-    const int e = idx_s[p];
-    if (e >= 0 && e < E) atomicAdd(&cnt_s[e], 1);
-  }
-  __syncthreads();
-  if (tid < 32) {
-    const int lane = tid;
-    int nz = 0, np = 0;
-    for (int j = 0; j < 8; ++j) {
-      const int e = lane * 8 + j;
-      if (e < E && cnt_s[e] > 0) { ++nz; np += cnt_s[e]; }
-    }
-    int nz_ex = nz, np_ex = np;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int a1 = __shfl_up_sync(0xffffffffu, nz_ex, o), a2 = __shfl_up_sync(0xffffffffu, np_ex, o);
-      if (lane >= o) { nz_ex += a1; np_ex += a2; }
-    }
-    nz_ex -= nz;
-    np_ex -= np;
-    for (int j = 0; j < 8; ++j) {
-      const int e = lane * 8 + j;
-      if (e < E && cnt_s[e] > 0) {
-        uniq_s[nz_ex] = e;
-        uoff_s[nz_ex] = np_ex;
-        start_s[e] = np_ex;
-        ++nz_ex;
-        np_ex += cnt_s[e];
-      }
-    }
-    if (lane == 31) {
-      *nuniq_s = nz_ex;
-      uoff_s[nz_ex] = np_ex;
-    }
-  }
-  __syncthreads();
-  for (int p = tid; p < P; p += blockDim.x) {
-    const int e = idx_s[p];
-    if (e < 0 || e >= E) continue;
-    int rank = 0;
-    for (int q = 0; q < p; ++q) rank += (idx_s[q] == e);
-    upairs_s[start_s[e] + rank] = p;
-    ptok_s[start_s[e] + rank] = p / K;
-  }
-  __syncthreads();
+// ------------------------------------------------------------------ routing in one warp
+
+// Order-preserving 32-bit key of a float (larger float -> larger key); 0 is below every float's key.
+__device__ __forceinline__ uint32_t fkey(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-// One routed gate/up row pair (gate row i and up row I + i of expert e) from its ring slot, for every pair of
-// unique expert uix; same reduction as compute_routed in moe_decode.cu.
-__device__ __forceinline__ void fused_gate_job(const BlockArgs& a, const float* xs, const uint8_t* slot, int uix,
+// The reference's top-k rule (router_topk_kernel, kernels.cuh:774-809) over one token's logits: K rounds of argmax
+// by (value desc, index asc), weights exp(v - max) / sum over the picks. A round is a per-lane scan of its 8 values
+// and two warp reductions (redux.sync: max of the value key, then min of the index among the lanes holding it).
+__device__ void topk_warp_redux(const float* row, int E, int K, int32_t* idx_out, float* wts_out) {
+  const int lane = threadIdx.x & 31;
+  uint32_t key[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + i * 32;
+    key[i] = fkey(e < E ? __ldcg(row + e) : -1e30f);
+  }
+  float pv[8];
+  int pi[8];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    uint32_t bk = 0;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (key[i] > bk) { bk = key[i]; bi = lane + i * 32; }
+    const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+    const int wi = (int)__reduce_min_sync(0xffffffffu, bk == mk ? (uint32_t)bi : 0x7fffffffu);
+    pv[kk] = fkey_inv(mk);
+    pi[kk] = wi;
+    if (kk < K) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (lane + i * 32 == wi) key[i] = 0;
+    }
+  }
+  float mx = pv[0];
+#pragma unroll
+  for (int kk = 1; kk < 8; ++kk)
+    if (kk < K) mx = fmaxf(mx, pv[kk]);
+  float den = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    pv[kk] = __expf(pv[kk] - mx);
+    if (kk < K) den += pv[kk];
+  }
+  float myw = 0.f;
+  int myi = 0;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    if (lane == kk) { myw = pv[kk]; myi = pi[kk]; }
+  if (lane < K) {
+    idx_out[lane] = myi;
+    wts_out[lane] = myw / den;
+  }
+}
+
+// The unique-expert table in one warp (same contents and order as build_unique in moe_decode.cu): the P <= 64 pairs
+// sorted by (expert, pair index) with a bitonic network over 64 keys (element i in lane i % 32, register i / 32);
+// uniq[u] the ascending experts, uoff[u] their first sorted position, upairs/ptok the sorted pairs and their tokens.
+// Invalid indices sort last and are dropped.
+__device__ void table_warp(const int32_t* idx_s, int P, int E, int K, int* uniq_s, int* uoff_s, int* upairs_s,
+                           int* ptok_s, int* nuniq_s) {
+  const int lane = threadIdx.x & 31;
+  uint32_t v0, v1;
+  {
+    const int e0 = lane < P ? idx_s[lane] : -1, e1 = lane + 32 < P ? idx_s[lane + 32] : -1;
+    v0 = (lane < P && e0 >= 0 && e0 < E) ? ((uint32_t)e0 << 6) | (uint32_t)lane : 0xffffffffu;
+    v1 = (lane + 32 < P && e1 >= 0 && e1 < E) ? ((uint32_t)e1 << 6) | (uint32_t)(lane + 32) : 0xffffffffu;
+  }
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      uint32_t o0, o1;
+      if (j == 32) {
+        o0 = v1;
+        o1 = v0;
+      } else {
+        o0 = __shfl_xor_sync(0xffffffffu, v0, j);
+        o1 = __shfl_xor_sync(0xffffffffu, v1, j);
+      }
+      const int i0 = lane, i1 = lane + 32;
+      const bool keep_lo0 = ((i0 & j) == 0) == ((i0 & k) == 0), keep_lo1 = ((i1 & j) == 0) == ((i1 & k) == 0);
+      v0 = keep_lo0 ? min(v0, o0) : max(v0, o0);
+      v1 = keep_lo1 ? min(v1, o1) : max(v1, o1);
+    }
+  }
+  // v0 / v1 hold sorted positions lane / lane + 32
+  const bool valid0 = v0 != 0xffffffffu, valid1 = v1 != 0xffffffffu;
+  const int e0 = (int)(v0 >> 6), e1 = (int)(v1 >> 6);
+  int prev0 = __shfl_up_sync(0xffffffffu, e0, 1);
+  int prev1 = __shfl_up_sync(0xffffffffu, e1, 1);
+  const int last0 = __shfl_sync(0xffffffffu, e0, 31);
+  if (lane == 0) {
+    prev0 = -1;
+    prev1 = last0;
+  }
+  const bool f0 = valid0 && e0 != prev0, f1 = valid1 && e1 != prev1;
+  const uint32_t b0 = __ballot_sync(0xffffffffu, f0), b1 = __ballot_sync(0xffffffffu, f1);
+  const uint32_t le = 0xffffffffu >> (31 - lane);
+  const int u0 = __popc(b0 & le) - 1, u1 = __popc(b0) + __popc(b1 & le) - 1;
+  const int nvalid = __popc(__ballot_sync(0xffffffffu, valid0)) + __popc(__ballot_sync(0xffffffffu, valid1));
+  if (f0) {
+    uniq_s[u0] = e0;
+    uoff_s[u0] = lane;
+  }
+  if (f1) {
+    uniq_s[u1] = e1;
+    uoff_s[u1] = lane + 32;
+  }
+  if (valid0) {
+    const int p = (int)(v0 & 63);
+    upairs_s[lane] = p;
+    ptok_s[lane] = p / K;
+  }
+  if (valid1) {
+    const int p = (int)(v1 & 63);
+    upairs_s[lane + 32] = p;
+    ptok_s[lane + 32] = p / K;
+  }
+  if (lane == 0) {
+    const int U = __popc(b0) + __popc(b1);
+    *nuniq_s = U;
+    uoff_s[U] = nvalid;
+  }
+}
+
+// ------------------------------------------------------------------ per-job arithmetic (three-kernel path order)
+
+// One routed gate/up row pair (gate row i and up row I + i of unique expert uix) for every pair routed to it; same
+// reduction as compute_routed in moe_decode.cu.
+__device__ __forceinline__ void fused_gate_job(const BlockArgs& a, const float* xs, const uint8_t* grow,
+                                               const uint8_t* urow, const uint16_t* gsc, const uint16_t* usc, int uix,
                                                int i, const int* uoff_s, const int* upairs_s, const int* ptok_s,
                                                int gshift, const Nib8Magic& M) {
   const int lane = threadIdx.x & 31;
   const int H = a.w.H, I = a.w.I, nch = H >> 5;
-  const int half = H >> 1, sgroups = H / a.w.G;
-  const uint16_t* gsc = reinterpret_cast<const uint16_t*>(slot + H);
-  const uint16_t* usc = gsc + sgroups;
   for (int p = uoff_s[uix]; p < uoff_s[uix + 1]; ++p) {
     const int pair = upairs_s[p];
     const float* xt = xs + ptok_s[p] * H;
     float g = 0.f, u = 0.f;
     for (int c = lane; c < nch; c += 32) {
-      const uint4 gq = *reinterpret_cast<const uint4*>(slot + c * 16);
-      const uint4 uq = *reinterpret_cast<const uint4*>(slot + half + c * 16);
+      const uint4 gq = *reinterpret_cast<const uint4*>(grow + c * 16);
+      const uint4 uq = *reinterpret_cast<const uint4*>(urow + c * 16);
       const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w}, uw[4] = {uq.x, uq.y, uq.z, uq.w};
       Nib8Acc ag, au;
       nib8_zero(ag);
@@ -211,6 +352,12 @@ __device__ __forceinline__ void fused_gate_job(const BlockArgs& a, const float* 
   }
 }
 
+// Chunk list entry: kind 0 = gate/up jobs i0 .. i0 + n - 1 of unique expert a; kind 1 = down rows of unique experts
+// a .. a + n - 1.
+struct Chunk {
+  int kind, a, i0, n;
+};
+
 __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArgs f) {
   extern __shared__ __align__(128) uint8_t smem[];
   const BlockArgs& a = f.a;
@@ -218,51 +365,68 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   const int T = a.T, H = a.w.H, E = a.w.E, K = a.w.TOPK, I = a.w.I, Is = a.w.Is, G = a.w.G;
   const int P = T * K, nch = H >> 5, nvs = Is >> 3;
   const int grid = gridDim.x, cta = blockIdx.x;
-  const FusedSmem L = fused_smem(T, H, K, I, Is, f.rows_per_cta, f.slot_bytes, f.stages);
+  const int S = f.stages, SB = f.stage_bytes, C = f.cjobs, rpc = f.rows_per_cta;
+  const FusedSmem L = fused_smem(T, H, K, I, Is, rpc, SB, S);
   float* xs = reinterpret_cast<float*>(smem + L.xs);
   uint16_t* sinter_s = reinterpret_cast<uint16_t*>(smem + L.sinter);
   uint8_t* router_s = smem + L.router;
   uint8_t* sgu_s = smem + L.sgu;
   uint8_t* sdn_s = smem + L.sdn;
   float* acc_s = reinterpret_cast<float*>(smem + L.acc);
-  uint8_t* ring = smem + L.ring + (size_t)warp * f.stages * f.slot_bytes;
+  uint8_t* ring = smem + L.ring;
+  __shared__ __align__(8) uint64_t full_b[kMaxStages];
+  __shared__ __align__(8) uint64_t rbar, sbar;
+  __shared__ int cnt_s[kMaxStages], issued_s[kMaxStages];
+  __shared__ Chunk chunk_s[kMaxChunks];
   __shared__ float red[32];
   __shared__ int32_t idx_s[64];
   __shared__ float wts_s[64];
-  __shared__ int cnt_s[256], start_s[256], uniq_s[256], uoff_s[257], upairs_s[64], ptok_s[64];
-  __shared__ int nuniq_s, ok_s, is_last;
+  __shared__ int uniq_s[64], uoff_s[65], upairs_s[64], ptok_s[64];
+  __shared__ int nuniq_s, nchunks_s, ngate_s, ok_s, is_last, abort_s;
   __shared__ unsigned long long base_s;
-  const int h0 = cta * f.rows_per_cta, h1 = min(H, h0 + f.rows_per_cta);
-  if (tid == 0) base_s = (ld_acquire_u64(f.gbar) / grid) * grid;
-
-  // ---- start: routing-independent weights of this CTA (one cp.async group per thread)
+  const int h0 = cta * rpc, h1 = min(H, h0 + rpc);
+  const int rowb = H >> 1, sgb = (H / G) * 2;   // gate/up: row bytes, scale bytes per row
+  const int drowb = I >> 1, dsb = (I / G) * 2;  // down: row bytes, scale bytes per row
   const int nrows = E + 1;
-  for (int r = 0; r < kRouterRows; ++r) {
-    const int row = cta + r * grid;
-    if (row < nrows) {
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(row < E ? a.w.router + (int64_t)row * H : a.w.shared_gate);
-      for (int o = tid * 16; o < H * 2; o += kFThreads * 16) cp_async16(router_s + (size_t)r * H * 2 + o, src + o);
+  const uint8_t* gscale = reinterpret_cast<const uint8_t*>(a.w.exp_gu_s);
+  const uint8_t* dscale = reinterpret_cast<const uint8_t*>(a.w.exp_dn_s);
+
+  if (tid == 0) {
+    base_s = (ld_acquire_u64(f.gbar) / grid) * grid;
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_b[s], 1);
+      cnt_s[s] = 0;
+      issued_s[s] = 0;
     }
-  }
-  cp_commit();  // group: router rows
-  for (int r = 0; r < kSgu; ++r) {
-    const int j = cta + r * grid;
-    if (j < Is) {
-      const uint8_t* gsrc = reinterpret_cast<const uint8_t*>(a.w.shared_gate_up + (int64_t)j * H);
-      const uint8_t* usrc = reinterpret_cast<const uint8_t*>(a.w.shared_gate_up + (int64_t)(Is + j) * H);
-      uint8_t* dst = sgu_s + (size_t)r * 2 * H * 2;
-      for (int o = tid * 16; o < H * 2; o += kFThreads * 16) {
-        cp_async16(dst + o, gsrc + o);
-        cp_async16(dst + H * 2 + o, usrc + o);
+    mbar_init(&rbar, 1);
+    mbar_init(&sbar, 1);
+    abort_s = 0;
+    mbar_fence_init();
+    // ---- entry: routing-independent weights of this CTA
+    uint32_t tx = 0;
+    for (int r = 0; r < kRouterRows; ++r) tx += (cta + r * grid < nrows) ? H * 2 : 0;
+    expect_tx(&rbar, tx);
+    for (int r = 0; r < kRouterRows; ++r) {
+      const int row = cta + r * grid;
+      if (row < nrows)
+        bulk_g2s(router_s + (size_t)r * H * 2, row < E ? a.w.router + (int64_t)row * H : a.w.shared_gate, H * 2,
+                 &rbar);
+    }
+    tx = 0;
+    for (int r = 0; r < kSgu; ++r) tx += (cta + r * grid < Is) ? 2 * H * 2 : 0;
+    tx += h0 < h1 ? (h1 - h0) * Is * 2 : 0;
+    expect_tx(&sbar, tx);
+    for (int r = 0; r < kSgu; ++r) {
+      const int j = cta + r * grid;
+      if (j < Is) {
+        uint8_t* dst = sgu_s + (size_t)r * 2 * H * 2;
+        bulk_g2s(dst, a.w.shared_gate_up + (int64_t)j * H, H * 2, &sbar);
+        bulk_g2s(dst + H * 2, a.w.shared_gate_up + (int64_t)(Is + j) * H, H * 2, &sbar);
       }
     }
+    if (h0 < h1) bulk_g2s(sdn_s, a.w.shared_down + (int64_t)h0 * Is, (h1 - h0) * Is * 2, &sbar);
   }
-  if (h0 < h1) {
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(a.w.shared_down + (int64_t)h0 * Is);
-    const int bytes = (h1 - h0) * Is * 2;
-    for (int o = tid * 16; o < bytes; o += kFThreads * 16) cp_async16(sdn_s + o, src + o);
-  }
-  cp_commit();  // group: shared-expert rows
+  __syncthreads();
 
   // ---- phase R: RMSNorm of every token into xs (fp32, permuted); CTA 0 writes `normed`
   for (int t = 0; t < T; ++t) {
@@ -302,69 +466,165 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       }
     }
   }
-  cp_wait<1>();  // router rows landed; shared-expert rows may still be in flight
   __syncthreads();
 
   // Router rows (warps 0..1): gemv_bf16 order per lane over its 32-k chunks, butterfly sum.
   if (warp < kRouterRows) {
     const int row = cta + warp * grid;
     if (row < nrows) {
-      const uint8_t* wrow = router_s + (size_t)warp * H * 2;
-      for (int t = 0; t < T; ++t) {
-        const float4* xs4 = reinterpret_cast<const float4*>(xs + t * H);
-        float acc = 0.f;
-        for (int c = lane; c < nch; c += 32) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float x[8];
-            x_word(xs4, nch, c, q, x);
-            acc = dot_bf16_word(*reinterpret_cast<const uint4*>(wrow + c * 64 + q * 16), x, acc);
-          }
-        }
-        acc = warp_sum(acc);
+      const bool ok = __all_sync(0xffffffffu, bar_wait(&rbar, 0));
+      if (!ok) {
         if (lane == 0) {
-          if (row < E) a.logits[(int64_t)t * E + row] = a.w.router_bias ? acc + a.w.router_bias[row] : acc;
-          else a.gate[t] = sigmoid(acc);
+          atomicOr(a.err, (uint32_t)MOE_ERR_BARRIER);
+          abort_s = 1;
+        }
+      } else {
+        const uint8_t* wrow = router_s + (size_t)warp * H * 2;
+        for (int t = 0; t < T; ++t) {
+          const float4* xs4 = reinterpret_cast<const float4*>(xs + t * H);
+          float acc = 0.f;
+          for (int c = lane; c < nch; c += 32) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float x[8];
+              x_word(xs4, nch, c, q, x);
+              acc = dot_bf16_word(*reinterpret_cast<const uint4*>(wrow + c * 64 + q * 16), x, acc);
+            }
+          }
+          acc = warp_sum(acc);
+          if (lane == 0) {
+            if (row < E) a.logits[(int64_t)t * E + row] = a.w.router_bias ? acc + a.w.router_bias[row] : acc;
+            else a.gate[t] = sigmoid(acc);
+          }
         }
       }
     }
   }
   grid_arrive(f.gbar);
-  cp_wait<0>();  // shared-expert rows
-  __syncthreads();
 
   // Shared-expert gate/up pairs of this CTA while the router barrier settles (warps 2..5).
   if (warp >= 2 && warp < 2 + kSgu) {
     const int r = warp - 2, j = cta + r * grid;
     if (j < Is) {
-      const uint8_t* grow = sgu_s + (size_t)r * 2 * H * 2;
-      const uint8_t* urow = grow + H * 2;
-      for (int t = 0; t < T; ++t) {
-        const float4* xs4 = reinterpret_cast<const float4*>(xs + t * H);
-        float g = 0.f, u = 0.f;
-        for (int c = lane; c < nch; c += 32) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float x[8];
-            x_word(xs4, nch, c, q, x);
-            g = dot_bf16_word(*reinterpret_cast<const uint4*>(grow + c * 64 + q * 16), x, g);
-            u = dot_bf16_word(*reinterpret_cast<const uint4*>(urow + c * 64 + q * 16), x, u);
-          }
+      const bool ok = __all_sync(0xffffffffu, bar_wait(&sbar, 0));
+      if (!ok) {
+        if (lane == 0) {
+          atomicOr(a.err, (uint32_t)MOE_ERR_BARRIER);
+          abort_s = 1;
         }
-        g = warp_sum(g);
-        u = warp_sum(u);
-        if (lane == 0) a.sinter[(int64_t)t * Is + j] = f2bf(silu(bf2f(f2bf(g))) * bf2f(f2bf(u)));
+      } else {
+        const uint8_t* grow = sgu_s + (size_t)r * 2 * H * 2;
+        const uint8_t* urow = grow + H * 2;
+        for (int t = 0; t < T; ++t) {
+          const float4* xs4 = reinterpret_cast<const float4*>(xs + t * H);
+          float g = 0.f, u = 0.f;
+          for (int c = lane; c < nch; c += 32) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float x[8];
+              x_word(xs4, nch, c, q, x);
+              g = dot_bf16_word(*reinterpret_cast<const uint4*>(grow + c * 64 + q * 16), x, g);
+              u = dot_bf16_word(*reinterpret_cast<const uint4*>(urow + c * 64 + q * 16), x, u);
+            }
+          }
+          g = warp_sum(g);
+          u = warp_sum(u);
+          if (lane == 0) a.sinter[(int64_t)t * Is + j] = f2bf(silu(bf2f(f2bf(g))) * bf2f(f2bf(u)));
+        }
       }
     }
   }
   const unsigned long long base = base_s;
-  if (!grid_wait(f.gbar, base + grid, a.err, &ok_s)) return;
+  if (!grid_wait(f.gbar, base + grid, a.err, &ok_s) && tid == 0) abort_s = 1;
 
-  // ---- phase G: top-k per token (warp t), unique-expert table, routed gate/up through the per-warp rings
-  if (warp < T) topk_warp(a.logits + (int64_t)warp * E, E, K, idx_s + warp * K, wts_s + warp * K);
+  // ---- phase G: top-k per token (warp t), unique-expert table and chunk list (warp 0)
+  if (warp < T) topk_warp_redux(a.logits + (int64_t)warp * E, E, K, idx_s + warp * K, wts_s + warp * K);
   __syncthreads();
-  table_smem(idx_s, P, E, cnt_s, start_s, uniq_s, uoff_s, upairs_s, ptok_s, K, &nuniq_s);
-  const int U = nuniq_s;
+  if (warp == 0) {
+    table_warp(idx_s, P, E, K, uniq_s, uoff_s, upairs_s, ptok_s, &nuniq_s);
+    __syncwarp();
+    if (lane == 0) {
+      const int U = nuniq_s, J = U * I;
+      const int cj0 = (int)((int64_t)cta * J / grid), cj1 = (int)((int64_t)(cta + 1) * J / grid);
+      int n = 0;
+      for (int j = cj0; j < cj1 && n < kMaxChunks;) {
+        const int uix = j / I, i0 = j - uix * I;
+        const int m = min(C, min(cj1 - j, I - i0));
+        chunk_s[n++] = Chunk{0, uix, i0, m};
+        j += m;
+      }
+      ngate_s = n;
+      if (h0 < h1)
+        for (int b = 0; b < U && n < kMaxChunks; b += f.kd) chunk_s[n++] = Chunk{1, b, 0, min(f.kd, U - b)};
+      nchunks_s = n;
+    }
+  }
+  __syncthreads();
+  const int U = nuniq_s, nchunks = nchunks_s, ngate = ngate_s;
+
+  // Issues chunk c into stage c % S (one thread).
+  auto issue = [&](int c) {
+    const int s = c % S;
+    uint8_t* st = ring + (size_t)s * SB;
+    const Chunk ch = chunk_s[c];
+    if (ch.kind == 0) {
+      const int64_t g0 = (int64_t)uniq_s[ch.a] * 2 * I + ch.i0, u0 = g0 + I;
+      const uint32_t tx = (uint32_t)(2 * ch.n * rowb) + span_bytes(gscale + g0 * sgb, ch.n * sgb) +
+                          span_bytes(gscale + u0 * sgb, ch.n * sgb);
+      expect_tx(&full_b[s], tx);
+      bulk_g2s(st, a.w.exp_gu_q + g0 * rowb, ch.n * rowb, &full_b[s]);
+      bulk_g2s(st + C * rowb, a.w.exp_gu_q + u0 * rowb, ch.n * rowb, &full_b[s]);
+      bulk_span(st + 2 * C * rowb, gscale + g0 * sgb, ch.n * sgb, &full_b[s]);
+      bulk_span(st + 2 * C * rowb + gate_scale_region(C, H, G), gscale + u0 * sgb, ch.n * sgb, &full_b[s]);
+    } else {
+      const int nr = h1 - h0;
+      uint32_t tx = 0;
+      for (int b = 0; b < ch.n; ++b) {
+        const int64_t r0 = (int64_t)uniq_s[ch.a + b] * H + h0;
+        tx += (uint32_t)(nr * drowb) + span_bytes(dscale + r0 * dsb, nr * dsb);
+      }
+      expect_tx(&full_b[s], tx);
+      for (int b = 0; b < ch.n; ++b) {
+        const int64_t r0 = (int64_t)uniq_s[ch.a + b] * H + h0;
+        bulk_g2s(st + (size_t)b * rpc * drowb, a.w.exp_dn_q + r0 * drowb, nr * drowb, &full_b[s]);
+        bulk_span(st + (size_t)f.kd * rpc * drowb + (size_t)b * down_scale_region(rpc, I, G), dscale + r0 * dsb,
+                  nr * dsb, &full_b[s]);
+      }
+    }
+    issued_s[s] += 1;
+  };
+  // Called by every warp once it is done with chunk c: the last of the kFW warps refills the stage with chunk c + S.
+  auto release = [&](int c) {
+    __syncwarp();
+    if (lane == 0) {
+      const int s = c % S;
+      __threadfence_block();
+      const int old = atomicAdd(&cnt_s[s], 1);
+      if (old == kFW - 1) {
+        cnt_s[s] = 0;
+        __threadfence_block();
+        if (c + S < nchunks && !vload(&abort_s)) {
+          fence_proxy_async_smem();
+          issue(c + S);
+        }
+      }
+    }
+    __syncwarp();
+  };
+  // Waits for chunk c's bytes (every lane); false, and the CTA aborts, if the wait gives up.
+  auto wait_chunk = [&](int c) -> bool {
+    const bool ok = __all_sync(0xffffffffu, bar_wait(&full_b[c % S], (uint32_t)((c / S) & 1)));
+    if (!ok && lane == 0) {
+      atomicOr(a.err, (uint32_t)MOE_ERR_BARRIER);
+      abort_s = 1;
+    }
+    return ok;
+  };
+
+  if (tid == 0 && !abort_s) {
+    fence_proxy_async_smem();
+    for (int c = 0; c < min(S, nchunks); ++c) issue(c);
+  }
   if (cta == 0) {
     for (int p = tid; p < P; p += kFThreads) {
       a.idx[p] = idx_s[p];
@@ -375,70 +635,38 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     for (int u = tid; u <= U; u += kFThreads) a.uoff[u] = uoff_s[u];
     if (tid == 0) *a.nuniq = U;
   }
+  __syncthreads();
 
-  // This warp's items: gate/up jobs [g0, g1) of the U x I job space, then the down-row batches of row hw.
-  const int J = U * I;
-  const int cj0 = (int)((int64_t)cta * J / grid), cj1 = (int)((int64_t)(cta + 1) * J / grid);
-  const int g0 = cj0 + (int)((int64_t)warp * (cj1 - cj0) / kFW), g1 = cj0 + (int)((int64_t)(warp + 1) * (cj1 - cj0) / kFW);
-  const int ng = g1 - g0;
-  const int hw = h0 + warp;
-  const int nd = hw < h1 ? (U + 7) / 8 : 0;
-  const int n_items = ng + nd;
-  const int S = f.stages, SB = f.slot_bytes;
-  const int gshift = __ffs(G) - 6, dshift = __ffs(G) - 5;
-  const int rowb = H >> 1, sgb = (H / G) * 2;      // gate/up job: row bytes, scale bytes per row
-  const int drowb = I >> 1, dsb = (I / G) * 2;     // down: row bytes, scale bytes per row
-
-  auto issue = [&](int it) {
-    uint8_t* slot = ring + (size_t)(it % S) * SB;
-    if (it < ng) {
-      const int j = g0 + it, uix = j / I, i = j - uix * I, e = uniq_s[uix];
-      const uint8_t* gq = a.w.exp_gu_q + ((int64_t)e * 2 * I + i) * rowb;
-      const uint8_t* gs = reinterpret_cast<const uint8_t*>(a.w.exp_gu_s + ((int64_t)e * 2 * I + i) * (H / G));
-      warp_copy16(slot, gq, rowb, lane);
-      warp_copy16(slot + rowb, gq + (int64_t)I * rowb, rowb, lane);
-      warp_copy16(slot + 2 * rowb, gs, sgb, lane);
-      warp_copy16(slot + 2 * rowb + sgb, gs + (int64_t)I * sgb, sgb, lane);
-    } else {
-      const int b0 = (it - ng) * 8;
-      for (int b = 0; b < 8 && b0 + b < U; ++b) {
-        const int e = uniq_s[b0 + b];
-        warp_copy16(slot + b * drowb, a.w.exp_dn_q + ((int64_t)e * H + hw) * drowb, drowb, lane);
-        const uint8_t* sc =
-            reinterpret_cast<const uint8_t*>(a.w.exp_dn_s + ((int64_t)e * H + hw) * (I / G));
-        uint8_t* sdst = slot + 8 * drowb + b * dsb;
-        if (dsb >= 16) warp_copy16(sdst, sc, dsb, lane);
-        else if (lane == 0) cp_async8(sdst, sc);
-      }
-    }
-  };
-
-  for (int s = 0; s < S; ++s) {
-    if (s < n_items) issue(s);
-    cp_commit();
-  }
+  // Routed gate/up: job w of each gate/up chunk on warp w.
   const Nib8Magic M = nib8_magic();
-  for (int it = 0; it < ng; ++it) {
-    cp_wait_stages(S);
-    __syncwarp();
-    const int j = g0 + it, uix = j / I, i = j - uix * I;
-    fused_gate_job(a, xs, ring + (size_t)(it % S) * SB, uix, i, uoff_s, upairs_s, ptok_s, gshift, M);
-    __syncwarp();
-    if (it + S < n_items) issue(it + S);
-    cp_commit();
+  const int gshift = __ffs(G) - 6, dshift = __ffs(G) - 5;
+  bool live = !vload(&abort_s);
+  for (int c = 0; c < ngate; ++c) {
+    if (live) live = wait_chunk(c);
+    const Chunk ch = chunk_s[c];
+    if (live && warp < ch.n) {
+      const uint8_t* st = ring + (size_t)(c % S) * SB;
+      const int64_t g0 = (int64_t)uniq_s[ch.a] * 2 * I + ch.i0;
+      const uint8_t* gsc = st + 2 * C * rowb + span_delta(gscale + g0 * sgb) + warp * sgb;
+      const uint8_t* usc = st + 2 * C * rowb + gate_scale_region(C, H, G) + span_delta(gscale + (g0 + I) * sgb) +
+                           warp * sgb;
+      fused_gate_job(a, xs, st + warp * rowb, st + (C + warp) * rowb, reinterpret_cast<const uint16_t*>(gsc),
+                     reinterpret_cast<const uint16_t*>(usc), ch.a, ch.i0 + warp, uoff_s, upairs_s, ptok_s, gshift,
+                     M);
+    }
+    release(c);
   }
   grid_arrive(f.gbar);
-  if (!grid_wait(f.gbar, base + 2 * (unsigned long long)grid, a.err, &ok_s)) {
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    return;
-  }
+  if (!grid_wait(f.gbar, base + 2 * (unsigned long long)grid, a.err, &ok_s) && tid == 0) abort_s = 1;
+  __syncthreads();
 
-  // ---- phase D: stage inter (bf16, permuted) and sinter; reduce this warp's output row
+  // ---- phase D: stage inter (bf16, permuted) and sinter; reduce this warp's output row over the down chunks
   const int nchd = I >> 4, Ld = min(32, nchd), PI = inter_stride(I);
   uint16_t* inter_s = reinterpret_cast<uint16_t*>(smem + L.xs);
   for (int idx = tid; idx < P * I / 8; idx += kFThreads) {
     const int p = (idx * 8) / I, k = idx * 8 - p * I;
-    *reinterpret_cast<uint4*>(inter_s + (size_t)p * PI + iperm(k, Ld)) = __ldcg(reinterpret_cast<const uint4*>(a.inter) + idx);
+    *reinterpret_cast<uint4*>(inter_s + (size_t)p * PI + iperm(k, Ld)) =
+        __ldcg(reinterpret_cast<const uint4*>(a.inter) + idx);
   }
   for (int idx = tid; idx < T * Is / 8; idx += kFThreads)
     reinterpret_cast<uint4*>(sinter_s)[idx] = __ldcg(reinterpret_cast<const uint4*>(a.sinter) + idx);
@@ -446,40 +674,44 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
 
   float* acc_w = acc_s + (size_t)warp * T * 32;
   for (int t = 0; t < T; ++t) acc_w[t * 32 + lane] = 0.f;
-  for (int it = ng; it < n_items; ++it) {
-    cp_wait_stages(S);
-    __syncwarp();
-    const uint8_t* slot = ring + (size_t)(it % S) * SB;
-    const int b0 = (it - ng) * 8;
-    for (int b = 0; b < 8 && b0 + b < U; ++b) {
-      const uint8_t* wr = slot + b * drowb;
-      const uint16_t* sc = reinterpret_cast<const uint16_t*>(slot + 8 * drowb + b * dsb);
-      for (int p = uoff_s[b0 + b]; p < uoff_s[b0 + b + 1]; ++p) {
-        const int pair = upairs_s[p];
-        const uint8_t* xr = reinterpret_cast<const uint8_t*>(inter_s + (size_t)pair * PI);
-        float part = 0.f;
-        for (int c = lane; c < nchd; c += 32) {
-          const int j = c >> 5;
-          const uint2 wq = *reinterpret_cast<const uint2*>(wr + c * 8);
-          u64 x01, x23, x45, x67;
-          Nib8Acc A;
-          nib8_zero(A);
-          inter_pairs<false>(xr + (size_t)((j * 2) * Ld + lane) * 16, x01, x23, x45, x67);
-          nib8x2(wq.x, x01, x23, x45, x67, M, A);
-          inter_pairs<false>(xr + (size_t)((j * 2 + 1) * Ld + lane) * 16, x01, x23, x45, x67);
-          nib8x2(wq.y, x01, x23, x45, x67, M, A);
-          part = fmaf(nib8_fold(A), h2f(sc[c >> dshift]), part);
+  const int hw = h0 + warp;
+  live = !vload(&abort_s);
+  for (int c = ngate; c < nchunks; ++c) {
+    if (live) live = wait_chunk(c);
+    const Chunk ch = chunk_s[c];
+    if (live && hw < h1) {
+      const uint8_t* st = ring + (size_t)(c % S) * SB;
+      for (int b = 0; b < ch.n; ++b) {
+        const int uix = ch.a + b;
+        const int64_t r0 = (int64_t)uniq_s[uix] * H + h0;
+        const uint8_t* wr = st + ((size_t)b * rpc + warp) * drowb;
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(
+            st + (size_t)f.kd * rpc * drowb + (size_t)b * down_scale_region(rpc, I, G) + span_delta(dscale + r0 * dsb) +
+            warp * dsb);
+        for (int p = uoff_s[uix]; p < uoff_s[uix + 1]; ++p) {
+          const int pair = upairs_s[p];
+          const uint8_t* xr = reinterpret_cast<const uint8_t*>(inter_s + (size_t)pair * PI);
+          float part = 0.f;
+          for (int cc = lane; cc < nchd; cc += 32) {
+            const int j = cc >> 5;
+            const uint2 wq = *reinterpret_cast<const uint2*>(wr + cc * 8);
+            u64 x01, x23, x45, x67;
+            Nib8Acc A;
+            nib8_zero(A);
+            inter_pairs<false>(xr + (size_t)((j * 2) * Ld + lane) * 16, x01, x23, x45, x67);
+            nib8x2(wq.x, x01, x23, x45, x67, M, A);
+            inter_pairs<false>(xr + (size_t)((j * 2 + 1) * Ld + lane) * 16, x01, x23, x45, x67);
+            nib8x2(wq.y, x01, x23, x45, x67, M, A);
+            part = fmaf(nib8_fold(A), h2f(sc[cc >> dshift]), part);
+          }
+          float* slotacc = acc_w + ptok_s[p] * 32 + lane;
+          *slotacc = fmaf(wts_s[pair], part, *slotacc);
         }
-        float* slotacc = acc_w + ptok_s[p] * 32 + lane;
-        *slotacc = fmaf(wts_s[pair], part, *slotacc);
       }
     }
-    __syncwarp();
-    if (it + S < n_items) issue(it + S);
-    cp_commit();
+    release(c);
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  if (hw < h1) {
+  if (live && hw < h1 && __all_sync(0xffffffffu, bar_wait(&sbar, 0))) {
     float routed_t = 0.f, shared_t = 0.f;
     for (int t = 0; t < T; ++t) {
       const float v = warp_sum(acc_w[t * 32 + lane]);
@@ -511,7 +743,16 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       a.hidden[o] = f.next_norm ? fmaf(g, shared_t, hh + routed_t) : hh + fmaf(g, shared_t, routed_t);
     }
   }
-  if (!f.next_norm) return;
+  // No copy may still be landing when the CTA exits: wait (bounded) for the last chunk issued to every stage and
+  // for the entry copies (immediate on the normal path).
+  __syncthreads();
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s)
+      if (issued_s[s] > 0) bar_wait(&full_b[s], (uint32_t)((issued_s[s] - 1) & 1));
+    bar_wait(&rbar, 0);
+    bar_wait(&sbar, 0);
+  }
+  if (!f.next_norm || vload(&abort_s)) return;
   // Next layer's RMSNorm: the last CTA to finish (shared_gate_combine_rmsnorm_kernel).
   __syncthreads();
   if (tid == 0) {
@@ -559,56 +800,83 @@ static int max_smem_optin() {
   return n;
 }
 
-// Slot: the larger of one gate/up row pair (+ scales) and one batch of 8 down rows (+ scales), 16-byte multiple.
-static int fused_slot_bytes(const moe_layer_weights& w) {
-  const int gate = w.H + 2 * (w.H / w.G) * 2;
-  const int down = 8 * (w.I / 2) + 8 * (w.I / w.G) * 2;
-  return (std::max(gate, down) + 15) / 16 * 16;
-}
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-bool fused_config(const moe_layer_weights& w, int T, int* stages, size_t* smem, int* rows_per_cta) {
-  if (T < 1 || T > kFusedMaxT) return false;
+struct FusedCfg {
+  int stages, stage_bytes, cjobs, kd, rpc;
+  size_t smem;
+};
+
+static bool fused_plan(const moe_layer_weights& w, int T, FusedCfg* out) {
+  if (T < 1 || T > kFusedMaxT || w.TOPK * T > 64) return false;
   const int grid = device_sms();
   if (w.E + 1 > kRouterRows * grid || w.Is > kSgu * grid || w.H > 4096) return false;
+  // the bulk copies start at 16-byte aligned weight rows
+  if (!aligned16(w.router) || !aligned16(w.shared_gate) || !aligned16(w.shared_gate_up) ||
+      !aligned16(w.shared_down) || !aligned16(w.exp_gu_q) || !aligned16(w.exp_dn_q) || !aligned16(w.exp_gu_s) ||
+      !aligned16(w.exp_dn_s))
+    return false;
   const int rpc = (w.H + grid - 1) / grid;
   if (rpc > kFW) return false;  // one output row per warp
-  const int slot = fused_slot_bytes(w);
+  int C = kFW;
+  while (C > 1 && 2 * C * (w.H / 2) > 32 * 1024) C >>= 1;
+  int kd = 8;
+  while (kd > 1 && kd * rpc * (w.I / 2) > 32 * 1024) --kd;
+  // chunk-list bound: the CTA's gate/up jobs split at chunk size and expert boundaries, plus the down chunks
+  const int P = T * w.TOPK;
+  const int per_cta = P * w.I / grid + 1;
+  if (per_cta / C + per_cta / w.I + 2 + (P + kd - 1) / kd > kMaxChunks) return false;
+  const int sb = (std::max(gate_stage_bytes(C, w.H, w.G), down_stage_bytes(kd, rpc, w.I, w.G)) + 127) / 128 * 128;
   const int limit = max_smem_optin() - 6 * 1024;  // static shared memory of the kernel
-  for (int s = 4; s >= 2; --s) {
-    const FusedSmem L = fused_smem(T, w.H, w.TOPK, w.I, w.Is, rpc, slot, s);
+  for (int s = kMaxStages; s >= 2; --s) {
+    const FusedSmem L = fused_smem(T, w.H, w.TOPK, w.I, w.Is, rpc, sb, s);
     if ((int)L.total <= limit) {
-      *stages = s;
-      *smem = L.total;
-      *rows_per_cta = rpc;
+      out->stages = s;
+      out->stage_bytes = sb;
+      out->cjobs = C;
+      out->kd = kd;
+      out->rpc = rpc;
+      out->smem = L.total;
       return true;
     }
   }
   return false;
 }
 
+bool fused_config(const moe_layer_weights& w, int T, int* stages, size_t* smem, int* rows_per_cta) {
+  FusedCfg c;
+  if (!fused_plan(w, T, &c)) return false;
+  *stages = c.stages;
+  *smem = c.smem;
+  *rows_per_cta = c.rpc;
+  return true;
+}
+
 cudaError_t launch_fused_decode(const BlockArgs& a, unsigned long long* gbar, bool next_norm, cudaStream_t s) {
-  int stages = 0, rpc = 0;
-  size_t smem = 0;
-  if (!fused_config(a.w, a.T, &stages, &smem, &rpc)) return cudaErrorInvalidValue;
+  FusedCfg c;
+  if (!fused_plan(a.w, a.T, &c)) return cudaErrorInvalidValue;
   static size_t granted = 0;
-  if (smem > granted) {
-    cudaError_t e = cudaFuncSetAttribute(moe_fused_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)std::max(smem, (size_t)200 * 1024));
+  if (c.smem > granted) {
+    const size_t want = std::max(c.smem, (size_t)200 * 1024);
+    cudaError_t e =
+        cudaFuncSetAttribute(moe_fused_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
     if (e != cudaSuccess) return e;
-    granted = std::max(smem, (size_t)200 * 1024);
+    granted = want;
   }
   FusedArgs f;
   memset(&f, 0, sizeof f);
   f.a = a;
   f.gbar = gbar;
-  f.slot_bytes = fused_slot_bytes(a.w);
-  f.stages = stages;
-  f.rows_per_cta = rpc;
+  f.stages = c.stages;
+  f.stage_bytes = c.stage_bytes;
+  f.cjobs = c.cjobs;
+  f.kd = c.kd;
+  f.rows_per_cta = c.rpc;
   f.next_norm = next_norm ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(device_sms());
   cfg.blockDim = dim3(kFThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = c.smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
