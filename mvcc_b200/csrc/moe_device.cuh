@@ -18,6 +18,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   __syncthreads();
   if (lane == 0) red[warp] = v;
   __syncthreads();
+  __syncwarp();  // bar.sync does not reconverge the warp split by the lane-0 store
   float t = lane < nw ? red[lane] : 0.f;
   return warp_sum(t);
 }

@@ -148,6 +148,14 @@ __device__ __forceinline__ bool bar_wait(uint64_t* mbar, uint32_t parity) {
 }
 __device__ __forceinline__ int vload(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
+// CTA barrier that also reconverges the calling warp: after a section run by one lane (or part of a warp), the warp
+// can leave bar.sync still split into groups that then issue every later instruction separately; __syncwarp joins
+// them again.
+__device__ __forceinline__ void cta_sync() {
+  __syncthreads();
+  __syncwarp();
+}
+
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -159,8 +167,9 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 // own first arrival lies in [base, base + G)) and barrier k completes at base + k x G. Arrival is a release
 // reduction (no round trip); the wait spins, bounded, on an acquire load.
 __device__ __forceinline__ void grid_arrive(unsigned long long* gbar) {
-  __syncthreads();
+  cta_sync();
   if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(gbar) : "memory");
+  __syncwarp();
 }
 __device__ __forceinline__ bool grid_wait(const unsigned long long* gbar, unsigned long long target, uint32_t* err,
                                           int* ok_s) {
@@ -177,7 +186,7 @@ __device__ __forceinline__ bool grid_wait(const unsigned long long* gbar, unsign
     }
     *ok_s = ok;
   }
-  __syncthreads();
+  cta_sync();
   return *ok_s != 0;
 }
 
@@ -194,7 +203,9 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
 
 // The reference's top-k rule (router_topk_kernel, kernels.cuh:774-809) over one token's logits: K rounds of argmax
 // by (value desc, index asc), weights exp(v - max) / sum over the picks. A round is a per-lane scan of its 8 values
-// and two warp reductions (redux.sync: max of the value key, then min of the index among the lanes holding it).
+// and two warp reductions (redux.sync: max of the value key, then min of the index among the lanes holding it); lane
+// kk keeps pick kk. The rounds stay a loop: this code runs once per launch, and a compact body costs fewer
+// instruction fetches than an unrolled one.
 __device__ void topk_warp_redux(const float* row, int E, int K, int32_t* idx_out, float* wts_out) {
   const int lane = threadIdx.x & 31;
   uint32_t key[8];
@@ -203,10 +214,10 @@ __device__ void topk_warp_redux(const float* row, int E, int K, int32_t* idx_out
     const int e = lane + i * 32;
     key[i] = fkey(e < E ? __ldcg(row + e) : -1e30f);
   }
-  float pv[8];
-  int pi[8];
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
+  uint32_t mykey = 0;
+  int myidx = 0;
+#pragma unroll 1
+  for (int kk = 0; kk < K; ++kk) {
     uint32_t bk = 0;
     int bi = 0x7fffffff;
 #pragma unroll
@@ -214,51 +225,45 @@ __device__ void topk_warp_redux(const float* row, int E, int K, int32_t* idx_out
       if (key[i] > bk) { bk = key[i]; bi = lane + i * 32; }
     const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
     const int wi = (int)__reduce_min_sync(0xffffffffu, bk == mk ? (uint32_t)bi : 0x7fffffffu);
-    pv[kk] = fkey_inv(mk);
-    pi[kk] = wi;
-    if (kk < K) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (lane + i * 32 == wi) key[i] = 0;
+    if (lane == kk) {
+      mykey = mk;
+      myidx = wi;
     }
-  }
-  float mx = pv[0];
 #pragma unroll
-  for (int kk = 1; kk < 8; ++kk)
-    if (kk < K) mx = fmaxf(mx, pv[kk]);
+    for (int i = 0; i < 8; ++i)
+      if (lane + i * 32 == wi) key[i] = 0;
+  }
+  // picks come in descending order, so the first is the maximum
+  const float mx = fkey_inv(__shfl_sync(0xffffffffu, mykey, 0));
+  const float ev = lane < K ? __expf(fkey_inv(mykey) - mx) : 0.f;
   float den = 0.f;
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    pv[kk] = __expf(pv[kk] - mx);
-    if (kk < K) den += pv[kk];
-  }
-  float myw = 0.f;
-  int myi = 0;
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk)
-    if (lane == kk) { myw = pv[kk]; myi = pi[kk]; }
+#pragma unroll 1
+  for (int kk = 0; kk < K; ++kk) den += __shfl_sync(0xffffffffu, ev, kk);
   if (lane < K) {
-    idx_out[lane] = myi;
-    wts_out[lane] = myw / den;
+    idx_out[lane] = myidx;
+    wts_out[lane] = ev / den;
   }
+  __syncwarp();
 }
 
 // The unique-expert table in one warp (same contents and order as build_unique in moe_decode.cu): the P <= 64 pairs
-// sorted by (expert, pair index) with a bitonic network over 64 keys (element i in lane i % 32, register i / 32);
+// sorted by (expert, pair index) with a bitonic network over 64 keys (element i in lane i % 32, register i / 32;
+// kept as loops for the same reason as the top-k);
 // uniq[u] the ascending experts, uoff[u] their first sorted position, upairs/ptok the sorted pairs and their tokens.
 // Invalid indices sort last and are dropped.
 __device__ void table_warp(const int32_t* idx_s, int P, int E, int K, int* uniq_s, int* uoff_s, int* upairs_s,
                            int* ptok_s, int* nuniq_s) {
   const int lane = threadIdx.x & 31;
+  __syncwarp();
   uint32_t v0, v1;
   {
     const int e0 = lane < P ? idx_s[lane] : -1, e1 = lane + 32 < P ? idx_s[lane + 32] : -1;
     v0 = (lane < P && e0 >= 0 && e0 < E) ? ((uint32_t)e0 << 6) | (uint32_t)lane : 0xffffffffu;
     v1 = (lane + 32 < P && e1 >= 0 && e1 < E) ? ((uint32_t)e1 << 6) | (uint32_t)(lane + 32) : 0xffffffffu;
   }
-#pragma unroll
+#pragma unroll 1
   for (int k = 2; k <= 64; k <<= 1) {
-#pragma unroll
+#pragma unroll 1
     for (int j = k >> 1; j > 0; j >>= 1) {
       uint32_t o0, o1;
       if (j == 32) {
@@ -349,6 +354,7 @@ __device__ __forceinline__ void fused_gate_job(const BlockArgs& a, const float* 
     g = warp_sum(g);
     u = warp_sum(u);
     if (lane == 0) a.inter[(int64_t)pair * I + i] = f2bf(silu(g) * u);
+    __syncwarp();
   }
 }
 
@@ -426,7 +432,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     }
     if (h0 < h1) bulk_g2s(sdn_s, a.w.shared_down + (int64_t)h0 * Is, (h1 - h0) * Is * 2, &sbar);
   }
-  __syncthreads();
+  cta_sync();
 
   // ---- phase R: RMSNorm of every token into xs (fp32, permuted); CTA 0 writes `normed`
   for (int t = 0; t < T; ++t) {
@@ -466,7 +472,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       }
     }
   }
-  __syncthreads();
+  cta_sync();
 
   // Router rows (warps 0..1): gemv_bf16 order per lane over its 32-k chunks, butterfly sum.
   if (warp < kRouterRows) {
@@ -496,6 +502,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
             if (row < E) a.logits[(int64_t)t * E + row] = a.w.router_bias ? acc + a.w.router_bias[row] : acc;
             else a.gate[t] = sigmoid(acc);
           }
+          __syncwarp();
         }
       }
     }
@@ -530,6 +537,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
           g = warp_sum(g);
           u = warp_sum(u);
           if (lane == 0) a.sinter[(int64_t)t * Is + j] = f2bf(silu(bf2f(f2bf(g))) * bf2f(f2bf(u)));
+          __syncwarp();
         }
       }
     }
@@ -539,13 +547,13 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
 
   // ---- phase G: top-k per token (warp t), unique-expert table and chunk list (warp 0)
   if (warp < T) topk_warp_redux(a.logits + (int64_t)warp * E, E, K, idx_s + warp * K, wts_s + warp * K);
-  __syncthreads();
+  cta_sync();
   if (warp == 0) {
     table_warp(idx_s, P, E, K, uniq_s, uoff_s, upairs_s, ptok_s, &nuniq_s);
     __syncwarp();
     if (lane == 0) {
       const int U = nuniq_s, J = U * I;
-      const int cj0 = (int)((int64_t)cta * J / grid), cj1 = (int)((int64_t)(cta + 1) * J / grid);
+      const int cj0 = cta * J / grid, cj1 = (cta + 1) * J / grid;  // J <= 64 x 2048: no overflow
       int n = 0;
       for (int j = cj0; j < cj1 && n < kMaxChunks;) {
         const int uix = j / I, i0 = j - uix * I;
@@ -559,7 +567,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       nchunks_s = n;
     }
   }
-  __syncthreads();
+  cta_sync();
   const int U = nuniq_s, nchunks = nchunks_s, ngate = ngate_s;
 
   // Issues chunk c into stage c % S (one thread).
@@ -618,6 +626,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       atomicOr(a.err, (uint32_t)MOE_ERR_BARRIER);
       abort_s = 1;
     }
+    __syncwarp();
     return ok;
   };
 
@@ -635,7 +644,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     for (int u = tid; u <= U; u += kFThreads) a.uoff[u] = uoff_s[u];
     if (tid == 0) *a.nuniq = U;
   }
-  __syncthreads();
+  cta_sync();
 
   // Routed gate/up: job w of each gate/up chunk on warp w.
   const Nib8Magic M = nib8_magic();
@@ -658,7 +667,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   }
   grid_arrive(f.gbar);
   if (!grid_wait(f.gbar, base + 2 * (unsigned long long)grid, a.err, &ok_s) && tid == 0) abort_s = 1;
-  __syncthreads();
+  cta_sync();
 
   // ---- phase D: stage inter (bf16, permuted) and sinter; reduce this warp's output row over the down chunks
   const int nchd = I >> 4, Ld = min(32, nchd), PI = inter_stride(I);
@@ -670,7 +679,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   }
   for (int idx = tid; idx < T * Is / 8; idx += kFThreads)
     reinterpret_cast<uint4*>(sinter_s)[idx] = __ldcg(reinterpret_cast<const uint4*>(a.sinter) + idx);
-  __syncthreads();
+  cta_sync();
 
   float* acc_w = acc_s + (size_t)warp * T * 32;
   for (int t = 0; t < T; ++t) acc_w[t * 32 + lane] = 0.f;
@@ -745,7 +754,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   }
   // No copy may still be landing when the CTA exits: wait (bounded) for the last chunk issued to every stage and
   // for the entry copies (immediate on the normal path).
-  __syncthreads();
+  cta_sync();
   if (tid == 0) {
     for (int s = 0; s < S; ++s)
       if (issued_s[s] > 0) bar_wait(&full_b[s], (uint32_t)((issued_s[s] - 1) & 1));
@@ -754,12 +763,12 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   }
   if (!f.next_norm || vload(&abort_s)) return;
   // Next layer's RMSNorm: the last CTA to finish (shared_gate_combine_rmsnorm_kernel).
-  __syncthreads();
+  cta_sync();
   if (tid == 0) {
     __threadfence();
     is_last = atomicInc(&a.ticket[TICKET_COMBINE], gridDim.x - 1) == gridDim.x - 1;
   }
-  __syncthreads();
+  cta_sync();
   if (!is_last) return;
   __threadfence();
   for (int t = 0; t < T; ++t) {
