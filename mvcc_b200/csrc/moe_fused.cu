@@ -82,10 +82,11 @@ __host__ __device__ inline FusedSmem fused_smem(int T, int H, int TOPK, int I, i
   return L;
 }
 
-// Layout of one stage. Gate/up chunk of n <= C jobs: gate rows [C][H/2], up rows [C][H/2], then the gate and up
-// scale rows, each copied as the 16-byte aligned superset of its [n][H/G] fp16. Down chunk of n <= kd experts: rows
+// Layout of one stage. Gate/up chunk of n <= C consecutive jobs, in one expert or running on into the next (two
+// segments): gate rows [C][H/2], up rows [C][H/2], then the gate and the up scale rows, each segment's copied as the
+// 16-byte aligned superset of its [n_k][H/G] fp16, the second segment's after the first's. Down chunk of n <= kd experts: rows
 // [kd][rpc][I/2], then per expert its scale rows [rpc][I/G] fp16 as an aligned superset.
-__host__ __device__ inline int gate_scale_region(int C, int H, int G) { return a16(C * (H / G) * 2) + 32; }
+__host__ __device__ inline int gate_scale_region(int C, int H, int G) { return a16(C * (H / G) * 2) + 64; }
 __host__ __device__ inline int down_scale_region(int rpc, int I, int G) { return a16(rpc * (I / G) * 2) + 32; }
 __host__ __device__ inline int gate_stage_bytes(int C, int H, int G) {
   return 2 * C * (H / 2) + 2 * gate_scale_region(C, H, G);
@@ -202,36 +203,52 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
 }
 
 // The reference's top-k rule (router_topk_kernel, kernels.cuh:774-809) over one token's logits: K rounds of argmax
-// by (value desc, index asc), weights exp(v - max) / sum over the picks. A round is a per-lane scan of its 8 values
-// and two warp reductions (redux.sync: max of the value key, then min of the index among the lanes holding it); lane
-// kk keeps pick kk. The rounds stay a loop: this code runs once per launch, and a compact body costs fewer
-// instruction fetches than an unrolled one.
+// by (value desc, index asc), weights exp(v - max) / sum over the picks. Each lane first sorts its 8 logits by (value
+// desc, index asc); a round is then two warp reductions over the lanes' heads (redux.sync: max of the value key, min
+// of the index among the lanes holding it) and a shift in the winning lane. Lane kk keeps pick kk. The rounds stay a
+// loop: this code runs once per launch, and a compact body costs fewer instruction fetches than an unrolled one.
+__device__ __forceinline__ void cas_desc(uint32_t& ka, int& ia, uint32_t& kb, int& ib) {
+  // (ka, ia) before (kb, ib) when ka > kb, or ka == kb and ia < ib
+  const bool swap = kb > ka || (kb == ka && ib < ia);
+  const uint32_t k0 = swap ? kb : ka, k1 = swap ? ka : kb;
+  const int i0 = swap ? ib : ia, i1 = swap ? ia : ib;
+  ka = k0; kb = k1; ia = i0; ib = i1;
+}
 __device__ void topk_warp_redux(const float* row, int E, int K, int32_t* idx_out, float* wts_out) {
   const int lane = threadIdx.x & 31;
-  uint32_t key[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int e = lane + i * 32;
-    key[i] = fkey(e < E ? __ldcg(row + e) : -1e30f);
-  }
+  uint32_t k0, k1, k2, k3, k4, k5, k6, k7;
+  int i0 = lane, i1 = lane + 32, i2 = lane + 64, i3 = lane + 96, i4 = lane + 128, i5 = lane + 160, i6 = lane + 192,
+      i7 = lane + 224;
+  k0 = fkey(i0 < E ? __ldcg(row + i0) : -1e30f);
+  k1 = fkey(i1 < E ? __ldcg(row + i1) : -1e30f);
+  k2 = fkey(i2 < E ? __ldcg(row + i2) : -1e30f);
+  k3 = fkey(i3 < E ? __ldcg(row + i3) : -1e30f);
+  k4 = fkey(i4 < E ? __ldcg(row + i4) : -1e30f);
+  k5 = fkey(i5 < E ? __ldcg(row + i5) : -1e30f);
+  k6 = fkey(i6 < E ? __ldcg(row + i6) : -1e30f);
+  k7 = fkey(i7 < E ? __ldcg(row + i7) : -1e30f);
+  // Batcher's odd-even merge sort of 8 (19 compare-exchanges)
+  cas_desc(k0, i0, k1, i1); cas_desc(k2, i2, k3, i3); cas_desc(k4, i4, k5, i5); cas_desc(k6, i6, k7, i7);
+  cas_desc(k0, i0, k2, i2); cas_desc(k1, i1, k3, i3); cas_desc(k4, i4, k6, i6); cas_desc(k5, i5, k7, i7);
+  cas_desc(k1, i1, k2, i2); cas_desc(k5, i5, k6, i6);
+  cas_desc(k0, i0, k4, i4); cas_desc(k1, i1, k5, i5); cas_desc(k2, i2, k6, i6); cas_desc(k3, i3, k7, i7);
+  cas_desc(k2, i2, k4, i4); cas_desc(k3, i3, k5, i5);
+  cas_desc(k1, i1, k2, i2); cas_desc(k3, i3, k4, i4); cas_desc(k5, i5, k6, i6);
   uint32_t mykey = 0;
   int myidx = 0;
 #pragma unroll 1
   for (int kk = 0; kk < K; ++kk) {
-    uint32_t bk = 0;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (key[i] > bk) { bk = key[i]; bi = lane + i * 32; }
-    const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
-    const int wi = (int)__reduce_min_sync(0xffffffffu, bk == mk ? (uint32_t)bi : 0x7fffffffu);
+    const uint32_t mk = __reduce_max_sync(0xffffffffu, k0);
+    const int wi = (int)__reduce_min_sync(0xffffffffu, k0 == mk ? (uint32_t)i0 : 0x7fffffffu);
     if (lane == kk) {
       mykey = mk;
       myidx = wi;
     }
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (lane + i * 32 == wi) key[i] = 0;
+    if (i0 == wi) {  // the winner pops its head
+      k0 = k1; i0 = i1; k1 = k2; i1 = i2; k2 = k3; i2 = i3; k3 = k4; i3 = i4;
+      k4 = k5; i4 = i5; k5 = k6; i5 = i6; k6 = k7; i6 = i7; k7 = 0; i7 = 0x7fffffff;
+    }
+    __syncwarp();
   }
   // picks come in descending order, so the first is the maximum
   const float mx = fkey_inv(__shfl_sync(0xffffffffu, mykey, 0));
@@ -247,12 +264,11 @@ __device__ void topk_warp_redux(const float* row, int E, int K, int32_t* idx_out
 }
 
 // The unique-expert table in one warp (same contents and order as build_unique in moe_decode.cu): the P <= 64 pairs
-// sorted by (expert, pair index) with a bitonic network over 64 keys (element i in lane i % 32, register i / 32;
-// kept as loops for the same reason as the top-k);
+// sorted by (expert, pair index) with a bitonic network over 64 keys (element i in lane i % 32, register i / 32);
 // uniq[u] the ascending experts, uoff[u] their first sorted position, upairs/ptok the sorted pairs and their tokens.
 // Invalid indices sort last and are dropped.
 __device__ void table_warp(const int32_t* idx_s, int P, int E, int K, int* uniq_s, int* uoff_s, int* upairs_s,
-                           int* ptok_s, int* nuniq_s) {
+                           int* ptok_s, int* pu_s, int* nuniq_s) {
   const int lane = threadIdx.x & 31;
   __syncwarp();
   uint32_t v0, v1;
@@ -261,9 +277,9 @@ __device__ void table_warp(const int32_t* idx_s, int P, int E, int K, int* uniq_
     v0 = (lane < P && e0 >= 0 && e0 < E) ? ((uint32_t)e0 << 6) | (uint32_t)lane : 0xffffffffu;
     v1 = (lane + 32 < P && e1 >= 0 && e1 < E) ? ((uint32_t)e1 << 6) | (uint32_t)(lane + 32) : 0xffffffffu;
   }
-#pragma unroll 1
+#pragma unroll
   for (int k = 2; k <= 64; k <<= 1) {
-#pragma unroll 1
+#pragma unroll
     for (int j = k >> 1; j > 0; j >>= 1) {
       uint32_t o0, o1;
       if (j == 32) {
@@ -306,11 +322,13 @@ __device__ void table_warp(const int32_t* idx_s, int P, int E, int K, int* uniq_
     const int p = (int)(v0 & 63);
     upairs_s[lane] = p;
     ptok_s[lane] = p / K;
+    pu_s[lane] = u0;
   }
   if (valid1) {
     const int p = (int)(v1 & 63);
     upairs_s[lane + 32] = p;
     ptok_s[lane + 32] = p / K;
+    pu_s[lane + 32] = u1;
   }
   if (lane == 0) {
     const int U = __popc(b0) + __popc(b1);
@@ -358,6 +376,59 @@ __device__ __forceinline__ void fused_gate_job(const BlockArgs& a, const float* 
   }
 }
 
+// Two gate/up jobs of the same unique expert (rows i0 and i1) on one warp: the activation loads are shared, each
+// job's arithmetic is that of fused_gate_job.
+__device__ __forceinline__ void fused_gate_job2(const BlockArgs& a, const float* xs, const uint8_t* grow0,
+                                                const uint8_t* urow0, const uint16_t* gsc0, const uint16_t* usc0,
+                                                const uint8_t* grow1, const uint8_t* urow1, const uint16_t* gsc1,
+                                                const uint16_t* usc1, int uix, int i0, int i1, const int* uoff_s,
+                                                const int* upairs_s, const int* ptok_s, int gshift,
+                                                const Nib8Magic& M) {
+  const int lane = threadIdx.x & 31;
+  const int H = a.w.H, I = a.w.I, nch = H >> 5;
+  for (int p = uoff_s[uix]; p < uoff_s[uix + 1]; ++p) {
+    const int pair = upairs_s[p];
+    const float* xt = xs + ptok_s[p] * H;
+    float g0 = 0.f, u0 = 0.f, g1 = 0.f, u1 = 0.f;
+    for (int c = lane; c < nch; c += 32) {
+      const uint4 gq0 = *reinterpret_cast<const uint4*>(grow0 + c * 16);
+      const uint4 uq0 = *reinterpret_cast<const uint4*>(urow0 + c * 16);
+      const uint4 gq1 = *reinterpret_cast<const uint4*>(grow1 + c * 16);
+      const uint4 uq1 = *reinterpret_cast<const uint4*>(urow1 + c * 16);
+      const uint32_t gw0[4] = {gq0.x, gq0.y, gq0.z, gq0.w}, uw0[4] = {uq0.x, uq0.y, uq0.z, uq0.w};
+      const uint32_t gw1[4] = {gq1.x, gq1.y, gq1.z, gq1.w}, uw1[4] = {uq1.x, uq1.y, uq1.z, uq1.w};
+      Nib8Acc ag0, au0, ag1, au1;
+      nib8_zero(ag0);
+      nib8_zero(au0);
+      nib8_zero(ag1);
+      nib8_zero(au1);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        u64 x01, x23, x45, x67;
+        lds_pairs(xt + ((q * 2) * nch + c) * 4, x01, x23);
+        lds_pairs(xt + ((q * 2 + 1) * nch + c) * 4, x45, x67);
+        nib8x2(gw0[q], x01, x23, x45, x67, M, ag0);
+        nib8x2(uw0[q], x01, x23, x45, x67, M, au0);
+        nib8x2(gw1[q], x01, x23, x45, x67, M, ag1);
+        nib8x2(uw1[q], x01, x23, x45, x67, M, au1);
+      }
+      g0 = fmaf(nib8_fold(ag0), h2f(gsc0[c >> gshift]), g0);
+      u0 = fmaf(nib8_fold(au0), h2f(usc0[c >> gshift]), u0);
+      g1 = fmaf(nib8_fold(ag1), h2f(gsc1[c >> gshift]), g1);
+      u1 = fmaf(nib8_fold(au1), h2f(usc1[c >> gshift]), u1);
+    }
+    g0 = warp_sum(g0);
+    u0 = warp_sum(u0);
+    g1 = warp_sum(g1);
+    u1 = warp_sum(u1);
+    if (lane == 0) {
+      a.inter[(int64_t)pair * I + i0] = f2bf(silu(g0) * u0);
+      a.inter[(int64_t)pair * I + i1] = f2bf(silu(g1) * u1);
+    }
+    __syncwarp();
+  }
+}
+
 // Chunk list entry: kind 0 = gate/up jobs i0 .. i0 + n - 1 of unique expert a; kind 1 = down rows of unique experts
 // a .. a + n - 1.
 struct Chunk {
@@ -387,7 +458,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   __shared__ float red[32];
   __shared__ int32_t idx_s[64];
   __shared__ float wts_s[64];
-  __shared__ int uniq_s[64], uoff_s[65], upairs_s[64], ptok_s[64];
+  __shared__ int uniq_s[64], uoff_s[65], upairs_s[64], ptok_s[64], pu_s[64];
   __shared__ int nuniq_s, nchunks_s, ngate_s, ok_s, is_last, abort_s;
   __shared__ unsigned long long base_s;
   const int h0 = cta * rpc, h1 = min(H, h0 + rpc);
@@ -397,8 +468,19 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   const uint8_t* gscale = reinterpret_cast<const uint8_t*>(a.w.exp_gu_s);
   const uint8_t* dscale = reinterpret_cast<const uint8_t*>(a.w.exp_dn_s);
 
+  // token 0's activations are requested before the entry work below, which overlaps their latency
+  float4 pre_h[2];
+  uint2 pre_d[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int i = tid + r * kFThreads;
+    if (i < H / 4) {
+      pre_h[r] = reinterpret_cast<const float4*>(a.hidden)[i];
+      pre_d[r] = reinterpret_cast<const uint2*>(a.attn_out)[i];
+    }
+  }
   if (tid == 0) {
-    base_s = (ld_acquire_u64(f.gbar) / grid) * grid;
+    const unsigned long long gb = ld_acquire_u64(f.gbar);  // consumed at the end of this block
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_b[s], 1);
       cnt_s[s] = 0;
@@ -431,6 +513,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       }
     }
     if (h0 < h1) bulk_g2s(sdn_s, a.w.shared_down + (int64_t)h0 * Is, (h1 - h0) * Is * 2, &sbar);
+    base_s = (gb / grid) * grid;
   }
   cta_sync();
 
@@ -444,8 +527,8 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     for (int r = 0; r < 2; ++r) {  // H <= 4096 = 2 x 512 threads x 4
       const int i = tid + r * kFThreads;
       if (i < H / 4) {
-        const uint2 d = dr[i];
-        hv[r] = hr[i];
+        const uint2 d = t == 0 ? pre_d[r] : dr[i];
+        hv[r] = t == 0 ? pre_h[r] : hr[i];
         hv[r].x += lo_bf(d.x);
         hv[r].y += hi_bf(d.x);
         hv[r].z += lo_bf(d.y);
@@ -549,7 +632,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   if (warp < T) topk_warp_redux(a.logits + (int64_t)warp * E, E, K, idx_s + warp * K, wts_s + warp * K);
   cta_sync();
   if (warp == 0) {
-    table_warp(idx_s, P, E, K, uniq_s, uoff_s, upairs_s, ptok_s, &nuniq_s);
+    table_warp(idx_s, P, E, K, uniq_s, uoff_s, upairs_s, ptok_s, pu_s, &nuniq_s);
     __syncwarp();
     if (lane == 0) {
       const int U = nuniq_s, J = U * I;
@@ -557,7 +640,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       int n = 0;
       for (int j = cj0; j < cj1 && n < kMaxChunks;) {
         const int uix = j / I, i0 = j - uix * I;
-        const int m = min(C, min(cj1 - j, I - i0));
+        const int m = min(C, cj1 - j);  // may run on into the next expert (C <= I)
         chunk_s[n++] = Chunk{0, uix, i0, m};
         j += m;
       }
@@ -570,40 +653,55 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   cta_sync();
   const int U = nuniq_s, nchunks = nchunks_s, ngate = ngate_s;
 
-  // Issues chunk c into stage c % S (one thread).
+  // Issues chunk c into stage c % S; called by all 32 lanes of one warp, which spread the copies over lanes.
   auto issue = [&](int c) {
     const int s = c % S;
     uint8_t* st = ring + (size_t)s * SB;
     const Chunk ch = chunk_s[c];
+    fence_proxy_async_smem();  // this stage's earlier generic reads before the async-proxy writes
     if (ch.kind == 0) {
-      const int64_t g0 = (int64_t)uniq_s[ch.a] * 2 * I + ch.i0, u0 = g0 + I;
-      const uint32_t tx = (uint32_t)(2 * ch.n * rowb) + span_bytes(gscale + g0 * sgb, ch.n * sgb) +
-                          span_bytes(gscale + u0 * sgb, ch.n * sgb);
-      expect_tx(&full_b[s], tx);
-      bulk_g2s(st, a.w.exp_gu_q + g0 * rowb, ch.n * rowb, &full_b[s]);
-      bulk_g2s(st + C * rowb, a.w.exp_gu_q + u0 * rowb, ch.n * rowb, &full_b[s]);
-      bulk_span(st + 2 * C * rowb, gscale + g0 * sgb, ch.n * sgb, &full_b[s]);
-      bulk_span(st + 2 * C * rowb + gate_scale_region(C, H, G), gscale + u0 * sgb, ch.n * sgb, &full_b[s]);
-    } else {
-      const int nr = h1 - h0;
-      uint32_t tx = 0;
-      for (int b = 0; b < ch.n; ++b) {
-        const int64_t r0 = (int64_t)uniq_s[ch.a + b] * H + h0;
-        tx += (uint32_t)(nr * drowb) + span_bytes(dscale + r0 * dsb, nr * dsb);
+      // segment k: n_k jobs of unique expert a + k from row r_k, at stage position pos_k; lanes 4k .. 4k + 3 copy its
+      // gate rows, up rows, gate scales, up scales
+      const int n1 = min(ch.n, I - ch.i0), seg = (lane >> 2) & 1, part = lane & 3;
+      const int nk = seg ? ch.n - n1 : n1, rk = seg ? 0 : ch.i0, pos = seg ? n1 : 0;
+      const int64_t g0 = nk > 0 ? (int64_t)uniq_s[ch.a + seg] * 2 * I + rk : 0, u0 = g0 + I;
+      const int64_t gA = (int64_t)uniq_s[ch.a] * 2 * I + ch.i0;  // segment 0's first gate row
+      const uint32_t gsp0 = span_bytes(gscale + gA * sgb, n1 * sgb), usp0 = span_bytes(gscale + (gA + I) * sgb, n1 * sgb);
+      const uint32_t mine = (lane < 8 && nk > 0)
+                                ? (part < 2 ? (uint32_t)(nk * rowb)
+                                            : span_bytes(gscale + (part == 2 ? g0 : u0) * sgb, nk * sgb))
+                                : 0u;
+      const uint32_t tx = __reduce_add_sync(0xffffffffu, mine);
+      if (lane == 0) expect_tx(&full_b[s], tx);
+      __syncwarp();
+      if (lane < 8 && nk > 0) {
+        uint8_t* sc0 = st + 2 * C * rowb;
+        if (part == 0) bulk_g2s(st + pos * rowb, a.w.exp_gu_q + g0 * rowb, nk * rowb, &full_b[s]);
+        else if (part == 1) bulk_g2s(st + (C + pos) * rowb, a.w.exp_gu_q + u0 * rowb, nk * rowb, &full_b[s]);
+        else if (part == 2) bulk_span(sc0 + (seg ? gsp0 : 0), gscale + g0 * sgb, nk * sgb, &full_b[s]);
+        else bulk_span(sc0 + gate_scale_region(C, H, G) + (seg ? usp0 : 0), gscale + u0 * sgb, nk * sgb, &full_b[s]);
       }
-      expect_tx(&full_b[s], tx);
-      for (int b = 0; b < ch.n; ++b) {
-        const int64_t r0 = (int64_t)uniq_s[ch.a + b] * H + h0;
-        bulk_g2s(st + (size_t)b * rpc * drowb, a.w.exp_dn_q + r0 * drowb, nr * drowb, &full_b[s]);
-        bulk_span(st + (size_t)f.kd * rpc * drowb + (size_t)b * down_scale_region(rpc, I, G), dscale + r0 * dsb,
-                  nr * dsb, &full_b[s]);
+    } else {
+      const int nr = h1 - h0, b = lane >> 1;
+      const int64_t r0 = b < ch.n ? (int64_t)uniq_s[ch.a + b] * H + h0 : 0;
+      const uint32_t mine = (b < ch.n && (lane & 1) == 0) ? (uint32_t)(nr * drowb) + span_bytes(dscale + r0 * dsb, nr * dsb) : 0u;
+      const uint32_t tx = __reduce_add_sync(0xffffffffu, mine);
+      if (lane == 0) expect_tx(&full_b[s], tx);
+      __syncwarp();
+      if (b < ch.n) {
+        if ((lane & 1) == 0) bulk_g2s(st + (size_t)b * rpc * drowb, a.w.exp_dn_q + r0 * drowb, nr * drowb, &full_b[s]);
+        else
+          bulk_span(st + (size_t)f.kd * rpc * drowb + (size_t)b * down_scale_region(rpc, I, G), dscale + r0 * dsb,
+                    nr * dsb, &full_b[s]);
       }
     }
-    issued_s[s] += 1;
+    if (lane == 0) issued_s[s] += 1;
+    __syncwarp();
   };
   // Called by every warp once it is done with chunk c: the last of the kFW warps refills the stage with chunk c + S.
   auto release = [&](int c) {
     __syncwarp();
+    int refill = 0;
     if (lane == 0) {
       const int s = c % S;
       __threadfence_block();
@@ -611,12 +709,10 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       if (old == kFW - 1) {
         cnt_s[s] = 0;
         __threadfence_block();
-        if (c + S < nchunks && !vload(&abort_s)) {
-          fence_proxy_async_smem();
-          issue(c + S);
-        }
+        refill = c + S < nchunks && !vload(&abort_s);
       }
     }
+    if (__shfl_sync(0xffffffffu, refill, 0)) issue(c + S);
     __syncwarp();
   };
   // Waits for chunk c's bytes (every lane); false, and the CTA aborts, if the wait gives up.
@@ -630,9 +726,13 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     return ok;
   };
 
-  if (tid == 0 && !abort_s) {
-    fence_proxy_async_smem();
-    for (int c = 0; c < min(S, nchunks); ++c) issue(c);
+  // first fill of the ring: warp 0 issues the gate/up chunks, the last warp the down chunks, concurrently; the
+  // consumers synchronise on the stage barriers, not on a CTA barrier
+  if (!vload(&abort_s)) {
+    if (warp == 0)
+      for (int c = 0; c < min(S, ngate); ++c) issue(c);
+    else if (warp == kFW - 1)
+      for (int c = ngate; c < min(S, nchunks); ++c) issue(c);
   }
   if (cta == 0) {
     for (int p = tid; p < P; p += kFThreads) {
@@ -644,9 +744,8 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     for (int u = tid; u <= U; u += kFThreads) a.uoff[u] = uoff_s[u];
     if (tid == 0) *a.nuniq = U;
   }
-  cta_sync();
 
-  // Routed gate/up: job w of each gate/up chunk on warp w.
+  // Routed gate/up: jobs w and w + kFW of each gate/up chunk on warp w (two at once when both exist).
   const Nib8Magic M = nib8_magic();
   const int gshift = __ffs(G) - 6, dshift = __ffs(G) - 5;
   bool live = !vload(&abort_s);
@@ -655,13 +754,37 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     const Chunk ch = chunk_s[c];
     if (live && warp < ch.n) {
       const uint8_t* st = ring + (size_t)(c % S) * SB;
-      const int64_t g0 = (int64_t)uniq_s[ch.a] * 2 * I + ch.i0;
-      const uint8_t* gsc = st + 2 * C * rowb + span_delta(gscale + g0 * sgb) + warp * sgb;
-      const uint8_t* usc = st + 2 * C * rowb + gate_scale_region(C, H, G) + span_delta(gscale + (g0 + I) * sgb) +
-                           warp * sgb;
-      fused_gate_job(a, xs, st + warp * rowb, st + (C + warp) * rowb, reinterpret_cast<const uint16_t*>(gsc),
-                     reinterpret_cast<const uint16_t*>(usc), ch.a, ch.i0 + warp, uoff_s, upairs_s, ptok_s, gshift,
-                     M);
+      const int n1 = min(ch.n, I - ch.i0);
+      const int64_t gA = (int64_t)uniq_s[ch.a] * 2 * I + ch.i0;
+      const int64_t gB = ch.n > n1 ? (int64_t)uniq_s[ch.a + 1] * 2 * I : 0;
+      const uint32_t gsp0 = span_bytes(gscale + gA * sgb, n1 * sgb), usp0 = span_bytes(gscale + (gA + I) * sgb, n1 * sgb);
+      const uint8_t* sc0 = st + 2 * C * rowb;
+      // gate/up rows and scales of chunk job k
+      auto job = [&](int k, const uint16_t*& gsc, const uint16_t*& usc, int& uix, int& row) {
+        const bool second = k >= n1;
+        const int64_t gk = second ? gB : gA;
+        const int kk = second ? k - n1 : k;
+        gsc = reinterpret_cast<const uint16_t*>(sc0 + (second ? gsp0 : 0) + span_delta(gscale + gk * sgb) + kk * sgb);
+        usc = reinterpret_cast<const uint16_t*>(sc0 + gate_scale_region(C, H, G) + (second ? usp0 : 0) +
+                                                span_delta(gscale + (gk + I) * sgb) + kk * sgb);
+        uix = ch.a + (second ? 1 : 0);
+        row = second ? kk : ch.i0 + kk;
+      };
+      const uint16_t *gs0, *us0, *gs1, *us1;
+      int ux0, r0, ux1 = -1, r1 = 0;
+      job(warp, gs0, us0, ux0, r0);
+      const int w1 = warp + kFW;
+      if (w1 < ch.n) job(w1, gs1, us1, ux1, r1);
+      if (ux1 == ux0) {
+        fused_gate_job2(a, xs, st + warp * rowb, st + (C + warp) * rowb, gs0, us0, st + w1 * rowb,
+                        st + (C + w1) * rowb, gs1, us1, ux0, r0, r1, uoff_s, upairs_s, ptok_s, gshift, M);
+      } else {
+        fused_gate_job(a, xs, st + warp * rowb, st + (C + warp) * rowb, gs0, us0, ux0, r0, uoff_s, upairs_s, ptok_s,
+                       gshift, M);
+        if (ux1 >= 0)
+          fused_gate_job(a, xs, st + w1 * rowb, st + (C + w1) * rowb, gs1, us1, ux1, r1, uoff_s, upairs_s, ptok_s,
+                         gshift, M);
+      }
     }
     release(c);
   }
@@ -689,32 +812,45 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     if (live) live = wait_chunk(c);
     const Chunk ch = chunk_s[c];
     if (live && hw < h1) {
+      // the chunk's pairs are contiguous in sorted order; four partials at a time are independent, then they are
+      // accumulated in pair order (the order of the three-kernel path)
       const uint8_t* st = ring + (size_t)(c % S) * SB;
-      for (int b = 0; b < ch.n; ++b) {
-        const int uix = ch.a + b;
-        const int64_t r0 = (int64_t)uniq_s[uix] * H + h0;
-        const uint8_t* wr = st + ((size_t)b * rpc + warp) * drowb;
-        const uint16_t* sc = reinterpret_cast<const uint16_t*>(
-            st + (size_t)f.kd * rpc * drowb + (size_t)b * down_scale_region(rpc, I, G) + span_delta(dscale + r0 * dsb) +
-            warp * dsb);
-        for (int p = uoff_s[uix]; p < uoff_s[uix + 1]; ++p) {
-          const int pair = upairs_s[p];
-          const uint8_t* xr = reinterpret_cast<const uint8_t*>(inter_s + (size_t)pair * PI);
-          float part = 0.f;
-          for (int cc = lane; cc < nchd; cc += 32) {
-            const int j = cc >> 5;
-            const uint2 wq = *reinterpret_cast<const uint2*>(wr + cc * 8);
-            u64 x01, x23, x45, x67;
-            Nib8Acc A;
-            nib8_zero(A);
-            inter_pairs<false>(xr + (size_t)((j * 2) * Ld + lane) * 16, x01, x23, x45, x67);
-            nib8x2(wq.x, x01, x23, x45, x67, M, A);
-            inter_pairs<false>(xr + (size_t)((j * 2 + 1) * Ld + lane) * 16, x01, x23, x45, x67);
-            nib8x2(wq.y, x01, x23, x45, x67, M, A);
-            part = fmaf(nib8_fold(A), h2f(sc[cc >> dshift]), part);
+      const int pa = uoff_s[ch.a], pb = uoff_s[ch.a + ch.n];
+      for (int p0 = pa; p0 < pb; p0 += 4) {
+        float part[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          part[q] = 0.f;
+          const int p = p0 + q;
+          if (p < pb) {
+            const int b = pu_s[p] - ch.a;
+            const int64_t r0 = (int64_t)uniq_s[ch.a + b] * H + h0;
+            const uint8_t* wr = st + ((size_t)b * rpc + warp) * drowb;
+            const uint16_t* sc = reinterpret_cast<const uint16_t*>(st + (size_t)f.kd * rpc * drowb +
+                                                                   (size_t)b * down_scale_region(rpc, I, G) +
+                                                                   span_delta(dscale + r0 * dsb) + warp * dsb);
+            const uint8_t* xr = reinterpret_cast<const uint8_t*>(inter_s + (size_t)upairs_s[p] * PI);
+            for (int cc = lane; cc < nchd; cc += 32) {
+              const int j = cc >> 5;
+              const uint2 wq = *reinterpret_cast<const uint2*>(wr + cc * 8);
+              u64 x01, x23, x45, x67;
+              Nib8Acc A;
+              nib8_zero(A);
+              inter_pairs<false>(xr + (size_t)((j * 2) * Ld + lane) * 16, x01, x23, x45, x67);
+              nib8x2(wq.x, x01, x23, x45, x67, M, A);
+              inter_pairs<false>(xr + (size_t)((j * 2 + 1) * Ld + lane) * 16, x01, x23, x45, x67);
+              nib8x2(wq.y, x01, x23, x45, x67, M, A);
+              part[q] = fmaf(nib8_fold(A), h2f(sc[cc >> dshift]), part[q]);
+            }
           }
-          float* slotacc = acc_w + ptok_s[p] * 32 + lane;
-          *slotacc = fmaf(wts_s[pair], part, *slotacc);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int p = p0 + q;
+          if (p < pb) {
+            float* slotacc = acc_w + ptok_s[p] * 32 + lane;
+            *slotacc = fmaf(wts_s[upairs_s[p]], part[q], *slotacc);
+          }
         }
       }
     }
@@ -752,10 +888,10 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       a.hidden[o] = f.next_norm ? fmaf(g, shared_t, hh + routed_t) : hh + fmaf(g, shared_t, routed_t);
     }
   }
-  // No copy may still be landing when the CTA exits: wait (bounded) for the last chunk issued to every stage and
-  // for the entry copies (immediate on the normal path).
+  // No copy may still be landing when the CTA exits. On the normal path every copy was waited for by its
+  // consumers; after an abort, wait (bounded) for the last chunk issued to every stage and for the entry copies.
   cta_sync();
-  if (tid == 0) {
+  if (tid == 0 && vload(&abort_s)) {
     for (int s = 0; s < S; ++s)
       if (issued_s[s] > 0) bar_wait(&full_b[s], (uint32_t)((issued_s[s] - 1) & 1));
     bar_wait(&rbar, 0);
@@ -827,14 +963,15 @@ static bool fused_plan(const moe_layer_weights& w, int T, FusedCfg* out) {
     return false;
   const int rpc = (w.H + grid - 1) / grid;
   if (rpc > kFW) return false;  // one output row per warp
-  int C = kFW;
-  while (C > 1 && 2 * C * (w.H / 2) > 32 * 1024) C >>= 1;
-  int kd = 8;
-  while (kd > 1 && kd * rpc * (w.I / 2) > 32 * 1024) --kd;
+  // gate/up jobs per chunk: two per warp at the smallest batches (their activation loads are shared), else one
+  int C = T <= 2 ? 2 * kFW : kFW;
+  while (C > 1 && 2 * C * (w.H / 2) > (C > kFW ? 64 : 32) * 1024) C >>= 1;
+  int kd = C > kFW ? 16 : 8;
+  while (kd > 1 && down_stage_bytes(kd, rpc, w.I, w.G) > gate_stage_bytes(C, w.H, w.G)) --kd;
   // chunk-list bound: the CTA's gate/up jobs split at chunk size and expert boundaries, plus the down chunks
   const int P = T * w.TOPK;
   const int per_cta = P * w.I / grid + 1;
-  if (per_cta / C + per_cta / w.I + 2 + (P + kd - 1) / kd > kMaxChunks) return false;
+  if (per_cta / C + 2 + (P + kd - 1) / kd > kMaxChunks) return false;
   const int sb = (std::max(gate_stage_bytes(C, w.H, w.G), down_stage_bytes(kd, rpc, w.I, w.G)) + 127) / 128 * 128;
   const int limit = max_smem_optin() - 6 * 1024;  // static shared memory of the kernel
   for (int s = kMaxStages; s >= 2; --s) {
