@@ -4,8 +4,8 @@
 // One CTA per SM, 16 warps. Weight bytes move with bulk asynchronous copies (cp.async.bulk, completion counted on
 // shared-memory mbarriers) issued by one thread, a few large contiguous copies per CTA, so no warp stalls issuing
 // loads and every byte is requested as soon as its dependency allows:
-//   entry     bulk copies of the routing-independent weights this CTA owns: router rows (router row r -> CTA
-//             r % G; the shared gate vector is row E), shared-expert gate/up row pairs (pair j -> CTA j % G) and
+//   entry     bulk copies of the routing-independent weights this CTA owns: router rows (rows 2c, 2c + 1 -> CTA c;
+//             the shared gate vector is row E), shared-expert gate/up row pairs (pairs 4c .. 4c + 3 -> CTA c) and
 //             the shared-expert down rows of the CTA's output rows [h0, h1);
 //   phase R   RMSNorm of every token (every CTA, into shared memory), router logits of the CTA's rows -> global;
 //             arrive at grid barrier 1; the shared-expert gate/up pairs while the barrier settles; wait;
@@ -157,6 +157,13 @@ __device__ __forceinline__ void cta_sync() {
   __syncwarp();
 }
 
+// Relaxed read of the barrier counter at entry: any value from before this CTA's first arrival gives the base, and an
+// acquire load would hold back the bulk copies issued after it.
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -480,7 +487,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     }
   }
   if (tid == 0) {
-    const unsigned long long gb = ld_acquire_u64(f.gbar);  // consumed at the end of this block
+    const unsigned long long gb = ld_relaxed_u64(f.gbar);  // consumed at the end of this block
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_b[s], 1);
       cnt_s[s] = 0;
@@ -491,26 +498,17 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     abort_s = 0;
     mbar_fence_init();
     // ---- entry: routing-independent weights of this CTA
-    uint32_t tx = 0;
-    for (int r = 0; r < kRouterRows; ++r) tx += (cta + r * grid < nrows) ? H * 2 : 0;
-    expect_tx(&rbar, tx);
-    for (int r = 0; r < kRouterRows; ++r) {
-      const int row = cta + r * grid;
-      if (row < nrows)
-        bulk_g2s(router_s + (size_t)r * H * 2, row < E ? a.w.router + (int64_t)row * H : a.w.shared_gate, H * 2,
-                 &rbar);
-    }
-    tx = 0;
-    for (int r = 0; r < kSgu; ++r) tx += (cta + r * grid < Is) ? 2 * H * 2 : 0;
-    tx += h0 < h1 ? (h1 - h0) * Is * 2 : 0;
-    expect_tx(&sbar, tx);
-    for (int r = 0; r < kSgu; ++r) {
-      const int j = cta + r * grid;
-      if (j < Is) {
-        uint8_t* dst = sgu_s + (size_t)r * 2 * H * 2;
-        bulk_g2s(dst, a.w.shared_gate_up + (int64_t)j * H, H * 2, &sbar);
-        bulk_g2s(dst + H * 2, a.w.shared_gate_up + (int64_t)(Is + j) * H, H * 2, &sbar);
-      }
+    // router rows [r0, r1) of this CTA, contiguous in the router matrix up to row E (the shared gate vector)
+    const int r0 = min(nrows, kRouterRows * cta), r1 = min(nrows, r0 + kRouterRows), re = min(r1, E);
+    expect_tx(&rbar, (uint32_t)((r1 - r0) * H * 2));
+    if (re > r0) bulk_g2s(router_s, a.w.router + (int64_t)r0 * H, (re - r0) * H * 2, &rbar);
+    if (r1 > re) bulk_g2s(router_s + (size_t)(re - r0) * H * 2, a.w.shared_gate, H * 2, &rbar);
+    // shared-expert pairs [j0, j1): gate rows j0 .. j1 - 1 and up rows Is + j0 .. Is + j1 - 1, one copy each
+    const int j0 = min(Is, kSgu * cta), j1 = min(Is, j0 + kSgu);
+    expect_tx(&sbar, (uint32_t)(2 * (j1 - j0) * H * 2 + (h0 < h1 ? (h1 - h0) * Is * 2 : 0)));
+    if (j1 > j0) {
+      bulk_g2s(sgu_s, a.w.shared_gate_up + (int64_t)j0 * H, (j1 - j0) * H * 2, &sbar);
+      bulk_g2s(sgu_s + (size_t)kSgu * H * 2, a.w.shared_gate_up + (int64_t)(Is + j0) * H, (j1 - j0) * H * 2, &sbar);
     }
     if (h0 < h1) bulk_g2s(sdn_s, a.w.shared_down + (int64_t)h0 * Is, (h1 - h0) * Is * 2, &sbar);
     base_s = (gb / grid) * grid;
@@ -559,7 +557,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
 
   // Router rows (warps 0..1): gemv_bf16 order per lane over its 32-k chunks, butterfly sum.
   if (warp < kRouterRows) {
-    const int row = cta + warp * grid;
+    const int row = kRouterRows * cta + warp;
     if (row < nrows) {
       const bool ok = __all_sync(0xffffffffu, bar_wait(&rbar, 0));
       if (!ok) {
@@ -594,7 +592,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
 
   // Shared-expert gate/up pairs of this CTA while the router barrier settles (warps 2..5).
   if (warp >= 2 && warp < 2 + kSgu) {
-    const int r = warp - 2, j = cta + r * grid;
+    const int r = warp - 2, j = kSgu * cta + r;
     if (j < Is) {
       const bool ok = __all_sync(0xffffffffu, bar_wait(&sbar, 0));
       if (!ok) {
@@ -603,8 +601,8 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
           abort_s = 1;
         }
       } else {
-        const uint8_t* grow = sgu_s + (size_t)r * 2 * H * 2;
-        const uint8_t* urow = grow + H * 2;
+        const uint8_t* grow = sgu_s + (size_t)r * H * 2;
+        const uint8_t* urow = sgu_s + (size_t)(kSgu + r) * H * 2;
         for (int t = 0; t < T; ++t) {
           const float4* xs4 = reinterpret_cast<const float4*>(xs + t * H);
           float g = 0.f, u = 0.f;
