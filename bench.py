@@ -367,7 +367,7 @@ def prefill_case(m, shape, K, W, stream, world, dev, peaks, cpu_seconds, do_cpu)
     return out
 
 
-def ep_case(m, shape, K, W, stream, world, rank, dev, peaks):
+def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
     """Config 5: EP_TOKENS tokens per step over `world` ranks, experts sharded evenly, device time max over ranks."""
     T = EP_TOKENS // world
     with torch.cuda.stream(stream):
@@ -391,7 +391,12 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks):
         st = ep.EpRank(layer, rank, world, T)
         ex = ep.NcclExchange()
         sizes = []
-        step = lambda i: sizes.append(ep.ep_step(st, ex, hidden, attn, normed, stream=stream))  # noqa: E731
+        flag = torch.zeros(1, device=dev)
+        if exchange == "peers":
+            st.open_peers()
+            step = lambda i: ep.ep_step_peers(st, hidden, attn, normed, stream=stream, flag=flag)  # noqa: E731
+        else:
+            step = lambda i: sizes.append(ep.ep_step(st, ex, hidden, attn, normed, stream=stream))  # noqa: E731
         for i in range(W):
             step(i)
         torch.cuda.synchronize()
@@ -412,12 +417,22 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks):
         clocks.stop()
         clk = clocks.summary(t0, t1)
         ms = max_over_ranks(e0.elapsed_time(e1), world)
-        how = (f"mvcc_b200.ep: {shape.E // world} experts per rank; records exchanged with NCCL all_to_all_single "
-               "(counts, records, partial rows), one host read of the counts per step; shared expert on a side "
-               "stream")
-        recv = {"records_sent_per_step": float(np.mean([s for s, _ in sizes])),
-                "records_received_per_step": float(np.mean([r for _, r in sizes]))}
+        if exchange == "peers":
+            how = (f"mvcc_b200.ep: {shape.E // world} experts per rank; the dispatch kernel stores each record into the "
+                   "destination rank's buffer and the expert stage stores each partial row into the source rank's "
+                   "buffer over NVLink (CUDA IPC mappings), a one-element NCCL all-reduce after each as the barrier; "
+                   "no host synchronisation; shared expert on a side stream")
+            counts = st.send_count.cpu().numpy()
+            recv = {"records_sent_last_step": int(counts.sum())}
+        else:
+            how = (f"mvcc_b200.ep: {shape.E // world} experts per rank; records exchanged with NCCL all_to_all_single "
+                   "(counts, records, partial rows), one host read of the counts per step; shared expert on a side "
+                   "stream")
+            recv = {"records_sent_per_step": float(np.mean([s for s, _ in sizes])),
+                    "records_received_per_step": float(np.mean([r for _, r in sizes]))}
         assert st.error_word() == 0
+        barrier(world)
+        st.close_peers()
     hidden.copy_(hidden0)
     fl = prefill_flops(shape, EP_TOKENS)
     tf = fl["block"] / (ms / K * 1e-3) / 1e12
@@ -427,6 +442,7 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks):
            "n_gpus": world, "scaling": "strong", "how": how,
            "tflops": {"achieved_job": tf, "per_gpu": tf / world, "frac_per_gpu": tf / world / peaks["tf_sustained"],
                       "peak_kind": f"{peaks['kind']} bf16 sustained", "flops_per_step": fl["block"]},
+           "exchange": "none (one GPU)" if world == 1 else exchange,
            "gpu_launches_per_step_per_rank": launches_per_step(T) if world == 1 else 14,
            "clocks": clk}
     if recv:
@@ -527,7 +543,7 @@ def b200_arm(args, rank, world, local):
                                          args.cpu_seconds / 2, do_cpu)
     if not args.no_ep and world <= 8 and shape.E % world == 0:
         torch.cuda.empty_cache()
-        result["ep_prefill"] = ep_case(m, shape, args.ep_steps, W, stream, world, rank, dev, peaks)
+        result["ep_prefill"] = ep_case(m, shape, args.ep_steps, W, stream, world, rank, dev, peaks, args.ep_exchange)
     if world == 1 and rank == 0 and not args.no_cpu:
         with torch.cuda.stream(stream):
             l0 = m.synth_layer(shape, seed=1000, stream=stream)
@@ -635,6 +651,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
     ap.add_argument("--ep-steps", type=int, default=20)
     ap.add_argument("--no-ep", action="store_true", help="skip the config-5 expert-parallel measurement")
+    ap.add_argument("--ep-exchange", choices=["peers", "nccl"], default="peers",
+                    help="expert-parallel exchange: kernels' peer-memory stores (default) or NCCL all-to-all")
     ap.add_argument("--quick", action="store_true", help="headline batch only (no decode_batches sweep)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)

@@ -60,6 +60,46 @@ MOE_API int moe_ep_combine(const moe_layer_weights* w, void* workspace, size_t w
                            const uint16_t* next_rms1, int T, int world, const int32_t* tok_pos, const float* ret,
                            moe_stream_t stream);
 
+/* ---- peer-memory exchange: the same three stages with the data moved by the kernels themselves over NVLink.
+ *
+ * Every rank owns a receive buffer of moe_ep_recv_bytes(w, world, cap) bytes (records [world][cap][record], source
+ * s's block at s * cap, then int32 counts [world]) and a return buffer of moe_ep_ret_bytes bytes (fp32 rows
+ * [world][cap][H], destination d's block at d * cap), cap = the most tokens any rank passes per call. `peers` holds
+ * every rank's buffers as addresses valid on the calling device (moe_ipc_open of the peers' handles; the local
+ * buffers for this rank). moe_ep_dispatch_peers stores this rank's records and counts straight into the destination
+ * ranks' receive buffers; moe_ep_experts_peers reads this rank's receive buffer and stores each record's partial
+ * row straight into its source rank's return buffer; moe_ep_combine then reads the local return buffer with the
+ * tok_pos of the dispatch. Between dispatch and experts, and between experts and combine, every rank must pass a
+ * collective barrier (any collective, e.g. a one-element all-reduce, ordered on the same stream after the kernels):
+ * the kernels end their peer stores with system-scope fences, so the barrier publishes them. No host
+ * synchronisation, no per-step allocation. */
+typedef struct moe_ep_peers {
+  void* recv[8];
+  int32_t* rcount[8];  /* inside each recv buffer (its counts) */
+  float* ret[8];
+  int32_t rank, cap;
+} moe_ep_peers;
+MOE_API size_t moe_ep_recv_bytes(const moe_layer_weights* w, int world, int cap);
+MOE_API size_t moe_ep_ret_bytes(const moe_layer_weights* w, int world, int cap);
+/* Offset of the counts inside a receive buffer. */
+MOE_API size_t moe_ep_rcount_offset(const moe_layer_weights* w, int world, int cap);
+MOE_API int moe_ep_dispatch_peers(const moe_layer_weights* w, void* workspace, size_t workspace_bytes,
+                                  const float* hidden, const uint16_t* attn_out, uint16_t* normed, int T, int world,
+                                  const moe_ep_peers* peers, int32_t* send_count, int32_t* tok_pos,
+                                  moe_stream_t stream);
+/* workspace sized by moe_workspace_bytes(w_local, max(world * cap, 8)). */
+MOE_API int moe_ep_experts_peers(const moe_layer_weights* w_local, void* workspace, size_t workspace_bytes, int world,
+                                 const moe_ep_peers* peers, moe_stream_t stream);
+
+/* Setup helpers for the exchange buffers (the only calls of this library that allocate): device memory that CUDA
+ * IPC can share, its 64-byte IPC handle, and the mapping of a peer's handle into this process (cudaMalloc,
+ * cudaIpcGetMemHandle, cudaIpcOpenMemHandle with lazy peer access, and their releases). */
+MOE_API int moe_device_alloc(size_t bytes, void** ptr);
+MOE_API int moe_device_free(void* ptr);
+MOE_API int moe_ipc_handle(void* ptr, void* handle64);
+MOE_API int moe_ipc_open(const void* handle64, void** ptr);
+MOE_API int moe_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

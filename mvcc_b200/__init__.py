@@ -79,6 +79,16 @@ _SIGS = {
     "moe_ep_dispatch": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
     "moe_ep_experts": (_I, [_W, _P, ctypes.c_size_t, _P, _I, _P, _P]),
     "moe_ep_combine": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P]),
+    "moe_ep_recv_bytes": (ctypes.c_size_t, [_W, _I, _I]),
+    "moe_ep_ret_bytes": (ctypes.c_size_t, [_W, _I, _I]),
+    "moe_ep_rcount_offset": (ctypes.c_size_t, [_W, _I, _I]),
+    "moe_ep_dispatch_peers": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
+    "moe_ep_experts_peers": (_I, [_W, _P, ctypes.c_size_t, _I, _P, _P]),
+    "moe_device_alloc": (_I, [ctypes.c_size_t, ctypes.POINTER(_P)]),
+    "moe_device_free": (_I, [_P]),
+    "moe_ipc_handle": (_I, [_P, _P]),
+    "moe_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "moe_ipc_close": (_I, [_P]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(_lib, _name)

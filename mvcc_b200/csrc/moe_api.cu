@@ -393,7 +393,7 @@ int moe_ep_experts(const moe_layer_weights* w_local, void* workspace, size_t wor
   a.xstride = ep_record_bytes(w_local->H, w_local->TOPK) / 2;
   a.routed = part;
   cudaError_t e = prefill_bits_clear(a, s);
-  if (e == cudaSuccess) e = ep_mark(a, static_cast<const uint8_t*>(recv), s);
+  if (e == cudaSuccess) e = ep_mark(a, static_cast<const uint8_t*>(recv), nullptr, 0, s);
   if (e == cudaSuccess) e = prefill_routed_marked(a, s);
   return (int)e;
 }
@@ -417,5 +417,106 @@ int moe_ep_combine(const moe_layer_weights* w, void* workspace, size_t workspace
   return (int)prefill_combine(a, (cudaStream_t)stream);
 }
 
-}  // extern "C"
+size_t moe_ep_recv_bytes(const moe_layer_weights* w, int world, int cap) {
+  if (!ep_geometry_ok(w, world) || cap < 1) return 0;
+  return ws_align((size_t)world * cap * ep_record_bytes(w->H, w->TOPK)) + ws_align(sizeof(int32_t) * world);
+}
 
+size_t moe_ep_rcount_offset(const moe_layer_weights* w, int world, int cap) {
+  if (!ep_geometry_ok(w, world) || cap < 1) return 0;
+  return ws_align((size_t)world * cap * ep_record_bytes(w->H, w->TOPK));
+}
+
+size_t moe_ep_ret_bytes(const moe_layer_weights* w, int world, int cap) {
+  if (!ep_geometry_ok(w, world) || cap < 1) return 0;
+  return (size_t)world * cap * w->H * sizeof(float);
+}
+
+static bool peers_ok(const moe_ep_peers* p, int world) {
+  if (!p || p->rank < 0 || p->rank >= world || p->cap < 1) return false;
+  for (int d = 0; d < world; ++d)
+    if (!p->recv[d] || !p->rcount[d] || !p->ret[d] || reinterpret_cast<uintptr_t>(p->recv[d]) % 16 ||
+        reinterpret_cast<uintptr_t>(p->ret[d]) % 16)
+      return false;
+  return true;
+}
+
+static EpPeers to_peers(const moe_ep_peers* p) {
+  EpPeers q;
+  memset(&q, 0, sizeof q);
+  for (int d = 0; d < kEpMaxWorld; ++d) {
+    q.recv[d] = static_cast<uint8_t*>(p->recv[d]);
+    q.rcount[d] = p->rcount[d];
+    q.ret[d] = p->ret[d];
+  }
+  q.rank = p->rank;
+  q.cap = p->cap;
+  return q;
+}
+
+int moe_ep_dispatch_peers(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const float* hidden,
+                          const uint16_t* attn_out, uint16_t* normed, int T, int world, const moe_ep_peers* peers,
+                          int32_t* send_count, int32_t* tok_pos, moe_stream_t stream) {
+  if (!ep_geometry_ok(w, world) || !workspace || T < 1 || !peers_ok(peers, world) || T > peers->cap)
+    return (int)cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < layout_for(w, T).total)
+    return (int)cudaErrorInvalidValue;
+  if (!hidden || !attn_out || !normed || !send_count || !tok_pos || !w->router || !w->rms2 || !w->shared_gate)
+    return (int)cudaErrorInvalidValue;
+  const cudaStream_t s = (cudaStream_t)stream;
+  BlockArgs a = make_args(w, workspace, layout_for(w, T), T);
+  a.hidden = const_cast<float*>(hidden);
+  a.attn_out = attn_out;
+  a.normed = normed;
+  cudaError_t e = prefill_norm(a, s);
+  if (e == cudaSuccess) e = prefill_router(a, s);
+  if (e == cudaSuccess) e = ep_plan_pack_peers(a, world, to_peers(peers), send_count, tok_pos, s);
+  return (int)e;
+}
+
+int moe_ep_experts_peers(const moe_layer_weights* w_local, void* workspace, size_t workspace_bytes, int world,
+                         const moe_ep_peers* peers, moe_stream_t stream) {
+  if (!shape_ok(w_local) || !prefill_supported(*w_local) || !workspace || world < 1 || world > kEpMaxWorld ||
+      !peers_ok(peers, world) || !weights_present(w_local, false, true, false))
+    return (int)cudaErrorInvalidValue;
+  const int R = world * peers->cap;
+  const WsLayout L = layout_for(w_local, std::max(R, kPrefillMinT));
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < L.total) return (int)cudaErrorInvalidValue;
+  const cudaStream_t s = (cudaStream_t)stream;
+  const EpPeers q = to_peers(peers);
+  BlockArgs a = make_args(w_local, workspace, L, R);
+  a.normed = reinterpret_cast<uint16_t*>(q.recv[q.rank]);
+  a.xstride = ep_record_bytes(w_local->H, w_local->TOPK) / 2;
+  cudaError_t e = prefill_bits_clear(a, s);
+  if (e == cudaSuccess) e = ep_mark(a, q.recv[q.rank], q.rcount[q.rank], q.cap, s);
+  if (e == cudaSuccess) e = prefill_routed_marked_gemms(a, s);
+  if (e == cudaSuccess) e = ep_return_peers(a, world, q, s);
+  return (int)e;
+}
+
+int moe_device_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return (int)cudaErrorInvalidValue;
+  return (int)cudaMalloc(ptr, bytes);
+}
+
+int moe_device_free(void* ptr) { return (int)cudaFree(ptr); }
+
+int moe_ipc_handle(void* ptr, void* handle64) {
+  if (!ptr || !handle64) return (int)cudaErrorInvalidValue;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e == cudaSuccess) memcpy(handle64, &h, sizeof h);
+  return (int)e;
+}
+
+int moe_ipc_open(const void* handle64, void** ptr) {
+  if (!ptr || !handle64) return (int)cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof h);
+  return (int)cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+int moe_ipc_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
+
+}  // extern "C"

@@ -5,6 +5,10 @@
 // normed activations plus, per slot, the expert's id on that rank (-1 when the slot's expert lives elsewhere) and
 // the routing weight. The receiving rank runs its experts over the records (the prefill GEMMs) and returns one
 // fp32 partial row per record; the source sums the partials of a token in rank order (moe_prefill.cu's combine).
+// The exchange either packs the records into one send buffer grouped by destination (for an all-to-all library
+// call), or, in peer mode, stores each record straight into the destination rank's receive buffer and each partial
+// row straight into the source rank's return buffer through peer-memory mappings (NVLink), every such store
+// followed by a system-scope fence so that a collective barrier after the kernel publishes it.
 // The reference runs the block on one GPU (qwen.cu:429-448); this split has no counterpart there.
 #include "moe_device.cuh"
 #include "moe_ep.h"
@@ -26,7 +30,7 @@ __device__ __forceinline__ uint32_t dest_mask(const int32_t* idx, int K, int E, 
 // One CTA: per-destination counts of the tokens in a contiguous token range per thread, block scans, then each
 // token's record index per destination (-1 = not sent).
 __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const BlockArgs a, int world, int32_t* tok_pos,
-                                                               int32_t* send_count) {
+                                                               int32_t* send_count, int peer_mode, EpPeers peers) {
   __shared__ int sm[32];
   const int T = a.T, K = a.w.TOPK, E = a.w.E, El = E / world, tid = threadIdx.x;
   const int per = (T + kPlanThreads - 1) / kPlanThreads;
@@ -45,9 +49,15 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const BlockArgs a
   for (int d = 0; d < kEpMaxWorld; ++d) {
     int tot;
     run[d] = block_excl_scan(c[d], sm, &tot);
-    off[d] = o;
+    off[d] = peer_mode ? d * peers.cap : o;
     o += tot;
-    if (tid == 0 && d < world) send_count[d] = tot;
+    if (tid == 0 && d < world) {
+      send_count[d] = tot;
+      if (peer_mode) {
+        peers.rcount[d][peers.rank] = tot;
+        __threadfence_system();
+      }
+    }
   }
   for (int t = t0; t < t1; ++t) {
     const uint32_t m = dest_mask(a.idx + (int64_t)t * K, K, E, El);
@@ -63,7 +73,8 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const BlockArgs a
 
 // One CTA per token: its normed row (held in registers) and per-destination meta into each of its records.
 __global__ void __launch_bounds__(kPackThreads) ep_pack_kernel(const BlockArgs a, int world, int rec_bytes,
-                                                               uint8_t* send, const int32_t* tok_pos) {
+                                                               uint8_t* send, const int32_t* tok_pos, int peer_mode,
+                                                               EpPeers peers) {
   const int t = blockIdx.x, tid = threadIdx.x, H = a.w.H, K = a.w.TOPK, E = a.w.E, El = E / world;
   const int nv = H / 8;  // 16-byte chunks of a row (H <= 4096: at most 4 per thread)
   const uint4* src = reinterpret_cast<const uint4*>(a.normed + (int64_t)t * H);
@@ -82,7 +93,8 @@ __global__ void __launch_bounds__(kPackThreads) ep_pack_kernel(const BlockArgs a
   for (int d = 0; d < world; ++d) {
     const int pos = tok_pos[(int64_t)t * world + d];
     if (pos < 0) continue;
-    uint8_t* rec = send + (int64_t)pos * rec_bytes;
+    uint8_t* rec = peer_mode ? peers.recv[d] + ((int64_t)peers.rank * peers.cap + (pos - d * peers.cap)) * rec_bytes
+                             : send + (int64_t)pos * rec_bytes;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int i = tid + r * kPackThreads;
@@ -94,14 +106,24 @@ __global__ void __launch_bounds__(kPackThreads) ep_pack_kernel(const BlockArgs a
       reinterpret_cast<float*>(rec + 2 * H + 4 * K)[tid] = wt;
     }
   }
+  if (peer_mode) __threadfence_system();
 }
 
 // One thread per (record, slot): meta into a.idx / a.wts, local slots into the pair bitmaps.
-__global__ void __launch_bounds__(256) ep_mark_kernel(const BlockArgs a, const uint8_t* recv, int rec_bytes) {
+__global__ void __launch_bounds__(256) ep_mark_kernel(const BlockArgs a, const uint8_t* recv, int rec_bytes,
+                                                      const int32_t* rcount, int cap) {
   const int K = a.w.TOPK, H = a.w.H, P = a.T * K;
   const int p = blockIdx.x * 256 + threadIdx.x;
   if (p >= P) return;
   const int r = p / K, k = p - r * K;
+  if (rcount) {  // rows past a source's count hold no record
+    const int src = r / cap;
+    if (r - src * cap >= __ldcg(rcount + src)) {
+      a.idx[p] = -1;
+      a.wts[p] = 0.f;
+      return;
+    }
+  }
   const uint8_t* rec = recv + (int64_t)r * rec_bytes;
   const int e = reinterpret_cast<const int32_t*>(rec + 2 * H)[k];
   a.idx[p] = e;
@@ -114,18 +136,65 @@ __global__ void __launch_bounds__(256) ep_mark_kernel(const BlockArgs a, const u
   atomicOr(a.bits + (int64_t)e * a.nwp + (p >> 5), 1u << (p & 31));
 }
 
+// One CTA per record row r = src * cap + j of the receive buffer (peer mode): rows with a record sum their valid
+// slots in slot order (as prefill_combine_kernel's mode 1) and store the fp32 row into rank src's return buffer.
+__global__ void __launch_bounds__(256) ep_return_kernel(const BlockArgs a, int world, EpPeers peers) {
+  const int r = blockIdx.x, tid = threadIdx.x, H = a.w.H, K = a.w.TOPK;
+  const int src = r / peers.cap, j = r - src * peers.cap;
+  if (j >= __ldcg(peers.rcount[peers.rank] + src)) return;
+  bool ok[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) ok[k] = k < K && (unsigned)a.idx[(int64_t)r * K + k] < (unsigned)a.w.E;
+  float4* dst = reinterpret_cast<float4*>(peers.ret[src] + ((int64_t)peers.rank * peers.cap + j) * H);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int i = tid + q * 256;
+    if (i >= H / 4) continue;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (!ok[k]) continue;
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(a.slot + ((int64_t)r * K + k) * H) + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    dst[i] = acc;
+  }
+  __threadfence_system();
+}
+
+static const EpPeers kNoPeers = {};
+
 cudaError_t ep_plan_pack(const BlockArgs& a, int world, uint8_t* send, int32_t* send_count, int32_t* tok_pos,
                          cudaStream_t s) {
-  ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(a, world, tok_pos, send_count);
+  ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(a, world, tok_pos, send_count, 0, kNoPeers);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  ep_pack_kernel<<<a.T, kPackThreads, 0, s>>>(a, world, ep_record_bytes(a.w.H, a.w.TOPK), send, tok_pos);
+  ep_pack_kernel<<<a.T, kPackThreads, 0, s>>>(a, world, ep_record_bytes(a.w.H, a.w.TOPK), send, tok_pos, 0,
+                                              kNoPeers);
   return cudaGetLastError();
 }
 
-cudaError_t ep_mark(const BlockArgs& a, const uint8_t* recv, cudaStream_t s) {
+cudaError_t ep_plan_pack_peers(const BlockArgs& a, int world, const EpPeers& peers, int32_t* send_count,
+                               int32_t* tok_pos, cudaStream_t s) {
+  ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(a, world, tok_pos, send_count, 1, peers);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  ep_pack_kernel<<<a.T, kPackThreads, 0, s>>>(a, world, ep_record_bytes(a.w.H, a.w.TOPK), nullptr, tok_pos, 1,
+                                              peers);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_mark(const BlockArgs& a, const uint8_t* recv, const int32_t* rcount, int cap, cudaStream_t s) {
   const int P = a.T * a.w.TOPK;
-  ep_mark_kernel<<<(P + 255) / 256, 256, 0, s>>>(a, recv, ep_record_bytes(a.w.H, a.w.TOPK));
+  ep_mark_kernel<<<(P + 255) / 256, 256, 0, s>>>(a, recv, ep_record_bytes(a.w.H, a.w.TOPK), rcount, cap);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_return_peers(const BlockArgs& a, int world, const EpPeers& peers, cudaStream_t s) {
+  ep_return_kernel<<<world * peers.cap, 256, 0, s>>>(a, world, peers);
   return cudaGetLastError();
 }
 

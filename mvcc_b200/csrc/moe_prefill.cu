@@ -435,6 +435,11 @@ cudaError_t prefill_routed_marked(const BlockArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+cudaError_t prefill_routed_marked_gemms(const BlockArgs& a, cudaStream_t s) {
+  cudaError_t e = run_sort(a, SORT_MARKED, s);
+  return e == cudaSuccess ? run_experts(a, s) : e;
+}
+
 cudaError_t prefill_combine(const BlockArgs& a, cudaStream_t s) {
   prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 2);
   return cudaGetLastError();

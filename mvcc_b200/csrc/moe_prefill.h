@@ -29,6 +29,8 @@ cudaError_t prefill_bits_clear(const BlockArgs& a, cudaStream_t s);
 // moe() on pair bitmaps, a.idx and a.wts the caller's kernel already wrote: scan, scatter, grouped GEMMs, slot-order
 // sum into a.routed (slots with an index outside [0, E) contribute nothing);
 cudaError_t prefill_routed_marked(const BlockArgs& a, cudaStream_t s);
+// the same without the final slot-order sum: the per-slot partials stay in a.slot;
+cudaError_t prefill_routed_marked_gemms(const BlockArgs& a, cudaStream_t s);
 // gated residual combine into a.hidden (+ next RMSNorm); routed rows from a.ep_pos / a.ep_ret when set.
 cudaError_t prefill_combine(const BlockArgs& a, cudaStream_t s);
 

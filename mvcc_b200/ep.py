@@ -12,9 +12,11 @@ expert. One step on each rank (include/moe_ep.h):
   5. all-to-all of the partial rows back, reverse splits;
   6. moe_ep_combine: per token the partials in rank order + gated shared expert into hidden.
 
-`ep_step` runs one rank's step with its exchanges through `NcclExchange` (all_to_all_single over a torch.distributed
-process group: NCCL on GPUs); `emulated_step` runs every rank's stages in one process on one GPU, the exchanges as
-device copies, for single-GPU parity tests of the multi-rank numerics. The reference runs the block on one GPU only
+Two exchanges: `ep_step_peers` (the default of ExpertParallelMoe) lets the kernels store the records and the partial
+rows straight into the peers' buffers over NVLink (CUDA IPC mappings), with a one-element all-reduce after each stage
+as the barrier that publishes them: no host synchronisation. `ep_step` moves packed buffers with all_to_all_single
+(one host read of the counts per step). `emulated_step` / `emulated_step_peers` run every rank's stages in one
+process on one GPU, for single-GPU parity tests of the multi-rank numerics. The reference runs the block on one GPU only
 (qwen.cu:429-448); the split has no counterpart there.
 """
 import contextlib
@@ -24,6 +26,41 @@ import dataclasses
 import torch
 
 from . import (MoeBlock, MoeLayer, MoeLayerWeights, MoeShape, _check, _lib, _ptr, _stream)
+
+
+class MoeEpPeers(ctypes.Structure):
+    """ctypes mirror of `moe_ep_peers` (include/moe_ep.h)."""
+
+    _fields_ = [("recv", ctypes.c_void_p * 8), ("rcount", ctypes.c_void_p * 8), ("ret", ctypes.c_void_p * 8),
+                ("rank", ctypes.c_int32), ("cap", ctypes.c_int32)]
+
+
+class DeviceBuffer:
+    """cudaMalloc'd device memory (shareable through CUDA IPC) owned by this object."""
+
+    def __init__(self, nbytes):
+        p = ctypes.c_void_p()
+        _check(_lib.moe_device_alloc(nbytes, ctypes.byref(p)), "moe_device_alloc")
+        self.ptr, self.nbytes = p.value, nbytes
+
+    def ipc_handle(self):
+        h = ctypes.create_string_buffer(64)
+        _check(_lib.moe_ipc_handle(ctypes.c_void_p(self.ptr), h), "moe_ipc_handle")
+        return h.raw
+
+    def free(self):
+        if self.ptr:
+            _lib.moe_device_free(ctypes.c_void_p(self.ptr))
+            self.ptr = None
+
+    def __del__(self):
+        self.free()
+
+
+def _ipc_open(handle):
+    p = ctypes.c_void_p()
+    _check(_lib.moe_ipc_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(p)), "moe_ipc_open")
+    return p.value
 
 
 class ExpertShard:
@@ -77,7 +114,77 @@ class EpRank:
         self.sout = torch.empty(max_tokens, s.H, dtype=torch.int16, device=dev)
         self.side = torch.cuda.Stream(device=dev)
         self._shared_done = None
+        # peer-mode exchange buffers: records in ([world][cap][record] + counts), partial rows back ([world][cap][H])
+        lc = ctypes.byref(layer.c)
+        self.recv_bytes = _lib.moe_ep_recv_bytes(lc, world, max_tokens)
+        self.ret_bytes = _lib.moe_ep_ret_bytes(lc, world, max_tokens)
+        self.rcount_off = _lib.moe_ep_rcount_offset(lc, world, max_tokens)
+        self.precv = DeviceBuffer(self.recv_bytes)
+        self.pret = DeviceBuffer(self.ret_bytes)
+        self.peers = None
+        self._opened = []
         torch.cuda.current_stream(dev).synchronize()
+
+    def set_peers(self, recv_ptrs, ret_ptrs):
+        """Every rank's receive and return buffers as addresses valid on this device (rank order)."""
+        pe = MoeEpPeers()
+        for d in range(self.world):
+            pe.recv[d] = recv_ptrs[d]
+            pe.rcount[d] = recv_ptrs[d] + self.rcount_off
+            pe.ret[d] = ret_ptrs[d]
+        pe.rank, pe.cap = self.rank, self.max_tokens
+        self.peers = pe
+
+    def open_peers(self, group=None):
+        """Exchange CUDA IPC handles of the exchange buffers over the process group and map the peers' buffers."""
+        import torch.distributed as dist
+        mine = (self.precv.ipc_handle(), self.pret.ipc_handle())
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine, group=group)
+        recv, ret = [], []
+        for d in range(self.world):
+            if d == self.rank:
+                recv.append(self.precv.ptr)
+                ret.append(self.pret.ptr)
+            else:
+                pr, pt = _ipc_open(allh[d][0]), _ipc_open(allh[d][1])
+                self._opened += [pr, pt]
+                recv.append(pr)
+                ret.append(pt)
+        self.set_peers(recv, ret)
+
+    def close_peers(self):
+        for p in self._opened:
+            _lib.moe_ipc_close(ctypes.c_void_p(p))
+        self._opened = []
+        self.peers = None
+
+    # -- peer-mode stages
+    def dispatch_peers(self, hidden, attn_out, normed, stream):
+        T = hidden.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > max_tokens {self.max_tokens}")
+        _check(_lib.moe_ep_dispatch_peers(ctypes.byref(self.layer.c), _ptr(self.src.ws), self.src.ws_bytes,
+                                          _ptr(hidden), _ptr(attn_out), _ptr(normed), T, self.world,
+                                          ctypes.byref(self.peers), _ptr(self.send_count), _ptr(self.tok_pos),
+                                          _stream(stream)), "moe_ep_dispatch_peers")
+        self.side.wait_stream(stream)
+        _check(_lib.moe_shared_expert(ctypes.byref(self.layer.c), _ptr(self.sh.ws), self.sh.ws_bytes, _ptr(normed),
+                                      _ptr(self.sout), T, _stream(self.side)), "moe_shared_expert")
+        self._shared_done = torch.cuda.Event()
+        self._shared_done.record(self.side)
+
+    def experts_peers(self, stream):
+        _check(_lib.moe_ep_experts_peers(ctypes.byref(self.shard.c), _ptr(self.xws), self.xws_bytes, self.world,
+                                         ctypes.byref(self.peers), _stream(stream)), "moe_ep_experts_peers")
+
+    def combine_peers(self, hidden, attn_out, normed, next_rms1, stream):
+        T = hidden.shape[0]
+        stream.wait_event(self._shared_done)
+        _check(_lib.moe_ep_combine(ctypes.byref(self.layer.c), _ptr(self.src.ws), self.src.ws_bytes, _ptr(hidden),
+                                   _ptr(attn_out), _ptr(self.sout), _ptr(normed), _ptr(next_rms1), T, self.world,
+                                   _ptr(self.tok_pos), ctypes.c_void_p(self.pret.ptr), _stream(stream)),
+               "moe_ep_combine")
 
     # -- stages (all asynchronous on `stream`)
     def dispatch(self, hidden, attn_out, normed, stream):
@@ -151,19 +258,50 @@ def ep_step(rank_state, exchange, hidden, attn_out, normed, next_rms1=None, stre
     return S, R
 
 
+def ep_step_peers(rank_state, hidden, attn_out, normed, next_rms1=None, stream=None, group=None, flag=None):
+    """One expert-parallel step of one rank with the peer-memory exchange: the dispatch kernel stores the records
+    into the destination ranks' buffers and the expert stage stores the partial rows into the source ranks' buffers
+    (NVLink); a one-element all-reduce after each publishes the stores to every rank. No host synchronisation."""
+    import torch.distributed as dist
+    st = torch.cuda.current_stream(rank_state.device) if stream is None else stream
+    if flag is None:
+        flag = torch.zeros(1, device=rank_state.device)
+    with torch.cuda.stream(st):
+        rank_state.dispatch_peers(hidden, attn_out, normed, st)
+        dist.all_reduce(flag, group=group)
+        rank_state.experts_peers(st)
+        dist.all_reduce(flag, group=group)
+        rank_state.combine_peers(hidden, attn_out, normed, next_rms1, st)
+
+
 class ExpertParallelMoe:
     """The expert-parallel MoE layer of one rank: `forward` is MoeBlock.forward for this rank's tokens, with the
     routed experts sharded over the process group."""
 
-    def __init__(self, layer: MoeLayer, max_tokens: int, group=None, rank=None, world=None):
+    def __init__(self, layer: MoeLayer, max_tokens: int, group=None, rank=None, world=None, exchange="peers"):
+        """exchange: "peers" (records and partial rows stored by the kernels into the peers' buffers over NVLink,
+        CUDA IPC mappings set up here) or "nccl" (all_to_all_single of packed buffers, one host read per step)."""
         import torch.distributed as dist
+        self.group = group
         self.rank = dist.get_rank(group) if rank is None else rank
         self.world = dist.get_world_size(group) if world is None else world
         self.state = EpRank(layer, self.rank, self.world, max_tokens)
+        self.mode = exchange
         self.exchange = NcclExchange(group)
+        self.flag = torch.zeros(1, device=self.state.device)
+        if exchange == "peers":
+            self.state.open_peers(group)
+        elif exchange != "nccl":
+            raise ValueError(f"unknown exchange {exchange!r}")
 
     def forward(self, hidden, attn_out, normed, next_rms1=None, stream=None):
+        if self.mode == "peers":
+            return ep_step_peers(self.state, hidden, attn_out, normed, next_rms1, stream, self.group, self.flag)
         return ep_step(self.state, self.exchange, hidden, attn_out, normed, next_rms1, stream)
+
+    def close(self):
+        """Unmaps the peers' buffers (before the process group goes away)."""
+        self.state.close_peers()
 
     def error_word(self):
         return self.state.error_word()
@@ -198,4 +336,24 @@ def emulated_step(ranks, hiddens, attn_outs, normeds, next_rms1=None, stream=Non
     return C
 
 
-__all__ = ["ExpertShard", "EpRank", "NcclExchange", "ExpertParallelMoe", "ep_step", "emulated_step", "MoeShape"]
+def emulated_step_peers(ranks, hiddens, attn_outs, normeds, next_rms1=None, stream=None):
+    """All ranks of a peer-mode step in one process on one GPU: every rank's buffers are local, each rank's kernels
+    store into the others' buffers directly, and stream order stands in for the barriers."""
+    W = len(ranks)
+    recv = [r.precv.ptr for r in ranks]
+    ret = [r.pret.ptr for r in ranks]
+    for r in ranks:
+        if r.peers is None:
+            r.set_peers(recv, ret)
+    st = torch.cuda.current_stream() if stream is None else stream
+    with torch.cuda.stream(st):
+        for r in range(W):
+            ranks[r].dispatch_peers(hiddens[r], attn_outs[r], normeds[r], st)
+        for r in range(W):
+            ranks[r].experts_peers(st)
+        for r in range(W):
+            ranks[r].combine_peers(hiddens[r], attn_outs[r], normeds[r], next_rms1, st)
+
+
+__all__ = ["ExpertShard", "EpRank", "NcclExchange", "ExpertParallelMoe", "ep_step", "ep_step_peers", "emulated_step",
+           "emulated_step_peers", "MoeShape", "MoeEpPeers", "DeviceBuffer"]

@@ -156,3 +156,29 @@ def test_all_tokens_on_one_shard():
         ok = stable_rows(S128, ref["logits"], gpu_logits=tr["logits"].cpu().numpy())
         assert O.max_rel_err(hid[r].cpu().numpy()[ok], ref["hidden"][ok]) < TOL_BF16
         assert ranks[r].error_word() == 0
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_peer_exchange_equals_packed_exchange(world):
+    """The peer-memory exchange (records and partial rows stored by the kernels into the other ranks' buffers) gives
+    the packed all-to-all exchange's results bit for bit: same records, same reductions, same rank order."""
+    E = ep()
+    L, layer = layer128()
+    Ts = [30 + 11 * r for r in range(world)]
+    a_ranks, acts, a_hid, a_nrm, _ = run_emulated(layer, world, Ts, 900 + world)
+    b_ranks = [E.EpRank(layer, r, world, max(Ts)) for r in range(world)]
+    hid = [torch.from_numpy(np.ascontiguousarray(h, np.float32)).cuda() for h, _ in acts]
+    att = [to_dev16(a) for _, a in acts]
+    nrm = [torch.zeros(T, S128.H, dtype=torch.int16, device="cuda") for T in Ts]
+    E.emulated_step_peers(b_ranks, hid, att, nrm)
+    torch.cuda.synchronize()
+    for r in range(world):
+        assert np.array_equal(hid[r].cpu().numpy(), a_hid[r].cpu().numpy())
+        assert np.array_equal(host16(nrm[r]), host16(a_nrm[r]))
+        assert b_ranks[r].error_word() == 0
+    # a second step on the same buffers (stale counts and records of the first must not leak)
+    E.emulated_step_peers(b_ranks, hid, att, nrm)
+    E.emulated_step(a_ranks, a_hid, [to_dev16(a) for _, a in acts], a_nrm)
+    torch.cuda.synchronize()
+    for r in range(world):
+        assert np.array_equal(hid[r].cpu().numpy(), a_hid[r].cpu().numpy())

@@ -1,6 +1,7 @@
-"""Expert-parallel step over real NCCL on 2 GPUs (skipped with fewer): every rank runs mvcc_b200.ep.ExpertParallelMoe
-on its own tokens; its result must equal, bit for bit, the single-process emulation of the same ranks (the exchange
-moves bytes, so the NCCL path and the emulation run the same kernels on the same data), and match the oracle's
+"""Expert-parallel step on 2 GPUs (skipped with fewer), with either exchange: NCCL all-to-all of packed buffers, or
+the kernels' own peer-memory stores over NVLink (CUDA IPC mappings) with all-reduce barriers. Every rank runs
+mvcc_b200.ep.ExpertParallelMoe on its own tokens; its result must equal, bit for bit, the single-process emulation of
+the same ranks (the exchange moves bytes, so both run the same kernels on the same data), and match the oracle's
 expert-parallel restatement within the block's tolerances."""
 import datetime
 import os
@@ -21,7 +22,7 @@ def free_port():
         return s.getsockname()[1]
 
 
-def worker(rank, world, port, q):
+def worker(rank, world, port, q, mode):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -43,10 +44,11 @@ def worker(rank, world, port, q):
             return h, to_dev16(acts[r][1]), torch.zeros(Ts[r], s.H, dtype=torch.int16, device="cuda")
 
         h, a, n = dev(rank)
-        moe = E.ExpertParallelMoe(layer, max(Ts))
+        moe = E.ExpertParallelMoe(layer, max(Ts), exchange=mode)
         moe.forward(h, a, n)
         torch.cuda.synchronize()
         err = moe.error_word()
+        moe.close()
         # the same ranks emulated in this process
         ranks = [E.EpRank(layer, r, world, max(Ts)) for r in range(world)]
         hs, as_, ns = zip(*[dev(r) for r in range(world)])
@@ -66,12 +68,13 @@ def worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_ep_step_over_nccl_matches_emulation():
+@pytest.mark.parametrize("mode", ["nccl", "peers"])
+def test_ep_step_over_nccl_matches_emulation(mode):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=worker, args=(r, WORLD, port, q, mode)) for r in range(WORLD)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in range(WORLD))
