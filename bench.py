@@ -446,7 +446,7 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
            "gpu_launches_per_step_per_rank": launches_per_step(T) if world == 1 else 14,
            "clocks": clk}
     if recv:
-        out["exchange"] = recv
+        out["exchange_stats"] = recv
     return out
 
 

@@ -459,6 +459,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
       const GemmTile t = load_tile(p, it / nN);
       const int nt = it % nN, ab = j & 1;
       if (!wait_bar(&acc_full[ab], (j >> 1) & 1, abort_flag, p.err)) break;
+      __syncwarp();  // lane 0's arrive of the previous item can leave the warp split until here
       fence_after_sync();
       const int r = q * 32 + lane;
       const bool valid = r < t.mcount;
@@ -557,12 +558,14 @@ __global__ void __launch_bounds__(kGThreads, 1)
     for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
       const int sbuf = j & 1;
       if (!wait_bar(&sc_full[sbuf], (j >> 1) & 1, abort_flag, p.err)) break;
+      __syncwarp();
       const uint8_t* scb = smem + c.sc + (size_t)sbuf * BN * c.sstride;
       for (int kt = 0; kt < nk; ++kt, ++g) {
         const int gr = g / c.rk, sr = gr % SR, sub = g - gr * c.rk, s = g % SA;
         ok = wait_bar(&fullR[sr], (gr / SR) & 1, abort_flag, p.err);
         ok = ok && (g < SA || wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err));
         if (!ok) break;
+        __syncwarp();  // lane 0's arrives of the previous step can leave the warp split until here
         const uint8_t* rawp = smem + c.raw + (size_t)sr * BN * RB + sub * 32;
         uint8_t* bdst = smem + c.b + (size_t)s * BN * 128;
 #pragma unroll
