@@ -370,6 +370,7 @@ def prefill_case(m, shape, K, W, stream, world, dev, peaks, cpu_seconds, do_cpu)
 def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
     """Config 5: EP_TOKENS tokens per step over `world` ranks, experts sharded evenly, device time max over ranks."""
     T = EP_TOKENS // world
+    peer_note = None
     with torch.cuda.stream(stream):
         layer = m.synth_layer(shape, seed=3000, stream=stream)  # same weights on every rank; each keeps its shard
         hidden, attn = m.synth_activations(shape, T, seed=31 + rank, stream=stream)
@@ -393,7 +394,19 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
         sizes = []
         flag = torch.zeros(1, device=dev)
         if exchange == "peers":
-            st.open_peers()
+            # every rank maps the peers' buffers; if any rank cannot, all fall back to the NCCL exchange together
+            fail = ""
+            try:
+                st.open_peers()
+            except Exception as e:  # noqa: BLE001 - reported in the JSON line
+                fail = f"{type(e).__name__}: {e}"
+            ok = torch.tensor([0.0 if fail else 1.0], device=dev)
+            torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
+            if ok.item() < 1.0:
+                st.close_peers()
+                exchange = "nccl"
+                peer_note = f"peer mapping unavailable, NCCL exchange used ({fail or 'on another rank'})"
+        if exchange == "peers":
             step = lambda i: ep.ep_step_peers(st, hidden, attn, normed, stream=stream, flag=flag)  # noqa: E731
         else:
             step = lambda i: sizes.append(ep.ep_step(st, ex, hidden, attn, normed, stream=stream))  # noqa: E731
@@ -447,6 +460,8 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
            "clocks": clk}
     if recv:
         out["exchange_stats"] = recv
+    if peer_note:
+        out["note"] = peer_note
     return out
 
 
