@@ -486,8 +486,9 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       pre_d[r] = reinterpret_cast<const uint2*>(a.attn_out)[i];
     }
   }
+  unsigned long long gb = 0;  // thread 0: the barrier counter at entry, consumed before the first arrival
   if (tid == 0) {
-    const unsigned long long gb = ld_relaxed_u64(f.gbar);  // consumed at the end of this block
+    gb = ld_relaxed_u64(f.gbar);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_b[s], 1);
       cnt_s[s] = 0;
@@ -511,7 +512,6 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       bulk_g2s(sgu_s + (size_t)kSgu * H * 2, a.w.shared_gate_up + (int64_t)(Is + j0) * H, (j1 - j0) * H * 2, &sbar);
     }
     if (h0 < h1) bulk_g2s(sdn_s, a.w.shared_down + (int64_t)h0 * Is, (h1 - h0) * Is * 2, &sbar);
-    base_s = (gb / grid) * grid;
   }
   cta_sync();
 
@@ -588,6 +588,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       }
     }
   }
+  if (tid == 0) base_s = (gb / grid) * grid;
   grid_arrive(f.gbar);
 
   // Shared-expert gate/up pairs of this CTA while the router barrier settles (warps 2..5).
