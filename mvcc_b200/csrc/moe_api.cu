@@ -1,9 +1,10 @@
-// moe_api.cu -- the extern "C" entry points declared in include/moe_block.h.
+// moe_api.cu -- the extern "C" entry points declared in include/moe_block.h and include/moe_ep.h.
 //
-// Host-side launch code replacing the MoE part of forward() (qwen.cu:429-448) and moe() (qwen.cu:345-363).
-// Every entry point validates the shape and the workspace size before launching anything and returns
-// cudaErrorInvalidValue on a violation; no entry point allocates memory or synchronises the stream (except
-// moe_workspace_error, which reads the error word back).
+// Host-side launch code replacing the MoE part of forward() (qwen.cu:429-448) and moe() (qwen.cu:345-363), and the
+// expert-parallel stages. Every compute entry point validates the shape and the workspace size before launching
+// anything and returns cudaErrorInvalidValue on a violation; none allocates memory or synchronises the stream (except
+// moe_workspace_error, which reads the error word back). The setup helpers moe_device_alloc / moe_ipc_* of the
+// expert-parallel exchange buffers are the only calls that allocate or map memory.
 #include <algorithm>
 #include <atomic>
 #include <climits>

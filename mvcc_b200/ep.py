@@ -3,21 +3,19 @@
 Rank d of `world` holds experts [d * E / world, (d + 1) * E / world) and the replicated router, norm and shared
 expert. One step on each rank (include/moe_ep.h):
 
-  1. moe_ep_dispatch: residual RMSNorm, router + top-k, one dispatch record per (token, rank owning >= 1 of its
-     experts), grouped by destination;
-  2. the shared expert of the rank's own tokens on a side stream, overlapping 3-5;
-  3. all-to-all of the per-destination record counts, read back to the host (the one host synchronisation of a step:
-     the record exchange needs its split sizes);
-  4. all-to-all of the records; moe_ep_experts on the received records -> one fp32 partial row per record;
-  5. all-to-all of the partial rows back, reverse splits;
-  6. moe_ep_combine: per token the partials in rank order + gated shared expert into hidden.
+  1. dispatch: residual RMSNorm, router + top-k, one record per (token, rank owning >= 1 of its experts);
+  2. the shared expert of the rank's own tokens on a side stream, overlapping 3-4;
+  3. the records reach their ranks, which run their experts over them -> one fp32 partial row per record;
+  4. the partial rows return to their source ranks; combine: per token the partials in rank order + the gated shared
+     expert into hidden.
 
-Two exchanges: `ep_step_peers` (the default of ExpertParallelMoe) lets the kernels store the records and the partial
-rows straight into the peers' buffers over NVLink (CUDA IPC mappings), with a one-element all-reduce after each stage
-as the barrier that publishes them: no host synchronisation. `ep_step` moves packed buffers with all_to_all_single
-(one host read of the counts per step). `emulated_step` / `emulated_step_peers` run every rank's stages in one
-process on one GPU, for single-GPU parity tests of the multi-rank numerics. The reference runs the block on one GPU only
-(qwen.cu:429-448); the split has no counterpart there.
+Two exchanges. `ep_step_peers` (the default of ExpertParallelMoe): the dispatch kernel stores each record into the
+destination rank's receive buffer and the expert stage stores each partial row into the source rank's return buffer,
+over NVLink through CUDA IPC mappings, with a one-element all-reduce after each stage as the barrier that publishes
+the stores; no host synchronisation. `ep_step`: packed buffers through all_to_all_single (counts first, read back to
+the host for the split sizes, then records and partial rows). `emulated_step` / `emulated_step_peers` run every
+rank's stages in one process on one GPU, for single-GPU parity tests of the multi-rank numerics. The reference runs
+the block on one GPU only (qwen.cu:429-448); the split has no counterpart there.
 """
 import contextlib
 import ctypes
