@@ -79,3 +79,42 @@ def test_expert_bytes_match_reference_formula():
     """decode_weight_bytes (qwen.cu:463-477) at G=64: 1,671,168 bytes per routed expert."""
     import mvcc_b200
     assert mvcc_b200.MoeShape().expert_bytes() == 1_671_168
+
+
+def test_expert_parallel_entry_points_check_before_launch():
+    """The expert-parallel stages reject unsupported splits and missing buffers with cudaErrorInvalidValue before any
+    launch, size their exchange buffers by formula, and launch nothing for an empty receive set."""
+    import mvcc_b200
+    import mvcc_b200.ep as ep
+    lib = mvcc_b200._lib
+    w = _w()
+    wp = ctypes.byref(w)
+    rec = lib.moe_ep_record_bytes(wp)
+    assert rec == 2 * 2048 + 8 * 8 == 4160
+    # world must divide E into shards of a multiple of 16 experts, at least TOPK, at most 8 ranks
+    for world, ok in ((1, True), (2, True), (8, True), (3, False), (16, False), (32, False)):
+        nb = lib.moe_ep_recv_bytes(wp, world, 64)
+        assert (nb > 0) == ok
+        if ok:
+            off = lib.moe_ep_rcount_offset(wp, world, 64)
+            assert off % 256 == 0 and off >= world * 64 * rec and nb >= off + 4 * world
+            assert lib.moe_ep_ret_bytes(wp, world, 64) == world * 64 * 2048 * 4
+    ws = ctypes.c_void_p(1 << 20)  # never dereferenced: every call below fails its checks first
+    assert lib.moe_ep_dispatch(wp, ws, 1 << 30, None, None, None, 4, 3, None, None, None, None) == 1
+    assert lib.moe_ep_dispatch(wp, None, 1 << 30, None, None, None, 4, 2, None, None, None, None) == 1
+    assert lib.moe_ep_combine(wp, ws, 1 << 30, None, None, None, None, None, 4, 2, None, None, None) == 1
+    # empty receive set: nothing to do, nothing launched
+    wl = _w(E=128)
+    for n in ("exp_gu_q", "exp_gu_s", "exp_dn_q", "exp_dn_s"):
+        setattr(wl, n, 1 << 20)  # present but never read: no record arrived
+    assert lib.moe_ep_experts(ctypes.byref(wl), ws, 1 << 30, None, 0, None, None) == 0
+    # peer mode: missing buffers or a rank outside the world
+    peers = ep.MoeEpPeers()
+    peers.rank, peers.cap = 0, 4
+    assert lib.moe_ep_dispatch_peers(wp, ws, 1 << 30, None, None, None, 4, 2, ctypes.byref(peers), None, None,
+                                     None) == 1
+    for d in range(2):
+        peers.recv[d] = peers.rcount[d] = peers.ret[d] = 1 << 20
+    peers.rank = 2
+    assert lib.moe_ep_experts_peers(ctypes.byref(wl), ws, 1 << 30, 2, ctypes.byref(peers), None) == 1
+    assert ctypes.sizeof(ep.MoeEpPeers) == 3 * 8 * 8 + 8

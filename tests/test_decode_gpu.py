@@ -226,6 +226,35 @@ def test_invalid_expert_index_is_flagged_not_faulted(orc):
     assert O.max_rel_err(routed[:1].cpu().numpy(), rr) < TOL_INT4
 
 
+def test_grid_barrier_timeout_is_reported_and_recoverable(orc):
+    """Failure detection without a GPU fault: the fused kernel's grid barriers wait on a counter in the workspace.
+    Setting it to 2^64 - G makes the G arrivals wrap it past zero, below a target it then never reaches: every
+    bounded wait runs out, the kernel records MOE_ERR_BARRIER (4) and returns; after moe_workspace_init the next call
+    is correct again."""
+    m = mb()
+    s, L, layer = layer_for("h1024_g64")
+    T = 1
+    blk = m.MoeBlock(layer, T)
+    grid = torch.cuda.get_device_properties(0).multi_processor_count
+    assert (1 << 64) % grid != 0
+    gbar = blk.ws[512:520].view(torch.int64)  # the workspace's grid-barrier counter (ws_layout: ticket, err, gbar)
+    gbar.fill_(-grid)  # 2^64 - G as uint64
+    hidden, attn = O.make_activations(s, T, 91)
+    h = torch.from_numpy(np.ascontiguousarray(hidden, np.float32)).cuda()
+    normed = torch.zeros(T, s.H, dtype=torch.int16, device="cuda")
+    blk.forward(h, to_dev16(attn), normed)
+    torch.cuda.synchronize()
+    assert blk.error_word() == 4
+    m._check(m._lib.moe_workspace_init(m._ptr(blk.ws), blk.ws_bytes, m._stream(None)), "moe_workspace_init")
+    torch.cuda.synchronize()
+    h = torch.from_numpy(np.ascontiguousarray(hidden, np.float32)).cuda()
+    blk.forward(h, to_dev16(attn), normed)
+    torch.cuda.synchronize()
+    ref = orc.block_forward(s, L, hidden, attn, mode=0)
+    assert O.max_rel_err(h.cpu().numpy(), ref["hidden"]) < TOL_BF16
+    assert blk.error_word() == 0
+
+
 def test_workspace_too_small_is_rejected():
     s, L, layer = layer_for("h512_g32_k4")
     m = mb()
