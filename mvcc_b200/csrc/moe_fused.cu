@@ -25,6 +25,7 @@
 // cooperative, so all CTAs are co-resident. Per-job reductions and numerics are those of the three-kernel path
 // (moe_decode.cu).
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "moe_device.cuh"
@@ -475,20 +476,10 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   const uint8_t* gscale = reinterpret_cast<const uint8_t*>(a.w.exp_gu_s);
   const uint8_t* dscale = reinterpret_cast<const uint8_t*>(a.w.exp_dn_s);
 
-  // token 0's activations are requested before the entry work below, which overlaps their latency
-  float4 pre_h[2];
-  uint2 pre_d[2];
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int i = tid + r * kFThreads;
-    if (i < H / 4) {
-      pre_h[r] = reinterpret_cast<const float4*>(a.hidden)[i];
-      pre_d[r] = reinterpret_cast<const uint2*>(a.attn_out)[i];
-    }
-  }
-  unsigned long long gb = 0;  // thread 0: the barrier counter at entry, consumed before the first arrival
+  // Entry: barriers and the routing-independent weight copies touch only this CTA's shared memory and read only
+  // weights, so under programmatic dependent launch they overlap the previous kernel's tail; everything after
+  // griddepcontrol.wait may read that kernel's outputs (hidden) and reuses the workspace.
   if (tid == 0) {
-    gb = ld_relaxed_u64(f.gbar);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_b[s], 1);
       cnt_s[s] = 0;
@@ -514,6 +505,19 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     if (h0 < h1) bulk_g2s(sdn_s, a.w.shared_down + (int64_t)h0 * Is, (h1 - h0) * Is * 2, &sbar);
   }
   cta_sync();
+  pdl_wait();
+  unsigned long long gb = 0;  // thread 0: the barrier counter at entry, consumed before the first arrival
+  if (tid == 0) gb = ld_relaxed_u64(f.gbar);
+  float4 pre_h[2];  // token 0's activations, requested before the norm's reduction needs them
+  uint2 pre_d[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int i = tid + r * kFThreads;
+    if (i < H / 4) {
+      pre_h[r] = reinterpret_cast<const float4*>(a.hidden)[i];
+      pre_d[r] = reinterpret_cast<const uint2*>(a.attn_out)[i];
+    }
+  }
 
   // ---- phase R: RMSNorm of every token into xs (fp32, permuted); CTA 0 writes `normed`
   for (int t = 0; t < T; ++t) {
@@ -791,6 +795,9 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   if (!grid_wait(f.gbar, base + 2 * (unsigned long long)grid, a.err, &ok_s) && tid == 0) abort_s = 1;
   cta_sync();
 
+  // the next kernel on the stream may start its entry on SMs this grid frees from here on
+  pdl_launch_dependents();
+
   // ---- phase D: stage inter (bf16, permuted) and sinter; reduce this warp's output row over the down chunks
   const int nchd = I >> 4, Ld = min(32, nchd), PI = inter_stride(I);
   uint16_t* inter_s = reinterpret_cast<uint16_t*>(smem + L.xs);
@@ -946,6 +953,16 @@ static int max_smem_optin() {
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Programmatic dependent launch, as for the three-kernel path: on unless the environment sets MOE_B200_PDL=0.
+static bool fused_pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("MOE_B200_PDL");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 struct FusedCfg {
   int stages, stage_bytes, cjobs, kd, rpc;
   size_t smem;
@@ -1023,11 +1040,13 @@ cudaError_t launch_fused_decode(const BlockArgs& a, unsigned long long* gbar, bo
   cfg.blockDim = dim3(kFThreads);
   cfg.dynamicSmemBytes = c.smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = fused_pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, moe_fused_decode_kernel, f);
 }
 
