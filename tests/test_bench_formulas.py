@@ -45,3 +45,24 @@ def test_launch_counts():
     assert b.launches_per_step(7) == 1
     assert b.launches_per_step(8) == 10       # the prefill sequence
     assert b.launches_per_step(4096) == 10
+
+
+def test_clock_summary_reads_reasons_and_window():
+    """The clocks object of the bench line: median SM clock, max clock and the throttle reasons active in the timed
+    region (the samples nvidia-smi prints as 'index, clocks.sm, clocks.max.sm, power, active, hw, hw_thermal,
+    sw_thermal, sw_power_cap')."""
+    b = load_bench()
+    cs = b.ClockSampler.__new__(b.ClockSampler)
+    cs.samples = [
+        (0.5, ["0", "1965", "1965", "500", "0x0", "Not Active", "Not Active", "Not Active", "Not Active"]),
+        (1.0, ["0", "1965", "1965", "700", "0x4", "Not Active", "Not Active", "Not Active", "Active"]),
+        (1.5, ["0", "1900", "1965", "900", "0x4", "Not Active", "Not Active", "Not Active", "Active"]),
+        (9.0, ["0", "1000", "1965", "900", "0x40", "Not Active", "Active", "Not Active", "Not Active"]),
+    ]
+    s = cs.summary(0.9, 2.0)
+    assert s["sm_mhz"] == 1932.5 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"] and s["samples"] == 2 and s["window"] == "timed region"
+    # a short timed region between samples falls back to the samples within 0.5 s of it
+    s = cs.summary(1.6, 1.7)
+    assert s["samples"] == 1 and s["sm_mhz"] == 1900.0 and s["window"] == "within 0.5 s of the timed region"
+    assert cs.summary(20.0, 21.0)["sm_mhz"] is None
