@@ -89,6 +89,17 @@ _SIGS = {
     "moe_ipc_handle": (_I, [_P, _P]),
     "moe_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
     "moe_ipc_close": (_I, [_P]),
+    # weight pack reader (include/moe_pack.h); the structures are declared in mvcc_b200/pack.py
+    "moe_pack_open": (_P, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
+    "moe_pack_close": (None, [_P]),
+    "moe_pack_last_error": (ctypes.c_char_p, [_P]),
+    "moe_pack_geometry_get": (_I, [_P, _P]),
+    "moe_pack_tensor_count": (_I, [_P]),
+    "moe_pack_tensor": (_I, [_P, ctypes.c_char_p, _P]),
+    "moe_pack_tensor_name": (ctypes.c_char_p, [_P, _I]),
+    "moe_pack_layer_host": (_I, [_P, _I, _W]),
+    "moe_pack_layer_bytes": (ctypes.c_size_t, [_P, _I]),
+    "moe_pack_upload_layer": (_I, [_P, _I, _P, ctypes.c_size_t, _W, _P]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(_lib, _name)

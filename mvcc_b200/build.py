@@ -2,7 +2,7 @@
 
     python mvcc_b200/build.py [--verbose] [--force]
 
-Each .cu file compiles to an object in mvcc_b200/_build/ (in parallel), then one shared library is linked next to
+Each .cu and .cpp file compiles to an object in mvcc_b200/_build/ (in parallel), then one shared library is linked next to
 this file, where mvcc_b200/__init__.py loads it. Rebuilds only what changed (source or header newer than object).
 """
 import concurrent.futures
@@ -23,7 +23,7 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", 
 
 
 def _sources():
-    return sorted(f for f in os.listdir(CSRC) if f.endswith(".cu"))
+    return sorted(f for f in os.listdir(CSRC) if f.endswith((".cu", ".cpp")))
 
 
 def _headers_mtime():
@@ -33,7 +33,7 @@ def _headers_mtime():
 
 
 def _compile(src, verbose):
-    obj = os.path.join(BUILD, src[:-3] + ".o")
+    obj = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
     cmd = [NVCC, *ARCH, *FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
     if verbose:
         cmd += ["-Xptxas", "-v"]
@@ -49,7 +49,7 @@ def build(verbose=False, force=False):
     todo = []
     objs = []
     for src in _sources():
-        obj = os.path.join(BUILD, src[:-3] + ".o")
+        obj = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
         objs.append(obj)
         s_m = max(os.path.getmtime(os.path.join(CSRC, src)), hdr)
         if force or verbose or not os.path.exists(obj) or os.path.getmtime(obj) < s_m:

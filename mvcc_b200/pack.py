@@ -1,0 +1,193 @@
+"""The .mvccq weight pack: reading one layer's MoE block into HBM (include/moe_pack.h), and writing packs.
+
+`MoePack` wraps the library's reader: the file is mapped read-only, its header parsed and checked, and
+`MoePack.layer(i)` copies layer i's nine block tensors into one device buffer and returns a `MoeLayer` over it --
+what the reference's `Model::load` does for these tensors (qwen.cu:158-166, 181-190), except that the weights land
+in HBM instead of a zero-copy host mapping (pack.hpp:140-149).
+
+`write_pack` writes the same format as the reference's converter (convert.py:175-211): "MVCCQ001", a little-endian
+u64 header length, the compact JSON header {"config", "tensors"} inside a fixed header slot (1 MiB by default),
+then each blob at the next 64-byte boundary. It exists so packs of synthetic layers (group 64 included, which no
+GPTQ checkpoint can be repacked to) can be written and read back through the same path as converted checkpoints.
+"""
+import ctypes
+import json
+import os
+import struct
+
+import numpy as np
+import torch
+
+from . import MoeError, MoeLayer, MoeLayerWeights, MoeShape, _lib, _stream
+
+MAGIC = b"MVCCQ001"
+HEADER_SLOT = 1 << 20
+BLOB_ALIGN = 64
+
+# Block tensor names inside a layer (convert.py:370-415) for each MoeLayer field, with the stored dtype.
+BLOCK_TENSORS = (
+    ("rms2", "rms2", "bf16"),
+    ("router", "router", "bf16"),
+    ("exp_gu_q", "exp.gate_up.q", "u8"),
+    ("exp_gu_s", "exp.gate_up.s", "f16"),
+    ("exp_dn_q", "exp.down.q", "u8"),
+    ("exp_dn_s", "exp.down.s", "f16"),
+    ("shared_gate_up", "shared.gate_up", "bf16"),
+    ("shared_down", "shared.down", "bf16"),
+    ("shared_gate", "shared.gate", "bf16"),
+)
+_NUMPY = {"bf16": np.uint16, "f16": np.float16, "f32": np.float32, "u8": np.uint8, "i8": np.int8}
+_TORCH = {"bf16": torch.int16, "f16": torch.int16, "f32": torch.float32, "u8": torch.uint8, "i8": torch.int8}
+
+
+class MoePackGeometry(ctypes.Structure):
+    """ctypes mirror of `moe_pack_geometry` (include/moe_pack.h)."""
+
+    _fields_ = [(n, ctypes.c_int32) for n in ("H", "L", "E", "TOPK", "I", "Is", "G")] + [("eps", ctypes.c_float)]
+
+
+class MoePackTensorInfo(ctypes.Structure):
+    """ctypes mirror of `moe_pack_tensor_info` (include/moe_pack.h)."""
+
+    _fields_ = [("off", ctypes.c_uint64), ("nbytes", ctypes.c_uint64), ("host", ctypes.c_void_p),
+                ("ndim", ctypes.c_int32), ("shape", ctypes.c_int64 * 6), ("dtype", ctypes.c_char * 8)]
+
+
+class PackError(MoeError):
+    def __init__(self, rc, msg):
+        super().__init__(f"{msg} (cudaError {rc})")
+        self.rc = rc
+
+
+class MoePack:
+    """A mapped .mvccq pack. Use as a context manager or call close(); tensors read from it are copies."""
+
+    def __init__(self, path):
+        err = ctypes.create_string_buffer(512)
+        h = _lib.moe_pack_open(os.fsencode(path), err, len(err))
+        if not h:
+            raise PackError(1, err.value.decode(errors="replace"))
+        self._h = ctypes.c_void_p(h)
+        self.path = path
+        g = MoePackGeometry()
+        self._check(_lib.moe_pack_geometry_get(self._h, ctypes.byref(g)))
+        self.geometry = g
+        self.shape = MoeShape(H=g.H, E=g.E, TOPK=g.TOPK, I=g.I, Is=g.Is, G=g.G, eps=g.eps)
+        self.layers = g.L
+
+    def _check(self, rc):
+        if rc != 0:
+            raise PackError(rc, _lib.moe_pack_last_error(self._h).decode(errors="replace"))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.moe_pack_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        if _lib is not None:
+            self.close()
+
+    def names(self):
+        return [_lib.moe_pack_tensor_name(self._h, i).decode() for i in range(_lib.moe_pack_tensor_count(self._h))]
+
+    def info(self, name):
+        inf = MoePackTensorInfo()
+        self._check(_lib.moe_pack_tensor(self._h, name.encode(), ctypes.byref(inf)))
+        return inf
+
+    def tensor(self, name):
+        """A host copy of one tensor (bf16 as uint16 bits, f16 as float16)."""
+        inf = self.info(name)
+        raw = ctypes.string_at(inf.host, inf.nbytes)
+        dt = inf.dtype.decode()
+        arr = np.frombuffer(raw, dtype=_NUMPY.get(dt, np.uint8))
+        shape = tuple(inf.shape[:inf.ndim])
+        return arr.reshape(shape) if dt in _NUMPY else arr
+
+    def layer_host(self, layer):
+        """Layer `layer`'s block tensors as host copies keyed by MoeLayer field (checked like layer())."""
+        w = MoeLayerWeights()
+        self._check(_lib.moe_pack_layer_host(self._h, layer, ctypes.byref(w)))
+        return {field: self.tensor(f"L{layer}.{sub}") for field, sub, _ in BLOCK_TENSORS}
+
+    def layer_bytes(self, layer):
+        n = _lib.moe_pack_layer_bytes(self._h, layer)
+        if n == 0:  # the same checks again, for their error code
+            self._check(_lib.moe_pack_layer_host(self._h, layer, ctypes.byref(MoeLayerWeights())) or 1)
+        return n
+
+    def layer(self, layer, device="cuda", stream=None) -> MoeLayer:
+        """Copies layer `layer`'s block into one device buffer (moe_pack_upload_layer) and returns its MoeLayer.
+        The copies are ordered on `stream` (default: the current stream)."""
+        nbytes = self.layer_bytes(layer)
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        w = MoeLayerWeights()
+        self._check(_lib.moe_pack_upload_layer(self._h, layer, ctypes.c_void_p(buf.data_ptr()), nbytes,
+                                               ctypes.byref(w), _stream(stream)))
+        base = buf.data_ptr()
+        t = {}
+        for field, sub, dt in BLOCK_TENSORS:
+            inf = self.info(f"L{layer}.{sub}")
+            off = getattr(w, field) - base
+            shape = tuple(inf.shape[:inf.ndim])
+            t[field] = buf[off:off + inf.nbytes].view(_TORCH[dt]).view(shape)
+        ml = MoeLayer(self.shape, t)
+        ml.storage = buf  # the tensors are views of this buffer
+        return ml
+
+
+def block_entries(layer_index, tensors):
+    """(name, dtype, array) pack entries for one layer's block from MoeLayer-keyed host arrays (bf16 and f16 as
+    16-bit patterns, INT4 packed as uint8), in the order the reference's converter writes them
+    (convert.py:372-415: norms, router, shared expert, routed experts)."""
+    order = ("rms2", "router", "shared_gate_up", "shared_down", "shared_gate", "exp_gu_q", "exp_gu_s", "exp_dn_q",
+             "exp_dn_s")
+    by_field = {f: (sub, dt) for f, sub, dt in BLOCK_TENSORS}
+    out = []
+    for f in order:
+        sub, dt = by_field[f]
+        a = np.ascontiguousarray(tensors[f])
+        if dt in ("bf16", "f16"):
+            a = a.view(np.uint16) if a.dtype != np.float16 else a
+        out.append((f"L{layer_index}.{sub}", dt, a))
+    return out
+
+
+def pack_config(shape: MoeShape, layers, **extra):
+    """The "config" keys the reader needs (convert.py:327-333 names), plus any others the caller passes."""
+    cfg = {"hidden": shape.H, "layers": layers, "experts": shape.E, "topk": shape.TOPK, "inter": shape.I,
+           "shared_inter": shape.Is, "eps": shape.eps, "group": shape.G}
+    cfg.update(extra)
+    return cfg
+
+
+def write_pack(path, config, entries, header_slot=HEADER_SLOT):
+    """Writes a .mvccq pack: `entries` is a sequence of (name, dtype, array) written in that order."""
+    tensors = {}
+    blobs = []
+    off = header_slot
+    for name, dtype, arr in entries:
+        a = np.ascontiguousarray(arr)
+        off += (-off) % BLOB_ALIGN
+        tensors[name] = {"off": off, "nbytes": a.nbytes, "dtype": dtype, "shape": [int(d) for d in a.shape]}
+        blobs.append((off, a))
+        off += a.nbytes
+    hdr = json.dumps({"config": config, "tensors": tensors}, separators=(",", ":")).encode()
+    if 16 + len(hdr) > header_slot:
+        raise ValueError(f"header of {len(hdr)} bytes does not fit the {header_slot}-byte slot")
+    with open(path, "wb") as f:
+        f.write(MAGIC + struct.pack("<Q", len(hdr)) + hdr)
+        f.write(b"\0" * (header_slot - 16 - len(hdr)))
+        pos = header_slot
+        for o, a in blobs:
+            f.write(b"\0" * (o - pos))
+            f.write(a.tobytes())
+            pos = o + a.nbytes
+    return path

@@ -1,0 +1,265 @@
+"""CPU tests of the .mvccq pack reader (include/moe_pack.h) and writer (mvcc_b200.pack).
+
+Pinned to packs written by the reference's own converter (tests/golden/make_pack_fixture.py runs convert.py's
+Writer): the reader must return every tensor byte for byte and the layer geometry; our writer must reproduce the
+reference writer's file byte for byte from the same arrays. Damaged packs must be refused with a reason, and the
+device copy must check its destination before any CUDA call (nothing here touches a GPU)."""
+import ctypes
+import gzip
+import hashlib
+import importlib.util
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+MANIFEST = json.load(open(os.path.join(HERE, "ref_pack_tiny.json")))
+
+
+def _fixture_module():
+    spec = importlib.util.spec_from_file_location("make_pack_fixture", os.path.join(HERE, "make_pack_fixture.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+FIX = _fixture_module()
+
+
+def _unpack(tmp_path, fname):
+    raw = gzip.open(os.path.join(HERE, fname + ".gz"), "rb").read()
+    assert hashlib.sha256(raw).hexdigest() == MANIFEST["files"][fname]["sha256"]
+    p = tmp_path / fname
+    p.write_bytes(raw)
+    return str(p), raw
+
+
+def P():
+    from mvcc_b200 import pack
+    return pack
+
+
+def test_reads_reference_written_pack(tmp_path):
+    path, _ = _unpack(tmp_path, "ref_pack_tiny.mvccq")
+    man = MANIFEST["files"]["ref_pack_tiny.mvccq"]
+    g = MANIFEST["geometry"]
+    with P().MoePack(path) as pk:
+        s = pk.shape
+        assert (s.H, s.E, s.TOPK, s.I, s.Is, s.G, pk.layers) == (g["H"], g["E"], g["TOPK"], g["I"], g["Is"], g["G"],
+                                                                 g["L"])
+        assert abs(s.eps - g["eps"]) < 1e-12
+        assert pk.names() == sorted(man["tensors"])
+        for name, digest in man["tensors"].items():
+            assert hashlib.sha256(pk.tensor(name).tobytes()).hexdigest() == digest, name
+        ents = {n: a for n, _, a in FIX.entries()}
+        for li in range(g["L"]):
+            host = pk.layer_host(li)
+            for field, sub, _ in P().BLOCK_TENSORS:
+                want = ents[f"L{li}.{sub}"]
+                assert host[field].shape == want.shape
+                assert host[field].tobytes() == np.ascontiguousarray(want).tobytes(), (li, field)
+
+
+def test_layer_weights_point_into_the_mapping(tmp_path):
+    """moe_pack_layer_host: the geometry plus host pointers at each tensor's file offset."""
+    import mvcc_b200 as m
+    path, raw = _unpack(tmp_path, "ref_pack_tiny.mvccq")
+    with P().MoePack(path) as pk:
+        w = m.MoeLayerWeights()
+        assert m._lib.moe_pack_layer_host(pk._h, 1, ctypes.byref(w)) == 0
+        assert (w.H, w.E, w.TOPK, w.I, w.Is, w.G) == (64, 4, 2, 32, 32, 32) and w.router_bias is None
+        for field, sub, _ in P().BLOCK_TENSORS:
+            inf = pk.info(f"L1.{sub}")
+            assert getattr(w, field) == inf.host
+            assert ctypes.string_at(inf.host, inf.nbytes) == raw[inf.off:inf.off + inf.nbytes]
+            assert inf.off % 64 == 0
+
+
+def test_writer_matches_reference_writer(tmp_path):
+    _, raw = _unpack(tmp_path, "ref_pack_tiny.mvccq")
+    out = tmp_path / "ours.mvccq"
+    P().write_pack(str(out), FIX.config(), FIX.entries())
+    assert out.read_bytes() == raw
+
+
+def test_layer_bytes_are_256_aligned_sums(tmp_path):
+    path, _ = _unpack(tmp_path, "ref_pack_tiny.mvccq")
+    with P().MoePack(path) as pk:
+        want = sum((pk.info(f"L0.{sub}").nbytes + 255) // 256 * 256 for _, sub, _ in P().BLOCK_TENSORS)
+        assert pk.layer_bytes(0) == want
+
+
+def test_int8_shared_expert_is_not_supported(tmp_path):
+    path, _ = _unpack(tmp_path, "ref_pack_tiny_int8.mvccq")
+    with P().MoePack(path) as pk:
+        assert "L0.shared.gate_up.q8" in pk.names()
+        with pytest.raises(P().PackError) as ei:
+            pk.layer_host(0)
+        assert ei.value.rc == 801 and "int8" in str(ei.value)
+        with pytest.raises(P().PackError) as ei:
+            pk.layer_bytes(1)
+        assert ei.value.rc == 801
+
+
+def test_layer_out_of_range(tmp_path):
+    path, _ = _unpack(tmp_path, "ref_pack_tiny.mvccq")
+    with P().MoePack(path) as pk:
+        for li in (-1, 2):
+            with pytest.raises(P().PackError, match="outside"):
+                pk.layer_host(li)
+
+
+def test_upload_checks_destination_before_any_copy(tmp_path):
+    import mvcc_b200 as m
+    path, _ = _unpack(tmp_path, "ref_pack_tiny.mvccq")
+    with P().MoePack(path) as pk:
+        w = m.MoeLayerWeights()
+        n = pk.layer_bytes(0)
+        lib = m._lib
+        assert lib.moe_pack_upload_layer(pk._h, 0, ctypes.c_void_p(8), n, ctypes.byref(w), None) == 1
+        assert "aligned" in lib.moe_pack_last_error(pk._h).decode()
+        assert lib.moe_pack_upload_layer(pk._h, 0, ctypes.c_void_p(4096), n - 1, ctypes.byref(w), None) == 1
+        assert "needs" in lib.moe_pack_last_error(pk._h).decode()
+        assert lib.moe_pack_upload_layer(pk._h, 0, None, n, ctypes.byref(w), None) == 1
+
+
+def _small_entries(router_rows=None, drop=None):
+    from mvcc_b200 import MoeShape
+    s = MoeShape(H=64, E=4, TOPK=2, I=32, Is=32, G=32)
+    rng = np.random.default_rng(3)
+    t = {"rms2": np.zeros(s.H, np.uint16), "router": np.zeros((router_rows or s.E, s.H), np.uint16),
+         "exp_gu_q": rng.integers(0, 255, (s.E, 2 * s.I, s.H // 2), dtype=np.uint8),
+         "exp_gu_s": np.zeros((s.E, 2 * s.I, s.H // s.G), np.uint16),
+         "exp_dn_q": rng.integers(0, 255, (s.E, s.H, s.I // 2), dtype=np.uint8),
+         "exp_dn_s": np.zeros((s.E, s.H, s.I // s.G), np.uint16),
+         "shared_gate_up": np.zeros((2 * s.Is, s.H), np.uint16), "shared_down": np.zeros((s.H, s.Is), np.uint16),
+         "shared_gate": np.zeros(s.H, np.uint16)}
+    ents = [e for e in P().block_entries(0, t) if e[0] != drop]
+    return s, ents
+
+
+def test_block_tensor_checks(tmp_path):
+    pk_mod = P()
+    s, ents = _small_entries(router_rows=5)
+    p = pk_mod.write_pack(str(tmp_path / "a.mvccq"), pk_mod.pack_config(s, 1), ents, header_slot=4096)
+    with pk_mod.MoePack(p) as pk:
+        with pytest.raises(pk_mod.PackError, match=r"L0\.router is bf16 \[5,64\], expected bf16 \[4,64\]"):
+            pk.layer_host(0)
+    s, ents = _small_entries(drop="L0.exp.down.s")
+    p = pk_mod.write_pack(str(tmp_path / "b.mvccq"), pk_mod.pack_config(s, 1), ents, header_slot=4096)
+    with pk_mod.MoePack(p) as pk:
+        with pytest.raises(pk_mod.PackError, match=r"no tensor L0\.exp\.down\.s"):
+            pk.layer_bytes(0)
+    # a wrong dtype on an otherwise well-formed entry
+    s, ents = _small_entries()
+    ents = [(n, "f16" if n == "L0.rms2" else d, a) for n, d, a in ents]
+    p = pk_mod.write_pack(str(tmp_path / "c.mvccq"), pk_mod.pack_config(s, 1), ents, header_slot=4096)
+    with pk_mod.MoePack(p) as pk:
+        with pytest.raises(pk_mod.PackError, match="rms2 is f16"):
+            pk.layer_host(0)
+
+
+def test_config_without_group_means_128(tmp_path):
+    """Packs written before the "group" key existed carry the converter's default group size (convert.py:311)."""
+    pk_mod = P()
+    from mvcc_b200 import MoeShape
+    s = MoeShape(H=256, E=2, TOPK=1, I=128, Is=128, G=128)
+    cfg = pk_mod.pack_config(s, 1)
+    del cfg["group"]
+    p = pk_mod.write_pack(str(tmp_path / "g.mvccq"), cfg, [("x", "u8", np.zeros(4, np.uint8))], header_slot=1024)
+    with pk_mod.MoePack(p) as pk:
+        assert pk.shape.G == 128
+
+
+def test_unicode_names_round_trip(tmp_path):
+    pk_mod = P()
+    s, ents = _small_entries()
+    name = "L0.xé中\U0001F600"
+    ents.append((name, "f32", np.arange(3, dtype=np.float32)))
+    p = pk_mod.write_pack(str(tmp_path / "u.mvccq"), pk_mod.pack_config(s, 1), ents, header_slot=8192)
+    with pk_mod.MoePack(p) as pk:
+        assert name in pk.names()
+        assert np.array_equal(pk.tensor(name), np.arange(3, dtype=np.float32))
+
+
+def _raw_pack(header: bytes, body: bytes = b"", hlen=None):
+    n = len(header) if hlen is None else hlen
+    return b"MVCCQ001" + struct.pack("<Q", n) + header + body
+
+
+CFG = {"hidden": 64, "layers": 1, "experts": 4, "topk": 2, "inter": 32, "shared_inter": 32, "eps": 1e-6,
+       "group": 32}
+
+
+def _hdr(tensors, cfg=CFG):
+    return json.dumps({"config": cfg, "tensors": tensors}).encode()
+
+
+@pytest.mark.parametrize("case,expect", [
+    ("magic", "bad magic"),
+    ("short", "too short"),
+    ("hlen", "header length"),
+    ("json", "header JSON"),
+    ("trailing", "trailing"),
+    ("nested", "nested too deeply"),
+    ("no_config", "no \"config\""),
+    ("bad_geometry", "config.experts"),
+    ("indivisible", "multiples of group"),
+    ("outside", "outside the file"),
+    ("in_header", "outside the file"),
+    ("nbytes", "nbytes disagrees"),
+    ("fraction", "shape holds a non-integer"),
+    ("escape", "escape"),
+])
+def test_damaged_packs_are_refused(tmp_path, case, expect):
+    body = b"\0" * 256
+    ok_t = {"x": {"off": 0, "nbytes": 16, "dtype": "u8", "shape": [16]}}
+
+    if case == "magic":
+        raw = b"MVCCQ002" + _raw_pack(_hdr({}))[8:]
+    elif case == "short":
+        raw = b"MVCCQ001"
+    elif case == "hlen":
+        raw = _raw_pack(_hdr({}), hlen=1 << 40)
+    elif case == "json":
+        raw = _raw_pack(b'{"config": {"hidden": 64,}}')
+    elif case == "trailing":
+        raw = _raw_pack(_hdr({}) + b" x")
+    elif case == "nested":
+        raw = _raw_pack(b'{"config": ' + b"[" * 100 + b"]" * 100 + b"}")
+    elif case == "no_config":
+        raw = _raw_pack(b'{"tensors": {}}')
+    elif case == "bad_geometry":
+        raw = _raw_pack(_hdr({}, dict(CFG, experts=0)))
+    elif case == "indivisible":
+        raw = _raw_pack(_hdr({}, dict(CFG, hidden=48)))
+    elif case in ("outside", "in_header", "nbytes", "fraction"):
+        h0 = _hdr(ok_t)
+        start = 16 + len(h0) + 64
+        t = {"x": {"off": start, "nbytes": 16, "dtype": "u8", "shape": [16]}}
+        if case == "outside":
+            t["x"]["nbytes"] = 1 << 20
+            t["x"]["shape"] = [1 << 20]
+        elif case == "in_header":
+            t["x"]["off"] = 8
+        elif case == "nbytes":
+            t["x"]["dtype"] = "bf16"
+        else:
+            t["x"]["shape"] = [15.5]
+        h = _hdr(t)
+        h += b" " * (len(h0) + 64 - len(h))  # keep the data start where the offsets assume it
+        raw = _raw_pack(h, body)
+    elif case == "escape":
+        raw = _raw_pack(b'{"config": {"a\\q": 1}, "tensors": {}}')
+    p = tmp_path / f"{case}.mvccq"
+    p.write_bytes(raw)
+    with pytest.raises(P().PackError, match=expect):
+        P().MoePack(str(p))
+
+
+def test_missing_file(tmp_path):
+    with pytest.raises(P().PackError, match="cannot open"):
+        P().MoePack(str(tmp_path / "nope.mvccq"))

@@ -1,0 +1,76 @@
+"""GPU tests of loading a layer from a .mvccq pack into HBM (moe_pack_upload_layer) and running the block on it.
+
+A pack of two seeded layers is written with mvcc_b200.pack.write_pack (whose output the CPU tests pin, byte for
+byte, to the reference's converter); layer 1 is copied to the device through the C ABI; the device bytes must equal
+the file's, and the block on those weights must match the CPU oracle on the same host arrays (int4 bar 2e-2, bf16
+bar 1e-2, max relative error)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16 = 1e-2
+
+
+def _write(tmp_path, s, seeds):
+    from mvcc_b200 import MoeShape, pack
+    ms = MoeShape(H=s.H, E=s.E, TOPK=s.TOPK, I=s.I, Is=s.Is, G=s.G, eps=s.eps)
+    layers = [O.make_layer(s, sd) for sd in seeds]
+    ents = []
+    for li, L in enumerate(layers):
+        ents += pack.block_entries(li, L)
+    path = pack.write_pack(str(tmp_path / "m.mvccq"), pack.pack_config(ms, len(layers)), ents)
+    return path, layers
+
+
+@pytest.mark.parametrize("G", [64, 128])
+@pytest.mark.parametrize("T", [2, 16])
+def test_block_on_uploaded_layer_matches_oracle(tmp_path, G, T):
+    import mvcc_b200 as m
+    from mvcc_b200 import pack
+    s = O.Shape(H=1024, E=32, TOPK=8, I=512, Is=512, G=G)
+    path, layers = _write(tmp_path, s, (21, 22))
+    with pack.MoePack(path) as pk:
+        layer = pk.layer(1)
+    torch.cuda.synchronize()  # pack closed: the copies must not depend on the mapping any more
+    for field in m.MoeLayer.NAMES:
+        host = np.ascontiguousarray(layers[1][field])
+        dev = layer.t[field].cpu().numpy()
+        assert dev.tobytes() == host.tobytes(), field
+    hidden, attn = O.make_activations(s, T, 5)
+    blk = m.MoeBlock(layer, T)
+    h = torch.from_numpy(hidden.copy()).cuda()
+    a = torch.from_numpy(attn.view(np.int16)).cuda()
+    n = torch.zeros(T, s.H, dtype=torch.int16, device="cuda")
+    blk.forward(h, a, n)
+    torch.cuda.synchronize()
+    ref = O.Oracle().block_forward(s, layers[1], hidden, attn, mode=0 if T < 8 else 1)
+    # tokens whose 8th/9th logit margin exceeds twice the GPU-vs-oracle logit error cannot route differently
+    gl = blk.trace(T)["logits"].cpu().numpy()
+    srt = np.sort(ref["logits"], axis=1)[:, ::-1]
+    ok = srt[:, s.TOPK - 1] - srt[:, s.TOPK] > 2 * np.abs(gl - ref["logits"]).max(axis=1) + 1e-6
+    assert ok.mean() >= 0.5
+    assert O.max_rel_err(h.cpu().numpy()[ok], ref["hidden"][ok]) < TOL_BF16
+    nb = O.bf16_to_f32(n.cpu().numpy().view(np.uint16))
+    assert O.max_rel_err(nb[ok], O.bf16_to_f32(ref["normed"])[ok]) < TOL_BF16
+    assert blk.error_word() == 0
+
+
+def test_upload_into_a_short_region_fails_cleanly(tmp_path):
+    import ctypes
+
+    import mvcc_b200 as m
+    from mvcc_b200 import pack
+    s = O.Shape(H=1024, E=32, TOPK=8, I=512, Is=512, G=64)
+    path, _ = _write(tmp_path, s, (21,))
+    with pack.MoePack(path) as pk:
+        n = pk.layer_bytes(0)
+        buf = torch.empty(n, dtype=torch.uint8, device="cuda")
+        w = m.MoeLayerWeights()
+        rc = m._lib.moe_pack_upload_layer(pk._h, 0, ctypes.c_void_p(buf.data_ptr()), n - 256, ctypes.byref(w),
+                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 1
+        assert w.router is None  # nothing filled in
