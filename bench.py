@@ -438,9 +438,9 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
             counts = st.send_count.cpu().numpy()
             recv = {"records_sent_last_step": int(counts.sum())}
         else:
-            how = (f"mvcc_b200.ep: {shape.E // world} experts per rank; records exchanged with NCCL all_to_all_single "
-                   "(counts, records, partial rows), one host read of the counts per step; shared expert on a side "
-                   "stream")
+            how = (f"mvcc_b200.ep: {shape.E // world} experts per rank; count matrix all-gathered (one host read per "
+                   "step, checked on every rank), records and partial rows exchanged with NCCL all_to_all_single; "
+                   "shared expert on a side stream")
             recv = {"records_sent_per_step": float(np.mean([s for s, _ in sizes])),
                     "records_received_per_step": float(np.mean([r for _, r in sizes]))}
         assert st.error_word() == 0

@@ -12,8 +12,8 @@ expert. One step on each rank (include/moe_ep.h):
 Two exchanges. `ep_step_peers` (the default of ExpertParallelMoe): the dispatch kernel stores each record into the
 destination rank's receive buffer and the expert stage stores each partial row into the source rank's return buffer,
 over NVLink through CUDA IPC mappings, with a one-element all-reduce after each stage as the barrier that publishes
-the stores; no host synchronisation. `ep_step`: packed buffers through all_to_all_single (counts first, read back to
-the host for the split sizes, then records and partial rows). `emulated_step` / `emulated_step_peers` run every
+the stores; no host synchronisation. `ep_step`: packed buffers through all_to_all_single (the W x W count matrix
+all-gathered and read back to the host for the split sizes and checked on every rank, then records and partial rows). `emulated_step` / `emulated_step_peers` run every
 rank's stages in one process on one GPU, for single-GPU parity tests of the multi-rank numerics. The reference runs
 the block on one GPU only (qwen.cu:429-448); the split has no counterpart there.
 """
@@ -23,7 +23,7 @@ import dataclasses
 
 import torch
 
-from . import (MoeBlock, MoeLayer, MoeLayerWeights, MoeShape, _check, _lib, _ptr, _stream)
+from . import (MoeBlock, MoeError, MoeLayer, MoeLayerWeights, MoeShape, _check, _lib, _ptr, _stream)
 
 
 class MoeEpPeers(ctypes.Structure):
@@ -219,6 +219,22 @@ class EpRank:
         return w | rc
 
 
+class EpError(MoeError):
+    """An expert-parallel step that cannot complete: a bad record count, or an exchange that failed (a rank that
+    left, stalled past the process group's timeout, or whose collective errored)."""
+
+
+def check_count_matrix(counts, per_source):
+    """counts[s][d] = records rank s sends to rank d. A token goes at most once to each rank, so every entry lies in
+    [0, per_source] (the receive buffer holds per_source records from each source). Raises EpError on the first
+    entry outside that range, naming the source and destination ranks."""
+    for s, row in enumerate(counts):
+        for d, v in enumerate(row):
+            if not 0 <= v <= per_source:
+                raise EpError(f"rank {s} reports {v} records for rank {d} (valid: 0..{per_source}); "
+                              "step abandoned on every rank before the record exchange")
+
+
 class NcclExchange:
     """The exchanges of one rank over a torch.distributed process group (NCCL on GPUs, gloo in the CPU tests)."""
 
@@ -226,11 +242,19 @@ class NcclExchange:
         self.group = group
 
     def counts(self, rank_state):
-        """Per-destination record counts out, per-source counts in; both as host lists (one synchronisation)."""
+        """Per-destination record counts out, per-source counts in, as host lists. The whole W x W count matrix is
+        all-gathered (read back to the host once) and every rank checks all of it, so a bad count stops every rank
+        at the same point with the same EpError: no rank enters the record exchange with sizes its peers disagree
+        with."""
         import torch.distributed as dist
-        dist.all_to_all_single(rank_state.recv_count, rank_state.send_count, group=self.group)
-        both = torch.stack([rank_state.send_count, rank_state.recv_count]).cpu()
-        return both[0].tolist(), both[1].tolist()
+        W, r = rank_state.world, rank_state.rank
+        flat = torch.empty(W * W, dtype=torch.int32, device=rank_state.send_count.device)
+        dist.all_gather_into_tensor(flat, rank_state.send_count, group=self.group)
+        mat = flat.view(W, W)
+        host = mat.cpu().tolist()
+        check_count_matrix(host, rank_state.recv.shape[0] // W)
+        rank_state.recv_count.copy_(mat[:, r])
+        return host[r], [row[r] for row in host]
 
     def a2a(self, out, inp, out_splits, in_splits):
         import torch.distributed as dist
@@ -245,14 +269,25 @@ def ep_step(rank_state, exchange, hidden, attn_out, normed, next_rms1=None, stre
         ctx = torch.cuda.stream(st)
     else:  # host-side doubles of the stages (CPU tests over gloo)
         st, ctx = None, contextlib.nullcontext()
-    with ctx:
-        rank_state.dispatch(hidden, attn_out, normed, st)
-        sc, rc = exchange.counts(rank_state)
-        S, R = sum(sc), sum(rc)
-        exchange.a2a(rank_state.recv[:R], rank_state.send[:S], rc, sc)
-        rank_state.experts(R, st)
-        exchange.a2a(rank_state.ret[:S], rank_state.part[:R], sc, rc)
-        rank_state.combine(hidden, attn_out, normed, next_rms1, st)
+    stage = "dispatch"
+    try:
+        with ctx:
+            rank_state.dispatch(hidden, attn_out, normed, st)
+            stage = "count exchange"
+            sc, rc = exchange.counts(rank_state)
+            S, R = sum(sc), sum(rc)
+            stage = "record exchange"
+            exchange.a2a(rank_state.recv[:R], rank_state.send[:S], rc, sc)
+            stage = "experts"
+            rank_state.experts(R, st)
+            stage = "partial-row exchange"
+            exchange.a2a(rank_state.ret[:S], rank_state.part[:R], sc, rc)
+            stage = "combine"
+            rank_state.combine(hidden, attn_out, normed, next_rms1, st)
+    except EpError:
+        raise
+    except RuntimeError as e:  # collective errors and timeouts (torch.distributed raises RuntimeError subclasses)
+        raise EpError(f"rank {rank_state.rank}: expert-parallel step failed in the {stage}: {e}") from e
     return S, R
 
 

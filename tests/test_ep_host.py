@@ -148,3 +148,87 @@ def test_ep_step_over_gloo(world):
     assert all(ok for _, ok, _, _ in res), res
     # every record sent is received somewhere
     assert sum(S for _, _, S, _ in res) == sum(R for _, _, _, R in res)
+
+
+# ---------------------------------------------------------------------------------------------- failure detection
+# Failures are made on the host among CPU ranks (no GPU is involved): a rank that reports an impossible record count,
+# a rank that leaves before the step, a rank that stalls past the process group's timeout. Every surviving rank must
+# end its step with EpError within a bound instead of hanging.
+
+PG_TIMEOUT_S = 4
+
+
+def failing_worker(rank, world, port, q, mode):
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=PG_TIMEOUT_S))
+    from mvcc_b200.ep import EpError, NcclExchange, ep_step
+    x = np.random.default_rng(rank).standard_normal((5 + rank, H)).astype(np.float32)
+    st = HostRank(rank, world, max_tokens=16)
+    faulty = rank == world - 1
+    if mode == "bad_count" and faulty:
+        dispatch = st.dispatch
+
+        def bad_dispatch(*a):
+            dispatch(*a)
+            st.send_count[0] = 10 ** 6  # more records than any rank can receive from one source
+
+        st.dispatch = bad_dispatch
+    if mode in ("leaves", "stalls") and faulty:
+        if mode == "stalls":
+            time.sleep(4 * PG_TIMEOUT_S)
+        q.put((rank, "left", 0.0))
+        q.close()
+        q.join_thread()
+        os._exit(0)  # leaves without taking part in the step or tearing the group down
+    t0 = time.monotonic()
+    try:
+        ep_step(st, NcclExchange(), torch.from_numpy(x), None, None)
+        out = "completed"
+    except EpError as e:
+        out = f"EpError: {e}"
+    q.put((rank, out, time.monotonic() - t0))
+    q.close()
+    q.join_thread()
+    if mode == "bad_count":  # every rank abandoned the step at the same point: the group is still usable
+        dist.barrier()
+        dist.destroy_process_group()
+    os._exit(0)
+
+
+def run_failing(world, mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=failing_worker, args=(r, world, port, q, mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=120) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.exitcode is None:
+                p.kill()
+    return res
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_bad_count_stops_every_rank_at_the_same_step(world):
+    res = run_failing(world, "bad_count")
+    msgs = {out for _, out, _ in res}
+    assert len(msgs) == 1, res  # the same verdict on every rank
+    (msg,) = msgs
+    assert msg.startswith("EpError: ") and f"rank {world - 1} reports 1000000 records for rank 0" in msg
+
+
+@pytest.mark.parametrize("mode", ["leaves", "stalls"])
+def test_missing_rank_ends_the_step_with_an_error(mode):
+    world = 3
+    res = run_failing(world, mode)
+    assert res[-1][:2] == (world - 1, "left")
+    for rank, out, dt in res[:-1]:
+        assert out.startswith("EpError: ") and "count exchange" in out, res
+        assert dt < 3 * PG_TIMEOUT_S + 10, res  # bounded by the group's timeout, not a hang
