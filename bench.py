@@ -277,6 +277,25 @@ def launches_per_step(T, fused_max=7, prefill_min=8, chunk=16):
     return 3 * ((T + chunk - 1) // chunk)
 
 
+def counted_launches(m, fn):
+    """Kernel launches the library issued while fn() ran, read from its own counter (moe_stats_get); None if the
+    counter cannot be read."""
+    try:
+        before = m.stats()["launches"]
+        fn()
+        torch.cuda.synchronize()
+        return int(m.stats()["launches"] - before)
+    except Exception:  # noqa: BLE001 -- the launch plan's formula stands in
+        return None
+
+
+def launches_claim(per_step_counted, T, K):
+    """gpu_launches for K steps: the counted launches of one step when available, else the launch plan's count."""
+    if per_step_counted is not None:
+        return per_step_counted * K, "library counter (moe_stats_get) over one untimed step, times the timed steps"
+    return launches_per_step(T) * K, "launch plan of the path (counter unavailable)"
+
+
 # ------------------------------------------------------------------ B200 arm
 
 def decode_case(m, shape, blocks, B, K, W, stream, world, dev, clocks=None):
@@ -295,6 +314,7 @@ def decode_case(m, shape, blocks, B, K, W, stream, world, dev, clocks=None):
         torch.cuda.synchronize()
         uniq.append(len(np.unique(blk[i].trace(B)["idx"].cpu().numpy())))
     U = float(np.mean(uniq))
+    per = counted_launches(m, lambda: step(0))
     hidden0 = hidden.clone()
     ms, clk = timed(graph_plan(step, K, stream), stream, world, clocks)
     S = min(K, GRAPH_STEPS)
@@ -302,7 +322,8 @@ def decode_case(m, shape, blocks, B, K, W, stream, world, dev, clocks=None):
                      S, max(1, min(K // S, 8)), stream)
     hidden.copy_(hidden0)
     ms_e2e, hb, db = e2e_time(lambda i: blk[i % len(blk)], hidden, attn, normed, K, stream, world)
-    return {"ms": ms, "U": U, "stage_us": st, "clocks": clk, "ms_e2e": ms_e2e, "h2d": hb, "d2h": db}
+    return {"ms": ms, "U": U, "stage_us": st, "clocks": clk, "ms_e2e": ms_e2e, "h2d": hb, "d2h": db,
+            "launches_per_step": per}
 
 
 def prefill_case(m, shape, K, W, stream, world, dev, peaks, cpu_seconds, do_cpu):
@@ -326,6 +347,7 @@ def prefill_case(m, shape, K, W, stream, world, dev, peaks, cpu_seconds, do_cpu)
     torch.cuda.synchronize()
     tr = blocks[(W - 1) % PREFILL_COPIES].trace(T)
     idx = tr["idx"].cpu().numpy()
+    per = counted_launches(m, lambda: step(W))
     load = np.bincount(idx.ravel(), minlength=shape.E)
     err = blocks[0].error_word() | blocks[1 % PREFILL_COPIES].error_word()
     ms, clk = timed(graph_plan(step, K, stream), stream, world, ClockSampler(dev))
@@ -358,7 +380,8 @@ def prefill_case(m, shape, K, W, stream, world, dev, peaks, cpu_seconds, do_cpu)
         "block_tflops": {"achieved": blk_tf, "frac": blk_tf / peaks["tf_sustained"], "flops_per_step": fl["block"]},
         "e2e": {"value": world * T * K / (ms_e2e / 1e3), "unit": "tok/s", "h2d_bytes_per_step": hb,
                 "d2h_bytes_per_step": db},
-        "gpu_launches": launches_per_step(T) * K,
+        "gpu_launches": launches_claim(per, T, K)[0],
+        "gpu_launches_source": launches_claim(per, T, K)[1],
         "error_word": err,
         "clocks": clk,
     }
@@ -531,7 +554,8 @@ def b200_arm(args, rank, world, local):
                       {"route": st[0], "gate_up": st[1], "down_combine": st[2]},
         "e2e": {"value": world * B * K / (head["ms_e2e"] / 1e3), "unit": "tok/s",
                 "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"]},
-        "gpu_launches": launches_per_step(B) * K,
+        "gpu_launches": launches_claim(head["launches_per_step"], B, K)[0],
+        "gpu_launches_source": launches_claim(head["launches_per_step"], B, K)[1],
         "clocks": head["clocks"],
     }
     if not args.quick:

@@ -66,6 +66,19 @@ MOE_API int moe_workspace_init(void* workspace, size_t workspace_bytes, moe_stre
 /* Reads (synchronously) and clears the workspace error word: 0 = no error recorded, else a code of moe_errc. */
 MOE_API int moe_workspace_error(void* workspace, size_t workspace_bytes, moe_stream_t stream);
 
+/* Library counters, the counterpart of the reference's mvccGetStats (crates/mvcc-cudart/src/api.rs:546; its
+ * benchmark reads the launch count, qwen.cu:479-484): kernel launches issued by this library (counted when the launch
+ * call succeeds; a launch recorded into a CUDA graph counts once, when captured, not per replay), block entry-point
+ * calls that passed their checks, and bytes the pack loader (moe_pack.h) copied to the device. Process-wide and
+ * thread-safe; moe_stats_reset sets all three to zero. */
+typedef struct moe_stats {
+  uint64_t launches;
+  uint64_t block_calls;
+  uint64_t pack_bytes;
+} moe_stats;
+MOE_API void moe_stats_get(moe_stats* out);
+MOE_API void moe_stats_reset(void);
+
 /* Error-word bits. MOE_ERR_BARRIER: a grid barrier of the fused decode kernel gave up waiting (bounded spin); the
  * call's results are invalid and the workspace must be re-initialised with moe_workspace_init. MOE_ERR_TIMEOUT: a
  * bounded pipeline wait inside a prefill GEMM tile gave up; that call's results are invalid. */

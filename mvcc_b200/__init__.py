@@ -50,6 +50,12 @@ class MoeTrace(ctypes.Structure):
                                                "offsets")]
 
 
+class MoeStats(ctypes.Structure):
+    """ctypes mirror of `moe_stats` (include/moe_block.h)."""
+
+    _fields_ = [("launches", ctypes.c_uint64), ("block_calls", ctypes.c_uint64), ("pack_bytes", ctypes.c_uint64)]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _W = ctypes.POINTER(MoeLayerWeights)
@@ -74,6 +80,8 @@ _SIGS = {
     "moe_synth_int4_rows": (_I, [_P, _P, ctypes.c_int64, _I, _I, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                  _P]),
     "moe_version": (ctypes.c_char_p, []),
+    "moe_stats_get": (None, [ctypes.POINTER(MoeStats)]),
+    "moe_stats_reset": (None, []),
     # expert-parallel stages (include/moe_ep.h)
     "moe_ep_record_bytes": (ctypes.c_size_t, [_W]),
     "moe_ep_dispatch": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
@@ -120,6 +128,18 @@ def _check(rc, what):
 
 def version():
     return _lib.moe_version().decode()
+
+
+def stats():
+    """The library's counters (moe_stats_get): kernel launches issued (a launch captured into a CUDA graph counts
+    once, at capture), block calls, bytes the pack loader copied to the device."""
+    st = MoeStats()
+    _lib.moe_stats_get(ctypes.byref(st))
+    return {"launches": st.launches, "block_calls": st.block_calls, "pack_bytes": st.pack_bytes}
+
+
+def reset_stats():
+    _lib.moe_stats_reset()
 
 
 def _ptr(t):

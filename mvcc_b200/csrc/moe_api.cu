@@ -1,4 +1,5 @@
-// moe_api.cu -- the extern "C" entry points declared in include/moe_block.h and include/moe_ep.h.
+// moe_api.cu -- the extern "C" entry points declared in include/moe_block.h and include/moe_ep.h, and the
+// library counters behind moe_stats_get.
 //
 // Host-side launch code replacing the MoE part of forward() (qwen.cu:429-448) and moe() (qwen.cu:345-363), and the
 // expert-parallel stages. Every compute entry point validates the shape and the workspace size before launching
@@ -109,7 +110,30 @@ int check_common(const moe_layer_weights* w, void* ws, size_t bytes, int T) {
 
 }  // namespace
 
+// Counters of moe_stats_get (relaxed atomics: each is a tally, nothing is ordered by them).
+namespace moe {
+namespace {
+std::atomic<uint64_t> g_launches{0}, g_block_calls{0}, g_pack_bytes{0};
+}  // namespace
+void note_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+void note_block_call() { g_block_calls.fetch_add(1, std::memory_order_relaxed); }
+void note_pack_bytes(uint64_t n) { g_pack_bytes.fetch_add(n, std::memory_order_relaxed); }
+}  // namespace moe
+
 extern "C" {
+
+void moe_stats_get(moe_stats* out) {
+  if (!out) return;
+  out->launches = moe::g_launches.load(std::memory_order_relaxed);
+  out->block_calls = moe::g_block_calls.load(std::memory_order_relaxed);
+  out->pack_bytes = moe::g_pack_bytes.load(std::memory_order_relaxed);
+}
+
+void moe_stats_reset(void) {
+  moe::g_launches.store(0, std::memory_order_relaxed);
+  moe::g_block_calls.store(0, std::memory_order_relaxed);
+  moe::g_pack_bytes.store(0, std::memory_order_relaxed);
+}
 
 int moe_check_shape(const moe_layer_weights* w) { return shape_ok(w) ? 0 : (int)cudaErrorInvalidValue; }
 
@@ -153,6 +177,7 @@ int block_forward_impl(const moe_layer_weights* w, void* workspace, size_t works
   int rc = check_common(w, workspace, workspace_bytes, T);
   if (rc) return rc;
   if (!hidden || !attn_out || !normed || !weights_present(w, true, true, true)) return (int)cudaErrorInvalidValue;
+  note_block_call();
   if (use_prefill(w, T)) {
     BlockArgs a = make_args(w, workspace, layout_for(w, T), T);
     a.hidden = hidden;

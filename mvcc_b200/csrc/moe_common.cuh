@@ -148,6 +148,16 @@ constexpr int kPrefillMinT = 8;
 constexpr int kTileRows = 128;
 __host__ __device__ inline int prefill_max_tiles(int P, int E) { return P / kTileRows + (E < P ? E : P) + 1; }
 
+// Launch accounting behind moe_stats_get: `launched(e)` passes a launch's status through and counts the launch when
+// it succeeded (the counters live in moe_api.cu).
+void note_launches(uint64_t n);
+void note_block_call();
+void note_pack_bytes(uint64_t n);
+inline cudaError_t launched(cudaError_t e) {
+  if (e == cudaSuccess) note_launches(1);
+  return e;
+}
+
 // Records the cudaEvent_t `ev` (nullable) on `s`; inside stream capture the record becomes a graph node that
 // timestamps every replay.
 inline cudaError_t record_event(void* ev, cudaStream_t s) {

@@ -687,7 +687,7 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, args...);
+  return launched(cudaLaunchKernelEx(&cfg, kern, args...));
 }
 
 template <int NB8>

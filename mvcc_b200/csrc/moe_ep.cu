@@ -170,32 +170,32 @@ static const EpPeers kNoPeers = {};
 cudaError_t ep_plan_pack(const BlockArgs& a, int world, uint8_t* send, int32_t* send_count, int32_t* tok_pos,
                          cudaStream_t s) {
   ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(a, world, tok_pos, send_count, 0, kNoPeers);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launched(cudaGetLastError());
   if (e != cudaSuccess) return e;
   ep_pack_kernel<<<a.T, kPackThreads, 0, s>>>(a, world, ep_record_bytes(a.w.H, a.w.TOPK), send, tok_pos, 0,
                                               kNoPeers);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 cudaError_t ep_plan_pack_peers(const BlockArgs& a, int world, const EpPeers& peers, int32_t* send_count,
                                int32_t* tok_pos, cudaStream_t s) {
   ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(a, world, tok_pos, send_count, 1, peers);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launched(cudaGetLastError());
   if (e != cudaSuccess) return e;
   ep_pack_kernel<<<a.T, kPackThreads, 0, s>>>(a, world, ep_record_bytes(a.w.H, a.w.TOPK), nullptr, tok_pos, 1,
                                               peers);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 cudaError_t ep_mark(const BlockArgs& a, const uint8_t* recv, const int32_t* rcount, int cap, cudaStream_t s) {
   const int P = a.T * a.w.TOPK;
   ep_mark_kernel<<<(P + 255) / 256, 256, 0, s>>>(a, recv, ep_record_bytes(a.w.H, a.w.TOPK), rcount, cap);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 cudaError_t ep_return_peers(const BlockArgs& a, int world, const EpPeers& peers, cudaStream_t s) {
   ep_return_kernel<<<world * peers.cap, 256, 0, s>>>(a, world, peers);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 }  // namespace moe

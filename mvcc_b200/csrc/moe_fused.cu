@@ -1047,7 +1047,7 @@ cudaError_t launch_fused_decode(const BlockArgs& a, unsigned long long* gbar, bo
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = fused_pdl_enabled() ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, moe_fused_decode_kernel, f);
+  return launched(cudaLaunchKernelEx(&cfg, moe_fused_decode_kernel, f));
 }
 
 }  // namespace moe

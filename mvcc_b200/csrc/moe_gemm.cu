@@ -731,7 +731,7 @@ static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, moe_gemm_kernel<BN, INT4, EPI>, p, tmA, tmB, tmS, c);
+  return launched(cudaLaunchKernelEx(&cfg, moe_gemm_kernel<BN, INT4, EPI>, p, tmA, tmB, tmS, c));
 }
 
 template <int BN, bool INT4>

@@ -21,6 +21,10 @@
 
 #include "moe_pack.h"
 
+namespace moe {
+void note_pack_bytes(uint64_t n);  // moe_stats_get's counter (moe_api.cu)
+}  // namespace moe
+
 namespace {
 
 // ----------------------------------------------------------------------------------------------- JSON reader
@@ -533,6 +537,7 @@ int moe_pack_upload_layer(moe_pack* pk, int layer, void* dev, size_t dev_bytes, 
     if (e != cudaSuccess) return pk->set_err((int)e, "host-to-device copy failed: %s", cudaGetErrorString(e));
     ptr[i] = dst;
     at += align_up((size_t)ent[i]->nbytes);
+    moe::note_pack_bytes(ent[i]->nbytes);
   }
   fill_weights(pk->geo, ptr, w);
   return 0;

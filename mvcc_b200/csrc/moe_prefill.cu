@@ -289,14 +289,15 @@ static cudaError_t run_sort(const BlockArgs& a, int from, cudaStream_t s) {
   cudaError_t e = cudaSuccess;
   if (from == SORT_TOPK) {
     prefill_topk_kernel<<<(a.T + kPT / 32 - 1) / (kPT / 32), kPT, 0, s>>>(a, 1);
+    if ((e = launched(cudaGetLastError())) != cudaSuccess) return e;
   } else if (from == SORT_MARK) {
     prefill_mark_kernel<<<(P + kPT - 1) / kPT, kPT, 0, s>>>(a);
+    if ((e = launched(cudaGetLastError())) != cudaSuccess) return e;
   }
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
   prefill_scan_kernel<<<a.w.E, kPT, 0, s>>>(a);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = launched(cudaGetLastError())) != cudaSuccess) return e;
   prefill_scatter_kernel<<<(P + kPT - 1) / kPT, kPT, 0, s>>>(a);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s, void* mark = nullptr) {
@@ -390,7 +391,7 @@ cudaError_t prefill_router(const BlockArgs& a, cudaStream_t s) {
   cudaError_t e = run_router(a, s);
   if (e != cudaSuccess) return e;
   prefill_topk_kernel<<<(a.T + kPT / 32 - 1) / (kPT / 32), kPT, 0, s>>>(a, 0);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 cudaError_t prefill_routed(const BlockArgs& a, uint16_t* inter_out, cudaStream_t s) {
@@ -399,30 +400,30 @@ cudaError_t prefill_routed(const BlockArgs& a, uint16_t* inter_out, cudaStream_t
   if (e == cudaSuccess) e = run_experts(a, s);
   if (e != cudaSuccess) return e;
   prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 1);
-  if ((e = cudaGetLastError()) != cudaSuccess || !inter_out) return e;
+  if ((e = launched(cudaGetLastError())) != cudaSuccess || !inter_out) return e;
   const int64_t n = (int64_t)a.T * a.w.TOPK * (a.w.I / 8);
   prefill_unsort_kernel<<<(unsigned)((n + kPT - 1) / kPT), kPT, 0, s>>>(a, inter_out);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 cudaError_t prefill_block(const BlockArgs& a, cudaStream_t s, void* const* marks) {
   cudaError_t e = clear_bits(a, s);
   if (e != cudaSuccess) return e;
   prefill_norm_kernel<<<a.T, kPT, 0, s>>>(a);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = launched(cudaGetLastError())) != cudaSuccess) return e;
   if ((e = run_router(a, s)) != cudaSuccess) return e;
   if ((e = run_sort(a, SORT_TOPK, s)) != cudaSuccess) return e;
   if (marks && (e = record_event(marks[1], s)) != cudaSuccess) return e;
   if ((e = run_experts(a, s, marks ? marks[2] : nullptr)) != cudaSuccess) return e;
   if ((e = prefill_shared(a, s)) != cudaSuccess) return e;
   prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 1 | 2);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = launched(cudaGetLastError())) != cudaSuccess) return e;
   return marks ? record_event(marks[3], s) : cudaSuccess;
 }
 
 cudaError_t prefill_norm(const BlockArgs& a, cudaStream_t s) {
   prefill_norm_kernel<<<a.T, kPT, 0, s>>>(a);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 cudaError_t prefill_bits_clear(const BlockArgs& a, cudaStream_t s) { return clear_bits(a, s); }
@@ -432,7 +433,7 @@ cudaError_t prefill_routed_marked(const BlockArgs& a, cudaStream_t s) {
   if (e == cudaSuccess) e = run_experts(a, s);
   if (e != cudaSuccess) return e;
   prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 1);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 cudaError_t prefill_routed_marked_gemms(const BlockArgs& a, cudaStream_t s) {
@@ -442,7 +443,7 @@ cudaError_t prefill_routed_marked_gemms(const BlockArgs& a, cudaStream_t s) {
 
 cudaError_t prefill_combine(const BlockArgs& a, cudaStream_t s) {
   prefill_combine_kernel<<<a.T, kPT, 0, s>>>(a, 2);
-  return cudaGetLastError();
+  return launched(cudaGetLastError());
 }
 
 }  // namespace moe

@@ -71,7 +71,7 @@ int moe_synth_normal_bf16(uint16_t* out, int64_t n, uint64_t seed, uint64_t stre
   if (n == 0) return 0;
   const int grid = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
   moe::synth_normal_bf16_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(out, n, seed, stream_id, mean, std);
-  return (int)cudaGetLastError();
+  return (int)moe::launched(cudaGetLastError());
 }
 
 int moe_synth_int4_rows(uint8_t* q, uint16_t* scales, int64_t rows, int K, int G, uint64_t seed, uint64_t stream_id,
@@ -81,7 +81,7 @@ int moe_synth_int4_rows(uint8_t* q, uint16_t* scales, int64_t rows, int K, int G
   const int64_t jobs = rows * (K / G);
   const int grid = (int)std::min<int64_t>((jobs + 255) / 256, 148 * 32);
   moe::synth_int4_rows_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(q, scales, rows, K, G, seed, stream_id, std);
-  return (int)cudaGetLastError();
+  return (int)moe::launched(cudaGetLastError());
 }
 
 }  // extern "C"

@@ -28,6 +28,16 @@ def test_library_exports_every_declared_symbol():
     assert set(names) <= set(mvcc_b200.EXPORTED)
 
 
+def test_stats_counters_read_and_reset():
+    """moe_stats_get / moe_stats_reset; a call refused before launch counts neither a launch nor a block call."""
+    import mvcc_b200
+    mvcc_b200.reset_stats()
+    assert mvcc_b200.stats() == {"launches": 0, "block_calls": 0, "pack_bytes": 0}
+    w = _w()
+    assert mvcc_b200._lib.moe_block_forward(ctypes.byref(w), None, 0, None, None, None, None, 1, None) == 1
+    assert mvcc_b200.stats() == {"launches": 0, "block_calls": 0, "pack_bytes": 0}
+
+
 def test_version():
     import mvcc_b200
     assert "sm_100a" in mvcc_b200.version()

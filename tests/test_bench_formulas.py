@@ -47,6 +47,35 @@ def test_launch_counts():
     assert b.launches_per_step(4096) == 10
 
 
+def test_launch_claim_prefers_the_library_counter():
+    """gpu_launches comes from the library's launch counter over one step when it can be read, else from the plan."""
+    b = load_bench()
+
+    class FakeLib:
+        n = 0
+
+        def stats(self):
+            return {"launches": self.n}
+
+    fake = FakeLib()
+
+    def step():
+        fake.n += 10
+
+    import torch
+    sync = torch.cuda.synchronize
+    torch.cuda.synchronize = lambda *a: None  # no device here
+    try:
+        per = b.counted_launches(fake, step)
+    finally:
+        torch.cuda.synchronize = sync
+    assert per == 10
+    assert b.launches_claim(per, 4096, 7) == (70, b.launches_claim(per, 4096, 7)[1])
+    assert "counter" in b.launches_claim(per, 1, 7)[1]
+    assert b.launches_claim(None, 1, 7)[0] == 7 and "plan" in b.launches_claim(None, 1, 7)[1]
+    assert b.counted_launches(object(), step) is None  # no counter: the plan stands in
+
+
 def test_clock_summary_reads_reasons_and_window():
     """The clocks object of the bench line: median SM clock, max clock and the throttle reasons active in the timed
     region (the samples nvidia-smi prints as 'index, clocks.sm, clocks.max.sm, power, active, hw, hw_thermal,
