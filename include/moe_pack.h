@@ -15,9 +15,16 @@
  * experts, topk, inter, shared_inter, eps, and group (absent in packs written before the key existed: 128, the
  * writer's default, convert.py:311).
  *
+ * int8 shared expert (convert.py --dense int8, convert.py:159-169, 376-385): L{i}.shared.gate_up.q8 / .s8 and
+ * L{i}.shared.down.q8 / .s8 (int8 rows, fp16 scales per group of K/cols(s8) inputs) are dequantised on the host to
+ * bf16(q * scale) -- the product is exact in fp32, so bf16 round-to-nearest-even is the only rounding -- and
+ * placed where the bf16 tensors would go. These are the weights the reference's tensor-core int8 GEMM multiplies
+ * (gemm_i8_tc_kernel dequantises each K step to the same bf16 values, kernels.cuh:363-400; used for T >= 32,
+ * qwen.cu:321-329); its GEMV and small-T paths multiply the fp32 products unrounded (kernels.cuh:215-330), which
+ * the bf16 weights match within the bf16 tolerance.
+ *
  * Errors: every call returns a cudaError_t value as int. A pack that cannot be used (missing tensor, wrong shape or
- * dtype, a blob outside the file) gives cudaErrorInvalidValue (1); a pack whose shared expert is stored as int8
- * (convert.py --dense int8: shared.gate_up.q8 / .s8) gives cudaErrorNotSupported (801). The reason is kept as text
+ * dtype, a blob outside the file) gives cudaErrorInvalidValue (1). The reason is kept as text
  * (moe_pack_last_error). The reference exits with a message instead (qwen.cu:140-153, pack.hpp:119-130).
  * A moe_pack is used by one host thread at a time.
  */
@@ -61,8 +68,9 @@ MOE_API int moe_pack_tensor(moe_pack* pack, const char* name, moe_pack_tensor_in
 /* Name of the i-th header entry in byte order of the names (NULL if i is out of range). */
 MOE_API const char* moe_pack_tensor_name(const moe_pack* pack, int i);
 
-/* Layer `layer`'s block weights as HOST pointers into the mapping, with the pack's geometry (router_bias NULL):
- * every tensor checked for presence, dtype and shape. For host-side checkers and the copy below. */
+/* Layer `layer`'s block weights as HOST pointers, with the pack's geometry (router_bias NULL): every tensor checked
+ * for presence, dtype and shape. The pointers lie in the mapping, except an int8 shared expert's, which point to its
+ * dequantised bf16 rows held by the pack; all stay valid until moe_pack_close. For host-side checkers. */
 MOE_API int moe_pack_layer_host(moe_pack* pack, int layer, moe_layer_weights* w);
 /* Device bytes that moe_pack_upload_layer needs for `layer` (each tensor at a 256-byte aligned offset); 0 if the
  * layer cannot be loaded (the reason in moe_pack_last_error). */

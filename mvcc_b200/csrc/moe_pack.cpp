@@ -11,6 +11,7 @@
 #include <unistd.h>
 
 #include <cerrno>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -240,6 +241,7 @@ struct moe_pack {
   std::map<std::string, Entry> tensors;  // ordered by name
   std::vector<const std::string*> names;
   std::string err;
+  std::map<std::pair<int, int>, std::vector<uint16_t>> dequant;  // (layer, block tensor) -> bf16 rows of an int8 pack
 
   int set_err(int code, const char* fmt, ...) __attribute__((format(printf, 3, 4))) {
     char buf[512];
@@ -330,6 +332,7 @@ struct Want {
   const char* dtype;
   int ndim;
   int64_t dims[3];
+  bool int8_ok;  // may be stored as int8 rows + fp16 group scales (convert.py --dense int8)
 };
 
 // The nine block tensors of one layer, in the order moe_layer_weights lists its pointers, with the shapes
@@ -337,49 +340,124 @@ struct Want {
 void block_wants(const moe_pack_geometry& g, Want w[kBlockTensors]) {
   const int64_t H = g.H, E = g.E, I = g.I, Is = g.Is, G = g.G;
   const Want all[kBlockTensors] = {
-      {"rms2", "bf16", 1, {H, 0, 0}},
-      {"router", "bf16", 2, {E, H, 0}},
-      {"exp.gate_up.q", "u8", 3, {E, 2 * I, H / 2}},
-      {"exp.gate_up.s", "f16", 3, {E, 2 * I, H / G}},
-      {"exp.down.q", "u8", 3, {E, H, I / 2}},
-      {"exp.down.s", "f16", 3, {E, H, I / G}},
-      {"shared.gate_up", "bf16", 2, {2 * Is, H, 0}},
-      {"shared.down", "bf16", 2, {H, Is, 0}},
-      {"shared.gate", "bf16", 1, {H, 0, 0}},
+      {"rms2", "bf16", 1, {H, 0, 0}, false},
+      {"router", "bf16", 2, {E, H, 0}, false},
+      {"exp.gate_up.q", "u8", 3, {E, 2 * I, H / 2}, false},
+      {"exp.gate_up.s", "f16", 3, {E, 2 * I, H / G}, false},
+      {"exp.down.q", "u8", 3, {E, H, I / 2}, false},
+      {"exp.down.s", "f16", 3, {E, H, I / G}, false},
+      {"shared.gate_up", "bf16", 2, {2 * Is, H, 0}, true},
+      {"shared.down", "bf16", 2, {H, Is, 0}, true},
+      {"shared.gate", "bf16", 1, {H, 0, 0}, false},
   };
   for (int i = 0; i < kBlockTensors; ++i) w[i] = all[i];
 }
 
-// Looks up and checks layer `layer`'s block tensors; fills ent[] in moe_layer_weights order.
-int find_block(moe_pack* pk, int layer, const Entry* ent[kBlockTensors]) {
+// Where one block tensor comes from: a stored tensor of the wanted dtype (`e`), or -- for the shared expert of an
+// int8 pack -- int8 rows `q8` [N,K] with fp16 scales `s8` [N, K/group] (quant_int8_rows, convert.py:159-169) that
+// the loader dequantizes to bf16.
+struct Src {
+  const Entry* e = nullptr;
+  const Entry* q8 = nullptr;
+  const Entry* s8 = nullptr;
+  int64_t rows = 0, cols = 0, group = 0;
+  uint64_t nbytes() const { return e ? e->nbytes : (uint64_t)(rows * cols * 2); }
+};
+
+std::string dims_text(const std::vector<int64_t>& v) {
+  std::string t;
+  for (size_t d = 0; d < v.size(); ++d) t += (d ? "," : "") + std::to_string(v[d]);
+  return t;
+}
+
+bool shape_is(const Entry& e, const char* dtype, int ndim, const int64_t* dims) {
+  bool ok = e.dtype == dtype && (int)e.shape.size() == ndim;
+  for (int d = 0; ok && d < ndim; ++d) ok = e.shape[d] == dims[d];
+  return ok;
+}
+
+// Looks up and checks layer `layer`'s block tensors; fills src[] in moe_layer_weights order.
+int find_block(moe_pack* pk, int layer, Src src[kBlockTensors]) {
   if (layer < 0 || layer >= pk->geo.L)
     return pk->set_err(kInvalid, "layer %d is outside the pack's %d layers", layer, pk->geo.L);
   Want want[kBlockTensors];
   block_wants(pk->geo, want);
   const std::string pre = "L" + std::to_string(layer) + ".";
   for (int i = 0; i < kBlockTensors; ++i) {
-    const std::string name = pre + want[i].suffix;
+    const Want& wt = want[i];
+    const std::string name = pre + wt.suffix;
+    src[i] = Src();
     auto it = pk->tensors.find(name);
-    if (it == pk->tensors.end()) {
-      if (pk->tensors.count(name + ".q8"))
-        return pk->set_err(kNotSupported, "%s is stored as int8 (convert.py --dense int8): not supported",
-                           name.c_str());
-      return pk->set_err(kInvalid, "pack has no tensor %s", name.c_str());
+    if (it == pk->tensors.end() && wt.int8_ok && pk->tensors.count(name + ".q8")) {
+      auto sq = pk->tensors.find(name + ".s8");
+      if (sq == pk->tensors.end()) return pk->set_err(kInvalid, "pack has %s.q8 but no %s.s8", name.c_str(), name.c_str());
+      const Entry& q = pk->tensors.at(name + ".q8");
+      const Entry& sc = sq->second;
+      const int64_t N = wt.dims[0], K = wt.dims[1];
+      if (!shape_is(q, "i8", 2, wt.dims))
+        return pk->set_err(kInvalid, "tensor %s.q8 is %s [%s], expected i8 [%lld,%lld]", name.c_str(), q.dtype.c_str(),
+                           dims_text(q.shape).c_str(), (long long)N, (long long)K);
+      if (sc.dtype != "f16" || sc.shape.size() != 2 || sc.shape[0] != N || sc.shape[1] < 1 || K % sc.shape[1])
+        return pk->set_err(kInvalid, "tensor %s.s8 is %s [%s], expected f16 [%lld, K/group]", name.c_str(),
+                           sc.dtype.c_str(), dims_text(sc.shape).c_str(), (long long)N);
+      src[i].q8 = &q;
+      src[i].s8 = &sc;
+      src[i].rows = N;
+      src[i].cols = K;
+      src[i].group = K / sc.shape[1];
+      continue;
     }
+    if (it == pk->tensors.end()) return pk->set_err(kInvalid, "pack has no tensor %s", name.c_str());
     const Entry& e = it->second;
-    bool ok = e.dtype == want[i].dtype && (int)e.shape.size() == want[i].ndim;
-    for (int d = 0; ok && d < want[i].ndim; ++d) ok = e.shape[d] == want[i].dims[d];
-    if (!ok) {
-      std::string got;
-      for (size_t d = 0; d < e.shape.size(); ++d) got += (d ? "," : "") + std::to_string(e.shape[d]);
-      std::string exp;
-      for (int d = 0; d < want[i].ndim; ++d) exp += (d ? "," : "") + std::to_string(want[i].dims[d]);
+    if (!shape_is(e, wt.dtype, wt.ndim, wt.dims)) {
+      std::vector<int64_t> exp(wt.dims, wt.dims + wt.ndim);
       return pk->set_err(kInvalid, "tensor %s is %s [%s], expected %s [%s]", name.c_str(), e.dtype.c_str(),
-                         got.c_str(), want[i].dtype, exp.c_str());
+                         dims_text(e.shape).c_str(), wt.dtype, dims_text(exp).c_str());
     }
-    ent[i] = &e;
+    src[i].e = &e;
   }
   return 0;
+}
+
+// IEEE 754 binary16 bits -> float (normal, subnormal, infinity and NaN encodings).
+float half_bits_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t ex = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+  uint32_t bits;
+  if (ex == 0x1F) {
+    bits = sign | 0x7F800000u | (man << 13);
+  } else if (ex != 0) {
+    bits = sign | ((ex + 112u) << 23) | (man << 13);  // rebias 15 -> 127
+  } else {
+    float f = std::ldexp((float)man, -24);  // subnormal: man * 2^-24, exact in float
+    memcpy(&bits, &f, 4);
+    bits |= sign;
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+// float -> bf16 bits, round to nearest, ties to even (NaN kept quiet).
+uint16_t float_to_bf16_rne(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return (uint16_t)((u >> 16) | 0x40u);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+// bf16(q * scale) row by row: the int8 value times its group's fp16 scale is exact in fp32 (8 + 11 significant
+// bits), so the single rounding is the one to bf16.
+void dequant_i8_rows(const int8_t* q, const uint16_t* sc, int64_t rows, int64_t cols, int64_t group, uint16_t* out) {
+  const int64_t groups = cols / group;
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t g = 0; g < groups; ++g) {
+      const float s = half_bits_to_float(sc[r * groups + g]);
+      const int8_t* qq = q + r * cols + g * group;
+      uint16_t* o = out + r * cols + g * group;
+      for (int64_t k = 0; k < group; ++k) o[k] = float_to_bf16_rne((float)qq[k] * s);
+    }
 }
 
 void fill_weights(const moe_pack_geometry& g, const void* const ptr[kBlockTensors], moe_layer_weights* w) {
@@ -408,6 +486,24 @@ size_t align_up(size_t x) { return (x + kDevAlign - 1) / kDevAlign * kDevAlign; 
 void copy_err(char* err, size_t err_len, const std::string& msg) {
   if (!err || err_len == 0) return;
   snprintf(err, err_len, "%s", msg.c_str());
+}
+
+}  // namespace
+
+namespace {
+
+// Host bytes of block tensor i: the blob in the mapping, or (int8 shared expert) its bf16 rows, dequantised once per
+// (layer, tensor) and kept until the pack is closed.
+const void* host_block_bytes(moe_pack* pk, int layer, int i, const Src& src) {
+  if (src.e) return pk->bytes() + src.e->off;
+  std::vector<uint16_t>& rows = pk->dequant[{layer, i}];
+  if (rows.empty()) {
+    rows.resize((size_t)(src.rows * src.cols));
+    dequant_i8_rows(reinterpret_cast<const int8_t*>(pk->bytes() + src.q8->off),
+                    reinterpret_cast<const uint16_t*>(pk->bytes() + src.s8->off), src.rows, src.cols, src.group,
+                    rows.data());
+  }
+  return rows.data();
 }
 
 }  // namespace
@@ -498,10 +594,10 @@ int moe_pack_tensor(moe_pack* pk, const char* name, moe_pack_tensor_info* info) 
 int moe_pack_layer_host(moe_pack* pk, int layer, moe_layer_weights* w) {
   if (!pk || !w) return kInvalid;
   pk->err.clear();
-  const Entry* ent[kBlockTensors];
-  if (int rc = find_block(pk, layer, ent)) return rc;
+  Src src[kBlockTensors];
+  if (int rc = find_block(pk, layer, src)) return rc;
   const void* ptr[kBlockTensors];
-  for (int i = 0; i < kBlockTensors; ++i) ptr[i] = pk->bytes() + ent[i]->off;
+  for (int i = 0; i < kBlockTensors; ++i) ptr[i] = host_block_bytes(pk, layer, i, src[i]);
   fill_weights(pk->geo, ptr, w);
   return 0;
 }
@@ -509,10 +605,10 @@ int moe_pack_layer_host(moe_pack* pk, int layer, moe_layer_weights* w) {
 size_t moe_pack_layer_bytes(moe_pack* pk, int layer) {
   if (!pk) return 0;
   pk->err.clear();
-  const Entry* ent[kBlockTensors];
-  if (find_block(pk, layer, ent)) return 0;
+  Src src[kBlockTensors];
+  if (find_block(pk, layer, src)) return 0;
   size_t total = 0;
-  for (int i = 0; i < kBlockTensors; ++i) total += align_up((size_t)ent[i]->nbytes);
+  for (int i = 0; i < kBlockTensors; ++i) total += align_up((size_t)src[i].nbytes());
   return total;
 }
 
@@ -520,10 +616,10 @@ int moe_pack_upload_layer(moe_pack* pk, int layer, void* dev, size_t dev_bytes, 
                           moe_stream_t stream) {
   if (!pk || !w) return kInvalid;
   pk->err.clear();
-  const Entry* ent[kBlockTensors];
-  if (int rc = find_block(pk, layer, ent)) return rc;
+  Src src[kBlockTensors];
+  if (int rc = find_block(pk, layer, src)) return rc;
   size_t need = 0;
-  for (int i = 0; i < kBlockTensors; ++i) need += align_up((size_t)ent[i]->nbytes);
+  for (int i = 0; i < kBlockTensors; ++i) need += align_up((size_t)src[i].nbytes());
   if (!dev || reinterpret_cast<uintptr_t>(dev) % kDevAlign)
     return pk->set_err(kInvalid, "device region must be %zu-byte aligned", kDevAlign);
   if (dev_bytes < need) return pk->set_err(kInvalid, "device region holds %zu bytes, layer needs %zu", dev_bytes, need);
@@ -531,13 +627,15 @@ int moe_pack_upload_layer(moe_pack* pk, int layer, void* dev, size_t dev_bytes, 
   size_t at = 0;
   for (int i = 0; i < kBlockTensors; ++i) {
     uint8_t* dst = static_cast<uint8_t*>(dev) + at;
-    // Pageable source: the call returns after the bytes are staged, so the mapping may be released afterwards.
-    const cudaError_t e = cudaMemcpyAsync(dst, pk->bytes() + ent[i]->off, (size_t)ent[i]->nbytes,
-                                          cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    const size_t n = (size_t)src[i].nbytes();
+    // Pageable source (the mapping, or the dequantised rows of an int8 shared expert): the call returns after the
+    // bytes are staged, so the source may be released afterwards.
+    const cudaError_t e =
+        cudaMemcpyAsync(dst, host_block_bytes(pk, layer, i, src[i]), n, cudaMemcpyHostToDevice, (cudaStream_t)stream);
     if (e != cudaSuccess) return pk->set_err((int)e, "host-to-device copy failed: %s", cudaGetErrorString(e));
     ptr[i] = dst;
-    at += align_up((size_t)ent[i]->nbytes);
-    moe::note_pack_bytes(ent[i]->nbytes);
+    at += align_up(n);
+    moe::note_pack_bytes(n);
   }
   fill_weights(pk->geo, ptr, w);
   return 0;

@@ -111,11 +111,24 @@ class MoePack:
         shape = tuple(inf.shape[:inf.ndim])
         return arr.reshape(shape) if dt in _NUMPY else arr
 
+    def block_shapes(self):
+        """Shape of each block tensor (keyed by MoeLayer field) at this pack's geometry."""
+        s = self.shape
+        return {"rms2": (s.H,), "router": (s.E, s.H), "exp_gu_q": (s.E, 2 * s.I, s.H // 2),
+                "exp_gu_s": (s.E, 2 * s.I, s.H // s.G), "exp_dn_q": (s.E, s.H, s.I // 2),
+                "exp_dn_s": (s.E, s.H, s.I // s.G), "shared_gate_up": (2 * s.Is, s.H),
+                "shared_down": (s.H, s.Is), "shared_gate": (s.H,)}
+
     def layer_host(self, layer):
-        """Layer `layer`'s block tensors as host copies keyed by MoeLayer field (checked like layer())."""
+        """Layer `layer`'s block tensors as host copies keyed by MoeLayer field, checked as for layer() (an int8
+        shared expert comes back as its dequantised bf16 rows, the values layer() uploads)."""
         w = MoeLayerWeights()
         self._check(_lib.moe_pack_layer_host(self._h, layer, ctypes.byref(w)))
-        return {field: self.tensor(f"L{layer}.{sub}") for field, sub, _ in BLOCK_TENSORS}
+        out = {}
+        for (field, _, dt), shape in zip(BLOCK_TENSORS, self.block_shapes().values()):
+            n = int(np.prod(shape)) * np.dtype(_NUMPY[dt]).itemsize
+            out[field] = np.frombuffer(ctypes.string_at(getattr(w, field), n), dtype=_NUMPY[dt]).reshape(shape)
+        return out
 
     def layer_bytes(self, layer):
         n = _lib.moe_pack_layer_bytes(self._h, layer)
@@ -133,20 +146,45 @@ class MoePack:
                                                ctypes.byref(w), _stream(stream)))
         base = buf.data_ptr()
         t = {}
-        for field, sub, dt in BLOCK_TENSORS:
-            inf = self.info(f"L{layer}.{sub}")
+        for (field, _, dt), shape in zip(BLOCK_TENSORS, self.block_shapes().values()):
             off = getattr(w, field) - base
-            shape = tuple(inf.shape[:inf.ndim])
-            t[field] = buf[off:off + inf.nbytes].view(_TORCH[dt]).view(shape)
+            n = int(np.prod(shape)) * np.dtype(_NUMPY[dt]).itemsize
+            t[field] = buf[off:off + n].view(_TORCH[dt]).view(shape)
         ml = MoeLayer(self.shape, t)
         ml.storage = buf  # the tensors are views of this buffer
         return ml
 
 
-def block_entries(layer_index, tensors):
+def quantize_int8_rows(w_bf16, group=128):
+    """Symmetric int8 rows with fp16 group scales, as the reference's converter makes them for --dense int8
+    (quant_int8_rows, convert.py:162-169): per (row, group of `group` inputs) scale = absmax / 127 (1 where the
+    group is all zero), q = clip(rint(w / scale), -127, 127) computed with the fp32 scale, the scale stored as fp16.
+    w_bf16: uint16 bf16 bit patterns [N, K]. Returns (int8 [N, K], float16 [N, K / group])."""
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    N, K = w.shape
+    f = (w.astype(np.uint32) << 16).view(np.float32).reshape(N, K // group, group)
+    amax = np.abs(f).max(axis=2, keepdims=True)
+    scale = np.where(amax > 0, amax / np.float32(127.0), np.float32(1.0)).astype(np.float32)
+    q = np.clip(np.rint(f / scale), -127, 127).astype(np.int8).reshape(N, K)
+    return q, scale.reshape(N, K // group).astype(np.float16)
+
+
+def dequantize_int8_rows(q, scales):
+    """bf16 bit patterns of q * scale (the product is exact in fp32; one round to nearest even), the values the
+    loader puts on the device for an int8 shared expert."""
+    q = np.asarray(q, np.int8)
+    N, K = q.shape
+    g = K // scales.shape[1]
+    f = q.astype(np.float32) * np.repeat(np.asarray(scales, np.float16).astype(np.float32), g, axis=1)
+    u = f.view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def block_entries(layer_index, tensors, shared_int8_group=None):
     """(name, dtype, array) pack entries for one layer's block from MoeLayer-keyed host arrays (bf16 and f16 as
     16-bit patterns, INT4 packed as uint8), in the order the reference's converter writes them
-    (convert.py:372-415: norms, router, shared expert, routed experts)."""
+    (convert.py:372-415: norms, router, shared expert, routed experts). With shared_int8_group, the shared expert's
+    two matrices are written as int8 rows + fp16 scales (quantize_int8_rows), as convert.py --dense int8 does."""
     order = ("rms2", "router", "shared_gate_up", "shared_down", "shared_gate", "exp_gu_q", "exp_gu_s", "exp_dn_q",
              "exp_dn_s")
     by_field = {f: (sub, dt) for f, sub, dt in BLOCK_TENSORS}
@@ -156,6 +194,10 @@ def block_entries(layer_index, tensors):
         a = np.ascontiguousarray(tensors[f])
         if dt in ("bf16", "f16"):
             a = a.view(np.uint16) if a.dtype != np.float16 else a
+        if shared_int8_group and f in ("shared_gate_up", "shared_down"):
+            q, sc = quantize_int8_rows(a, shared_int8_group)
+            out += [(f"L{layer_index}.{sub}.q8", "i8", q), (f"L{layer_index}.{sub}.s8", "f16", sc)]
+            continue
         out.append((f"L{layer_index}.{sub}", dt, a))
     return out
 

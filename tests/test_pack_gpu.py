@@ -15,24 +15,31 @@ pytestmark = pytest.mark.gpu
 TOL_BF16 = 1e-2
 
 
-def _write(tmp_path, s, seeds):
+def _write(tmp_path, s, seeds, int8_group=None):
+    """A pack of seeded layers; with int8_group the shared expert is stored as int8 rows (convert.py --dense int8)
+    and the returned host layers carry the bf16 values the loader dequantises them to."""
     from mvcc_b200 import MoeShape, pack
     ms = MoeShape(H=s.H, E=s.E, TOPK=s.TOPK, I=s.I, Is=s.Is, G=s.G, eps=s.eps)
     layers = [O.make_layer(s, sd) for sd in seeds]
     ents = []
     for li, L in enumerate(layers):
-        ents += pack.block_entries(li, L)
+        ents += pack.block_entries(li, L, shared_int8_group=int8_group)
     path = pack.write_pack(str(tmp_path / "m.mvccq"), pack.pack_config(ms, len(layers)), ents)
+    if int8_group:
+        with pack.MoePack(path) as pk:
+            layers = [dict(L, **{f: pk.layer_host(li)[f] for f in ("shared_gate_up", "shared_down")})
+                      for li, L in enumerate(layers)]
     return path, layers
 
 
-@pytest.mark.parametrize("G", [64, 128])
+@pytest.mark.parametrize("G,int8", [(64, None), (128, None), (64, 128)])
 @pytest.mark.parametrize("T", [2, 16])
-def test_block_on_uploaded_layer_matches_oracle(tmp_path, G, T):
+def test_block_on_uploaded_layer_matches_oracle(tmp_path, G, int8, T):
+    """int8 = 128: the shared expert stored as int8 rows with group-128 scales, dequantised to bf16 by the loader."""
     import mvcc_b200 as m
     from mvcc_b200 import pack
     s = O.Shape(H=1024, E=32, TOPK=8, I=512, Is=512, G=G)
-    path, layers = _write(tmp_path, s, (21, 22))
+    path, layers = _write(tmp_path, s, (21, 22), int8)
     with pack.MoePack(path) as pk:
         layer = pk.layer(1)
     torch.cuda.synchronize()  # pack closed: the copies must not depend on the mapping any more
