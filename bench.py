@@ -20,9 +20,12 @@ Further objects on the same line:
   e2e             the headline steps with each step's input (hidden fp32, attn_out bf16) copied from pinned host
                   memory and its outputs (hidden, normed) copied back inside the timed region;
   ep_prefill      BASELINE config 5: 16384 tokens per step through one int4 MoE layer, the 256 experts sharded over
-                  the N ranks (N = 1: the single-GPU prefill block; N > 1: mvcc_b200.ep over NCCL all-to-all, each
+                  the N ranks (N = 1: the single-GPU prefill block; N > 1: mvcc_b200.ep, records and partial rows
+                  moved by the kernels' peer-memory stores (or NCCL all-to-all with --ep-exchange nccl), each
                   rank holding 16384 / N of the tokens), tokens/s of the whole job from the max-over-ranks time
                   (`scaling` strong: the total work is fixed);
+  pack_load       one full-geometry layer loaded from a .mvccq weight pack into HBM (the library's pack loader),
+                  N = 1 only, skipped with --quick;
   cpu_baseline    the C oracle (test infrastructure) of the decode block on the host cores, N=1 rank 0 only.
 Under torchrun (N > 1) every rank runs its own replica of the single-GPU workloads (`value`, decode_batches,
 prefill; `scaling` weak: the decode block does not shard); ep_prefill is the sharded one.
@@ -488,6 +491,48 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
     return out
 
 
+def pack_load_case(m, shape, reps=3):
+    """One full-geometry layer loaded from a .mvccq pack into HBM through the library's loader
+    (moe_pack_upload_layer; the reference's Model::load lines, qwen.cu:181-190): random bytes in the pack layout,
+    written once to a temporary file, then read from the page cache and copied to the device `reps` times; best of
+    the reps, host wall clock around the call and a device synchronize. Failures are reported, not raised."""
+    import tempfile
+    from mvcc_b200 import pack
+    try:
+        s = shape
+        rng = np.random.default_rng(0)
+
+        def u16(*shp):
+            return rng.integers(0, 1 << 16, shp, dtype=np.uint16)
+
+        def u8(*shp):
+            return rng.integers(0, 256, shp, dtype=np.uint8)
+
+        t = {"rms2": u16(s.H), "router": u16(s.E, s.H), "exp_gu_q": u8(s.E, 2 * s.I, s.H // 2),
+             "exp_gu_s": u16(s.E, 2 * s.I, s.H // s.G), "exp_dn_q": u8(s.E, s.H, s.I // 2),
+             "exp_dn_s": u16(s.E, s.H, s.I // s.G), "shared_gate_up": u16(2 * s.Is, s.H),
+             "shared_down": u16(s.H, s.Is), "shared_gate": u16(s.H)}
+        with tempfile.TemporaryDirectory() as d:
+            path = pack.write_pack(os.path.join(d, "layer.mvccq"), pack.pack_config(s, 1), pack.block_entries(0, t))
+            del t
+            best = None
+            with pack.MoePack(path) as pk:
+                n = pk.layer_bytes(0)
+                for _ in range(reps):
+                    torch.cuda.synchronize()
+                    t0 = time.perf_counter()
+                    ml = pk.layer(0)
+                    torch.cuda.synchronize()
+                    dt = time.perf_counter() - t0
+                    best = dt if best is None else min(best, dt)
+                    del ml
+        return {"bytes": n, "ms": best * 1e3, "gbs": n / best / 1e9, "reps": reps,
+                "how": "moe_pack_upload_layer: page-cached file mapping -> one pageable host-to-device copy per "
+                       "tensor, 256-byte aligned in one device region; best of reps"}
+    except Exception as e:  # noqa: BLE001 -- reported in the JSON line
+        return {"error": f"{type(e).__name__}: {e}"}
+
+
 def b200_arm(args, rank, world, local):
     import mvcc_b200 as m
     dev = torch.device("cuda", local)
@@ -576,6 +621,9 @@ def b200_arm(args, rank, world, local):
         result["decode_batches"] = extra
     del blocks, layers
     torch.cuda.empty_cache()
+    if world == 1 and not args.quick:
+        result["pack_load"] = pack_load_case(m, shape)
+        torch.cuda.empty_cache()
     if not args.no_prefill:
         do_cpu = world == 1 and rank == 0 and not args.no_cpu
         result["prefill"] = prefill_case(m, shape, args.prefill_steps, W, stream, world, dev, peaks,
