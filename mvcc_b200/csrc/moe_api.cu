@@ -13,6 +13,8 @@
 
 #include <cstdlib>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "moe_common.cuh"
 #include "../../include/moe_ep.h"
 #include "moe_decode.h"
@@ -21,6 +23,17 @@
 #include "moe_prefill.h"
 
 using namespace moe;
+
+namespace {
+// One NVTX range per entry-point call, named after the entry point (visible in Nsight timelines; with no tool
+// attached NVTX calls return at once).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+}  // namespace
 
 namespace {
 
@@ -230,6 +243,7 @@ int block_forward_impl(const moe_layer_weights* w, void* workspace, size_t works
 int moe_block_forward(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
                       const uint16_t* attn_out, uint16_t* normed, const uint16_t* next_rms1, int T,
                       moe_stream_t stream) {
+  NvtxRange nvtx("moe_block_forward");
   return block_forward_impl(w, workspace, workspace_bytes, hidden, attn_out, normed, next_rms1, T, nullptr,
                             (cudaStream_t)stream);
 }
@@ -237,6 +251,7 @@ int moe_block_forward(const moe_layer_weights* w, void* workspace, size_t worksp
 int moe_block_forward_events(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
                              const uint16_t* attn_out, uint16_t* normed, const uint16_t* next_rms1, int T,
                              void* const* events, moe_stream_t stream) {
+  NvtxRange nvtx("moe_block_forward_events");
   if (!events) return (int)cudaErrorInvalidValue;
   return block_forward_impl(w, workspace, workspace_bytes, hidden, attn_out, normed, next_rms1, T, events,
                             (cudaStream_t)stream);
@@ -256,6 +271,7 @@ int moe_event_elapsed_ms(void* start, void* stop, float* ms) {
 
 int moe_router_topk(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const uint16_t* normed,
                     float* logits, int32_t* idx, float* wts, int T, moe_stream_t stream) {
+  NvtxRange nvtx("moe_router_topk");
   int rc = check_common(w, workspace, workspace_bytes, T);
   if (rc) return rc;
   if (!normed || !logits || !idx || !wts || !w->router) return (int)cudaErrorInvalidValue;
@@ -284,6 +300,7 @@ int moe_router_topk(const moe_layer_weights* w, void* workspace, size_t workspac
 int moe_routed_experts(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const uint16_t* normed,
                        const int32_t* idx, const float* wts, float* routed, uint16_t* inter_out, int T,
                        moe_stream_t stream) {
+  NvtxRange nvtx("moe_routed_experts");
   int rc = check_common(w, workspace, workspace_bytes, T);
   if (rc) return rc;
   if (!normed || !idx || !wts || !routed || !weights_present(w, false, true, false)) return (int)cudaErrorInvalidValue;
@@ -315,6 +332,7 @@ int moe_routed_experts(const moe_layer_weights* w, void* workspace, size_t works
 
 int moe_shared_expert(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const uint16_t* normed,
                       uint16_t* sout, int T, moe_stream_t stream) {
+  NvtxRange nvtx("moe_shared_expert");
   int rc = check_common(w, workspace, workspace_bytes, T);
   if (rc) return rc;
   if (!normed || !sout || !weights_present(w, false, false, true)) return (int)cudaErrorInvalidValue;
@@ -387,6 +405,7 @@ size_t moe_ep_record_bytes(const moe_layer_weights* w) {
 int moe_ep_dispatch(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const float* hidden,
                     const uint16_t* attn_out, uint16_t* normed, int T, int world, void* send, int32_t* send_count,
                     int32_t* tok_pos, moe_stream_t stream) {
+  NvtxRange nvtx("moe_ep_dispatch");
   if (!ep_geometry_ok(w, world) || !workspace || T < 1) return (int)cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < layout_for(w, T).total)
     return (int)cudaErrorInvalidValue;
@@ -406,6 +425,7 @@ int moe_ep_dispatch(const moe_layer_weights* w, void* workspace, size_t workspac
 
 int moe_ep_experts(const moe_layer_weights* w_local, void* workspace, size_t workspace_bytes, const void* recv, int R,
                    float* part, moe_stream_t stream) {
+  NvtxRange nvtx("moe_ep_experts");
   if (!shape_ok(w_local) || !prefill_supported(*w_local) || !workspace || R < 0) return (int)cudaErrorInvalidValue;
   if (!weights_present(w_local, false, true, false)) return (int)cudaErrorInvalidValue;
   if (R == 0) return 0;
@@ -427,6 +447,7 @@ int moe_ep_experts(const moe_layer_weights* w_local, void* workspace, size_t wor
 int moe_ep_combine(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
                    const uint16_t* attn_out, const uint16_t* sout, uint16_t* normed, const uint16_t* next_rms1,
                    int T, int world, const int32_t* tok_pos, const float* ret, moe_stream_t stream) {
+  NvtxRange nvtx("moe_ep_combine");
   if (!ep_geometry_ok(w, world) || !workspace || T < 1) return (int)cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < layout_for(w, T).total)
     return (int)cudaErrorInvalidValue;
@@ -483,6 +504,7 @@ static EpPeers to_peers(const moe_ep_peers* p) {
 int moe_ep_dispatch_peers(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, const float* hidden,
                           const uint16_t* attn_out, uint16_t* normed, int T, int world, const moe_ep_peers* peers,
                           int32_t* send_count, int32_t* tok_pos, moe_stream_t stream) {
+  NvtxRange nvtx("moe_ep_dispatch_peers");
   if (!ep_geometry_ok(w, world) || !workspace || T < 1 || !peers_ok(peers, world) || T > peers->cap)
     return (int)cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < layout_for(w, T).total)
@@ -502,6 +524,7 @@ int moe_ep_dispatch_peers(const moe_layer_weights* w, void* workspace, size_t wo
 
 int moe_ep_experts_peers(const moe_layer_weights* w_local, void* workspace, size_t workspace_bytes, int world,
                          const moe_ep_peers* peers, moe_stream_t stream) {
+  NvtxRange nvtx("moe_ep_experts_peers");
   if (!shape_ok(w_local) || !prefill_supported(*w_local) || !workspace || world < 1 || world > kEpMaxWorld ||
       !peers_ok(peers, world) || !weights_present(w_local, false, true, false))
     return (int)cudaErrorInvalidValue;
