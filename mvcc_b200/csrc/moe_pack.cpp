@@ -630,8 +630,10 @@ int moe_pack_upload_layer(moe_pack* pk, int layer, void* dev, size_t dev_bytes, 
     const size_t n = (size_t)src[i].nbytes();
     // Pageable source (the mapping, or the dequantised rows of an int8 shared expert): the call returns after the
     // bytes are staged, so the source may be released afterwards.
+    const bool cached = pk->dequant.count({layer, i}) != 0;
     const cudaError_t e =
         cudaMemcpyAsync(dst, host_block_bytes(pk, layer, i, src[i]), n, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    if (!src[i].e && !cached) pk->dequant.erase({layer, i});  // rows made only for this copy: already staged
     if (e != cudaSuccess) return pk->set_err((int)e, "host-to-device copy failed: %s", cudaGetErrorString(e));
     ptr[i] = dst;
     at += align_up(n);
