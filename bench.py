@@ -654,10 +654,11 @@ def oracle_shape(shape):
     return O.Shape(H=shape.H, E=shape.E, TOPK=shape.TOPK, I=shape.I, Is=shape.Is, G=shape.G, eps=shape.eps)
 
 
-def time_oracle(L, shape, B, seconds, mode=0, max_steps=None):
+def time_oracle(L, shape, B, seconds, mode=0, max_steps=None, threads=None):
+    """Steps of the C oracle's block on `threads` host threads (default: all) within `seconds`."""
     from oracle import oracle as O
     orc = O.Oracle()
-    n = orc.max_threads()
+    n = orc.max_threads() if threads is None else threads
     orc.set_threads(n)
     s = oracle_shape(shape)
     hidden, attn = O.make_activations(s, B, 3)
@@ -674,11 +675,15 @@ def time_oracle(L, shape, B, seconds, mode=0, max_steps=None):
 
 
 def cpu_baseline(layer, shape, B, seconds):
+    """The oracle's block on every host thread, plus a shorter single-thread (scalar) timing beside it."""
     L = host_layer(layer)
     steps, el, n = time_oracle(L, shape, B, seconds)
+    s1, el1, _ = time_oracle(L, shape, B, max(1.0, seconds / 4), threads=1)
     return {"value": steps * B / el, "unit": "tok/s", "cores": n, "kind": "port",
             "sample": f"{steps} decode steps of batch {B} through the C oracle of the block (decode numerics) on one "
-                      f"layer, {el:.1f} s, {n} threads ({os.cpu_count()} logical CPUs)"}
+                      f"layer, {el:.1f} s, {n} threads ({os.cpu_count()} logical CPUs)",
+            "single_thread": {"value": s1 * B / el1, "unit": "tok/s", "cores": 1,
+                              "sample": f"{s1} decode steps of batch {B}, {el1:.1f} s, 1 thread"}}
 
 
 def cpu_prefill(layer, shape, bias, seconds, tokens=64):

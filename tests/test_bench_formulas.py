@@ -95,3 +95,17 @@ def test_clock_summary_reads_reasons_and_window():
     s = cs.summary(1.6, 1.7)
     assert s["samples"] == 1 and s["sm_mhz"] == 1900.0 and s["window"] == "within 0.5 s of the timed region"
     assert cs.summary(20.0, 21.0)["sm_mhz"] is None
+
+
+def test_oracle_timing_thread_counts():
+    """The CPU baseline's timing loop runs the oracle's block on the requested host threads (1 = the scalar
+    timing beside the all-threads one)."""
+    b = load_bench()
+    import mvcc_b200 as m
+    from oracle import oracle as O
+    s = m.MoeShape(H=256, E=8, TOPK=2, I=128, Is=128, G=64)
+    L = O.make_layer(b.oracle_shape(s), 1)
+    steps, el, n = b.time_oracle(L, s, 1, 0.05, threads=1)
+    assert n == 1 and steps >= 1 and el >= 0.05
+    steps, el, n = b.time_oracle(L, s, 2, 0.05, max_steps=3)
+    assert n == O.Oracle().max_threads() and steps == 3 or el >= 0.05
