@@ -52,7 +52,8 @@ class DeviceBuffer:
             self.ptr = None
 
     def __del__(self):
-        self.free()
+        if _lib is not None:  # not during interpreter teardown
+            self.free()
 
 
 def _ipc_open(handle):
@@ -158,7 +159,12 @@ class EpRank:
         self.peers = None
 
     # -- peer-mode stages
+    def _need_peers(self):
+        if self.peers is None:
+            raise MoeError("peer exchange buffers are not mapped: call open_peers() (or set_peers()) first")
+
     def dispatch_peers(self, hidden, attn_out, normed, stream):
+        self._need_peers()
         T = hidden.shape[0]
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens > max_tokens {self.max_tokens}")
@@ -173,6 +179,7 @@ class EpRank:
         self._shared_done.record(self.side)
 
     def experts_peers(self, stream):
+        self._need_peers()
         _check(_lib.moe_ep_experts_peers(ctypes.byref(self.shard.c), _ptr(self.xws), self.xws_bytes, self.world,
                                          ctypes.byref(self.peers), _stream(stream)), "moe_ep_experts_peers")
 
