@@ -396,4 +396,4 @@ def emulated_step_peers(ranks, hiddens, attn_outs, normeds, next_rms1=None, stre
 
 
 __all__ = ["ExpertShard", "EpRank", "NcclExchange", "ExpertParallelMoe", "ep_step", "ep_step_peers", "emulated_step",
-           "emulated_step_peers", "MoeShape", "MoeEpPeers", "DeviceBuffer"]
+           "emulated_step_peers", "MoeShape", "MoeEpPeers", "DeviceBuffer", "EpError", "check_count_matrix"]
