@@ -18,7 +18,8 @@ Further objects on the same line:
                   tok/s, the tensor-pipe roofline of its dominant kernel (the routed gate/up grouped GEMM) and of
                   the whole block, its own e2e and clocks, and the C oracle on a bounded token sample;
   e2e             the headline steps with each step's input (hidden fp32, attn_out bf16) copied from pinned host
-                  memory and its outputs (hidden, normed) copied back inside the timed region;
+                  memory and its outputs (hidden, normed) copied back inside the timed region, one copy each way
+                  (the tensors sit back to back in one device buffer);
   ep_prefill      BASELINE config 5: 16384 tokens per step through one int4 MoE layer, the 256 experts sharded over
                   the N ranks (N = 1: the single-GPU prefill block; N > 1: mvcc_b200.ep, records and partial rows
                   moved by the kernels' peer-memory stores (or NCCL all-to-all with --ep-exchange nccl), each
@@ -250,23 +251,37 @@ def stage_times(m, fwd_events, S, reps, stream):
     return acc * 1e3 / (reps * S)
 
 
+def packed_io(hidden, attn, normed):
+    """One device buffer holding a step's inputs and outputs back to back -- attn_out (bf16), hidden (fp32, in and
+    out), normed (bf16) -- so that the inputs are one contiguous range (attn_out + hidden) and the results another
+    (hidden + normed): one host-to-device and one device-to-host copy per step. Returns the buffer, the three views
+    (initialised from the given tensors) and the input and output ranges."""
+    T, H = hidden.shape
+    na, nh, nn = attn.numel() * 2, hidden.numel() * 4, normed.numel() * 2
+    buf = torch.empty(na + nh + nn, dtype=torch.uint8, device=hidden.device)
+    a_v = buf[:na].view(torch.int16).view(T, H)
+    h_v = buf[na:na + nh].view(torch.float32).view(T, H)
+    n_v = buf[na + nh:].view(torch.int16).view(T, H)
+    a_v.copy_(attn)
+    h_v.copy_(hidden)
+    n_v.copy_(normed)
+    return buf, a_v, h_v, n_v, buf[:na + nh], buf[na:]
+
+
 def e2e_time(block_at, hidden, attn, normed, K, stream, world):
-    """The same steps fed from pinned host memory: H2D of hidden + attn_out and D2H of hidden + normed per step
-    inside the timed region."""
-    h_in = hidden.cpu().pin_memory()
-    a_in = attn.cpu().pin_memory()
-    h_out = torch.empty_like(h_in).pin_memory()
-    n_out = torch.empty(normed.shape, dtype=normed.dtype).pin_memory()
+    """The same steps fed from pinned host memory: inside the timed region, every step copies its inputs (attn_out
+    + hidden, one contiguous range) host-to-device and its results (hidden + normed) device-to-host."""
+    _, a_v, h_v, n_v, inp, out = packed_io(hidden, attn, normed)
+    host_in = inp.cpu().pin_memory()
+    host_out = torch.empty(out.numel(), dtype=torch.uint8).pin_memory()
 
     def step(i):
-        hidden.copy_(h_in, non_blocking=True)
-        attn.copy_(a_in, non_blocking=True)
-        block_at(i).forward(hidden, attn, normed, stream=stream)
-        h_out.copy_(hidden, non_blocking=True)
-        n_out.copy_(normed, non_blocking=True)
+        inp.copy_(host_in, non_blocking=True)
+        block_at(i).forward(h_v, a_v, n_v, stream=stream)
+        host_out.copy_(out, non_blocking=True)
 
     ms, _ = timed(graph_plan(step, K, stream), stream, world)
-    return ms, h_in.numel() * 4 + a_in.numel() * 2, h_out.numel() * 4 + n_out.numel() * 2
+    return ms, host_in.numel(), host_out.numel()
 
 
 def launches_per_step(T, fused_max=7, prefill_min=8, chunk=16):

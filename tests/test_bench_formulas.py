@@ -109,3 +109,23 @@ def test_oracle_timing_thread_counts():
     assert n == 1 and steps >= 1 and el >= 0.05
     steps, el, n = b.time_oracle(L, s, 2, 0.05, max_steps=3)
     assert n == O.Oracle().max_threads() and steps == 3 or el >= 0.05
+
+
+def test_packed_io_layout():
+    """e2e steps move their inputs in one copy (attn_out + hidden) and their results in one copy (hidden + normed):
+    the views alias one buffer in that order, 16-byte aligned, with the byte counts of the separate tensors."""
+    b = load_bench()
+    import torch
+    T, H = 3, 2048
+    h = torch.randn(T, H)
+    a = torch.randint(-30000, 30000, (T, H), dtype=torch.int16)
+    n = torch.zeros(T, H, dtype=torch.int16)
+    buf, av, hv, nv, inp, out = b.packed_io(h, a, n)
+    assert torch.equal(av, a) and torch.equal(hv, h) and torch.equal(nv, n)
+    assert inp.numel() == a.numel() * 2 + h.numel() * 4 and out.numel() == h.numel() * 4 + n.numel() * 2
+    hv.add_(1)
+    nv.fill_(7)
+    o = out.clone()
+    assert torch.equal(o[:T * H * 4].view(torch.float32).view(T, H), h + 1)
+    assert bool((o[T * H * 4:].view(torch.int16) == 7).all())
+    assert all(t.data_ptr() % 16 == 0 for t in (av, hv, nv))
