@@ -233,3 +233,78 @@ def write_pack(path, config, entries, header_slot=HEADER_SLOT):
             f.write(a.tobytes())
             pos = o + a.nbytes
     return path
+
+
+def synth_pack(path, shape: MoeShape, layers, seed=0, std=0.02, shared_int8_group=None):
+    """Writes a pack of `layers` seeded synthetic MoE layers (host numpy PCG64 draws, no GPU): bf16 N(0, std) router
+    and shared expert, rms2 = 1, and experts quantised by the rule of the device generator (moe_synth_int4_rows):
+    weights rounded to bf16, then per group of G inputs scale = fp16(absmax / 7) and q = clamp(rint(w / scale),
+    -7, 7) + 8 with that fp16 scale. The way to get group-64 packs, which no GPTQ checkpoint can be repacked to."""
+    s = shape
+    rng = np.random.default_rng(seed)
+
+    def bf16(*shp):
+        f = (std * rng.standard_normal(shp)).astype(np.float32)
+        u = f.view(np.uint32).astype(np.uint64)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even
+
+    def int4_rows(n, k):
+        w = (bf16(n, k // s.G, s.G).astype(np.uint32) << 16).view(np.float32)
+        sc = (np.abs(w).max(axis=2, keepdims=True) / 7).astype(np.float16)
+        scf = sc.astype(np.float32)
+        q = np.clip(np.rint(np.divide(w, scf, out=np.zeros_like(w), where=scf > 0)), -7, 7).astype(np.int32) + 8
+        q = q.reshape(n, k).astype(np.uint8)
+        return (q[:, 0::2] | (q[:, 1::2] << 4)).astype(np.uint8), sc.reshape(n, k // s.G)
+
+    ents = []
+    for li in range(layers):
+        gq, gs = int4_rows(s.E * 2 * s.I, s.H)
+        dq, ds = int4_rows(s.E * s.H, s.I)
+        t = {"rms2": np.full(s.H, 0x3F80, np.uint16), "router": bf16(s.E, s.H),
+             "exp_gu_q": gq.reshape(s.E, 2 * s.I, s.H // 2), "exp_gu_s": gs.reshape(s.E, 2 * s.I, s.H // s.G),
+             "exp_dn_q": dq.reshape(s.E, s.H, s.I // 2), "exp_dn_s": ds.reshape(s.E, s.H, s.I // s.G),
+             "shared_gate_up": bf16(2 * s.Is, s.H), "shared_down": bf16(s.H, s.Is), "shared_gate": bf16(s.H)}
+        ents += block_entries(li, t, shared_int8_group=shared_int8_group)
+    extra = {"dense": "int8"} if shared_int8_group else {}
+    return write_pack(path, pack_config(s, layers, **extra), ents)
+
+
+def _main(argv=None):
+    import argparse
+    ap = argparse.ArgumentParser(prog="python -m mvcc_b200.pack",
+                                 description="Inspect a .mvccq pack, or write a synthetic one.")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    pi = sub.add_parser("info", help="geometry, tensor count and each layer's block bytes on the device")
+    pi.add_argument("pack")
+    ps = sub.add_parser("synth", help="write a pack of seeded synthetic MoE layers")
+    ps.add_argument("out")
+    ps.add_argument("--layers", type=int, default=1)
+    ps.add_argument("--hidden", type=int, default=2048)
+    ps.add_argument("--experts", type=int, default=256)
+    ps.add_argument("--topk", type=int, default=8)
+    ps.add_argument("--inter", type=int, default=512)
+    ps.add_argument("--shared-inter", type=int, default=512)
+    ps.add_argument("--group", type=int, default=64)
+    ps.add_argument("--seed", type=int, default=0)
+    ps.add_argument("--int8-shared", type=int, default=0, metavar="GROUP",
+                    help="store the shared expert as int8 rows with this scale group (convert.py --dense int8)")
+    a = ap.parse_args(argv)
+    if a.cmd == "synth":
+        s = MoeShape(H=a.hidden, E=a.experts, TOPK=a.topk, I=a.inter, Is=a.shared_inter, G=a.group)
+        synth_pack(a.out, s, a.layers, seed=a.seed, shared_int8_group=a.int8_shared or None)
+        print(f"wrote {a.out}: {a.layers} layer(s), {os.path.getsize(a.out)} bytes")
+        return 0
+    with MoePack(a.pack) as pk:
+        s = pk.shape
+        print(f"{a.pack}: H={s.H} E={s.E} topk={s.TOPK} I={s.I} Is={s.Is} group={s.G} eps={s.eps:g} "
+              f"layers={pk.layers} tensors={len(pk.names())}")
+        for li in range(pk.layers):
+            try:
+                print(f"  L{li}: block {pk.layer_bytes(li)} bytes on the device")
+            except PackError as e:
+                print(f"  L{li}: {e}")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(_main())

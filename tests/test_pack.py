@@ -359,3 +359,24 @@ def test_int8_shared_expert_within_the_bf16_bar_of_int8_gemv_numerics(orc):
     inter = bf(g / (1.0 + np.exp(-g)) * u)
     sout = bf(inter @ deq(qdn, sdn).T)
     assert O.max_rel_err(O.bf16_to_f32(ref["sout"]), sout) < 1e-2
+
+
+def test_synth_pack_and_command_line(tmp_path, capsys):
+    """`python -m mvcc_b200.pack synth` writes a loadable pack whose INT4 experts follow the generator's rule, and
+    `info` reports its geometry and each layer's device bytes."""
+    pk_mod = P()
+    out = tmp_path / "syn.mvccq"
+    assert pk_mod._main(["synth", str(out), "--layers", "2", "--hidden", "256", "--experts", "8", "--topk", "2",
+                         "--inter", "128", "--shared-inter", "128", "--group", "64", "--int8-shared", "128"]) == 0
+    with pk_mod.MoePack(str(out)) as pk:
+        assert (pk.shape.H, pk.shape.E, pk.shape.G, pk.layers) == (256, 8, 64, 2)
+        h = pk.layer_host(1)
+        q = h["exp_gu_q"]
+        nib = np.stack([q & 15, q >> 4], axis=-1).reshape(q.shape[0], q.shape[1], -1)
+        assert nib.min() >= 1 and nib.max() <= 15  # q - 8 in [-7, 7]
+        sc = h["exp_gu_s"].astype(np.float32)
+        assert (sc > 0).all() and sc.max() < 0.02 * 6 / 7
+        assert "L0.shared.down.q8" in pk.names()
+    assert pk_mod._main(["info", str(out)]) == 0
+    text = capsys.readouterr().out
+    assert "H=256 E=8 topk=2 I=128 Is=128 group=64" in text and "L1: block" in text
