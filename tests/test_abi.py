@@ -128,3 +128,42 @@ def test_expert_parallel_entry_points_check_before_launch():
     peers.rank = 2
     assert lib.moe_ep_experts_peers(ctypes.byref(wl), ws, 1 << 30, 2, ctypes.byref(peers), None) == 1
     assert ctypes.sizeof(ep.MoeEpPeers) == 3 * 8 * 8 + 8
+
+
+def _abi_program(names):
+    """A program that includes every header and references every declared entry point (its address), so that
+    compiling it checks the headers and linking it checks the library's exports, from C and from C++."""
+    incs = "".join(f'#include "{os.path.basename(h)}"\n' for h in HEADERS)
+    refs = "".join(f"  (void *)&{n},\n" for n in names)
+    return (incs + "#include <stdio.h>\n"
+            "int main(void) {\n"
+            f"  void *fns[] = {{\n{refs}  0}};\n"
+            "  int n = 0;\n"
+            "  for (unsigned i = 0; i + 1 < sizeof fns / sizeof fns[0]; ++i) n += fns[i] != 0;\n"
+            "  moe_stats st;\n"
+            "  moe_stats_get(&st);\n"
+            "  printf(\"%d %llu\\n\", n, (unsigned long long)st.launches);\n"
+            "  return 0;\n}\n")
+
+
+@pytest.mark.parametrize("lang", ["c", "c++"])
+def test_headers_compile_and_link_from_c_and_cpp(tmp_path, lang):
+    """The boundary is a C ABI: the headers compile as C11 and C++17 with warnings as errors, and a program that
+    references every declared entry point links against libmoe_b200.so and runs on a host without a GPU."""
+    import subprocess
+
+    import mvcc_b200
+    names = _declared()
+    src = tmp_path / ("abi.c" if lang == "c" else "abi.cpp")
+    src.write_text(_abi_program(names))
+    exe = tmp_path / "abi"
+    cc = ["gcc", "-std=c11"] if lang == "c" else ["g++", "-std=c++17"]
+    libdir = os.path.dirname(mvcc_b200.LIB_PATH)
+    cmd = cc + ["-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe),
+                "-L", libdir, "-lmoe_b200", f"-Wl,-rpath,{libdir}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr
+    n, launches = run.stdout.split()
+    assert int(n) == len(names) and int(launches) == 0
