@@ -167,3 +167,31 @@ def test_headers_compile_and_link_from_c_and_cpp(tmp_path, lang):
     assert run.returncode == 0, run.stderr
     n, launches = run.stdout.split()
     assert int(n) == len(names) and int(launches) == 0
+
+
+def build_block_host(out_dir):
+    """Compiles tests/cpp/qwen_block_host.cpp (the block driven from C++ as qwen.cu would: pack -> HBM, workspace,
+    forward, error word) against include/ and libmoe_b200.so; returns the executable's path."""
+    import subprocess
+
+    import mvcc_b200
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    libdir = os.path.dirname(mvcc_b200.LIB_PATH)
+    exe = os.path.join(str(out_dir), "qwen_block_host")
+    cmd = ["g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+           "-I", os.path.join(cuda, "include"), os.path.join(ROOT, "tests", "cpp", "qwen_block_host.cpp"),
+           "-o", exe, "-L", libdir, "-lmoe_b200", f"-Wl,-rpath,{libdir}", "-L", os.path.join(cuda, "lib64"),
+           "-lcudart", f"-Wl,-rpath,{os.path.join(cuda, 'lib64')}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    return exe
+
+
+def test_cpp_block_host_builds(tmp_path):
+    """The C++ driver of the INTEGRATION.md sequence compiles and links; without arguments it prints its usage."""
+    import subprocess
+    exe = build_block_host(tmp_path)
+    run = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 2 and "usage" in run.stderr
+    run = subprocess.run([exe, str(tmp_path / "missing.mvccq")], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 1 and "cannot open" in run.stderr  # refused before any CUDA call
