@@ -5,7 +5,7 @@
 //
 //   qwen_block_host PACK [LAYER] [T]     prints "ok T=<T> launches=<n> max|hidden|=<v>" and exits 0 on success
 //
-// Test infrastructure: tests/test_abi.py compiles and links it on any host; on a B200 it runs it.
+// Test infrastructure: tests/test_abi.py compiles and links it (and checks its refusals) on any host.
 #include <cuda_runtime.h>
 
 #include <cmath>
