@@ -6,7 +6,7 @@
 // of the ring holds one step's A rows and bf16 B rows; full[s] completes when both are in, empty[s] when the MMAs
 // that read them are done -- one wait and one commit per step for the issuing thread, whose shared-memory round
 // trips (a few hundred cycles per barrier operation) must stay under a step's MMA time (512 cycles at N = 256).
-// 16 warps:
+// 8 + NDW warps (NDW = 8 dequantisation warps by default, 16 optionally):
 //   warps 0-1   A producers: contiguous A rows come in as one 2D TMA tile (box 64 x 128, 128-byte swizzle) per
 //               step; gathered rows (one per (token, slot) pair of the sorted pair list) come in by cp.async,
 //               eight lanes per row so that each row is one 128-byte line request, into the same swizzled K-major
@@ -19,8 +19,9 @@
 //               step, to acc_full[buffer];
 //   warps 4-7   epilogue: wait acc_full, tcgen05.ld the accumulator rows of their TMEM lane quarter, apply the
 //               epilogue, store, release the buffer (acc_empty) -- overlapping the next item's main loop;
-//   warps 8-15  INT4 only: each thread owns (row, K half) jobs of the tile (two at BN = 256) and converts their
-//               32 nibbles per step from the raw ring into the swizzled bf16 B of stage s as dequant32_bf16 does
+//   warps 8+    INT4 only: each thread owns (row, K half) jobs of the tile (two at BN = 256 with 8 warps, one
+//               with 16) and converts their 32 nibbles per step from the raw ring into the swizzled bf16 B of
+//               stage s as dequant32_bf16 does
 //               (kernels.cuh:925-940: bf16((q - 8) * scale), one rounding), fences the writes to the async proxy and
 //               arrives on full[s]. Raw bytes and scales come by TMA: loading them through the load/store unit
 //               costs about as many cycles as the conversion itself.
@@ -38,8 +39,9 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <mutex>
+#include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "moe_common.cuh"
 #include "moe_gemm.h"
@@ -50,8 +52,10 @@ namespace moe {
 using namespace tc;
 
 constexpr int kBK = 64, kTileM = 128;
-constexpr int kGWarps = 16, kGThreads = kGWarps * 32;
-constexpr int kDeqWarp0 = 8, kDeqThreads = 256;
+// Warps 0-7 have fixed roles; NDW dequantisation warps follow (8 by default, 16 with MOE_B200_GEMM_DEQ_WARPS=16
+// for the routed INT4 GEMMs: twice the warps to hide the conversion's latency, one job per thread at BN = 256).
+constexpr int kDeqWarp0 = 8;
+__host__ __device__ constexpr int gemm_threads(int ndw) { return (kDeqWarp0 + ndw) * 32; }
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far beyond any item's main loop
 
 struct GemmCfg {
@@ -257,10 +261,11 @@ __device__ __forceinline__ GemmTile load_tile(const GemmParams& p, int ti) {
   return t;
 }
 
-template <int BN, bool INT4, int EPI>
-__global__ void __launch_bounds__(kGThreads, 1)
+template <int BN, bool INT4, int EPI, int NDW>
+__global__ void __launch_bounds__(gemm_threads(NDW), 1)
     moe_gemm_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS, const GemmCfg c) {
+  constexpr int kDeqThreads = NDW * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -550,7 +555,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
   } else if constexpr (INT4) {
     // ---- dequantization: job (row r, K half h) covers 32 nibbles of row r per step; thread td owns jobs
     // td + kDeqThreads * j
-    constexpr int J = (BN * 2 + kDeqThreads - 1) / kDeqThreads;  // jobs per thread (2 at BN = 256)
+    constexpr int J = (BN * 2 + kDeqThreads - 1) / kDeqThreads;  // jobs per thread (2 at BN = 256, NDW = 8)
     const int td = threadIdx.x - kDeqWarp0 * 32;
     const int RB = 32 * c.rk;
     int g = 0, j = 0;
@@ -675,7 +680,7 @@ static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, bool INT4, int EPI>
+template <int BN, bool INT4, int EPI, int NDW = 8>
 static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaStream_t st) {
   GemmCfg c;
   if (!pick_cfg(BN, INT4, p.K, p.G, &c)) return cudaErrorInvalidValue;
@@ -712,8 +717,8 @@ static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaSt
   }
   static size_t granted = 0;
   if (c.total > granted) {
-    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<BN, INT4, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)c.total);
+    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<BN, INT4, EPI, NDW>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.total);
     if (e != cudaSuccess) return e;
     granted = c.total;
   }
@@ -723,7 +728,7 @@ static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaSt
   if (items <= 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)std::min<int64_t>(items, sms));
-  cfg.blockDim = dim3(kGThreads);
+  cfg.blockDim = dim3(gemm_threads(NDW));
   cfg.dynamicSmemBytes = c.total;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -731,7 +736,18 @@ static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return launched(cudaLaunchKernelEx(&cfg, moe_gemm_kernel<BN, INT4, EPI>, p, tmA, tmB, tmS, c));
+  return launched(cudaLaunchKernelEx(&cfg, moe_gemm_kernel<BN, INT4, EPI, NDW>, p, tmA, tmB, tmS, c));
+}
+
+// Dequantisation warps of the routed INT4 GEMMs: 8, or 16 when the environment sets MOE_B200_GEMM_DEQ_WARPS=16
+// (read once per process).
+static int deq_warps() {
+  static int n = 0;
+  if (!n) {
+    const char* v = getenv("MOE_B200_GEMM_DEQ_WARPS");
+    n = (v && atoi(v) == 16) ? 16 : 8;
+  }
+  return n;
 }
 
 template <int BN, bool INT4>
@@ -739,9 +755,15 @@ static cudaError_t launch_epi(const GemmParams& p, int epi, int max_tiles, bool 
   switch (epi) {
     case EPI_F32: return launch_t<BN, INT4, EPI_F32>(p, max_tiles, pdl, st);
     case EPI_BF16: return launch_t<BN, INT4, EPI_BF16>(p, max_tiles, pdl, st);
-    case EPI_SILU_TILE: return launch_t<BN, INT4, EPI_SILU_TILE>(p, max_tiles, pdl, st);
+    case EPI_SILU_TILE:
+      if constexpr (BN == 256 && INT4)
+        if (deq_warps() == 16) return launch_t<256, true, EPI_SILU_TILE, 16>(p, max_tiles, pdl, st);
+      return launch_t<BN, INT4, EPI_SILU_TILE>(p, max_tiles, pdl, st);
     case EPI_SILU_ROUND: return launch_t<BN, INT4, EPI_SILU_ROUND>(p, max_tiles, pdl, st);
-    case EPI_SLOT: return launch_t<BN, INT4, EPI_SLOT>(p, max_tiles, pdl, st);
+    case EPI_SLOT:
+      if constexpr (BN == 256 && INT4)
+        if (deq_warps() == 16) return launch_t<256, true, EPI_SLOT, 16>(p, max_tiles, pdl, st);
+      return launch_t<BN, INT4, EPI_SLOT>(p, max_tiles, pdl, st);
     default: return cudaErrorInvalidValue;
   }
 }
