@@ -614,16 +614,33 @@ static int dev_attr(cudaDeviceAttr a, int fallback) {
   return v;
 }
 
+// k-steps per raw INT4 box: the preference order below, or only the value the environment sets in
+// MOE_B200_GEMM_RAW_KSTEPS (1, 2 or 4; read once per process). One k-step per box makes a box row 32 bytes, so
+// the 16 rows a dequantisation warp reads fall on distinct banks; wider boxes mean fewer, larger TMA copies.
+static int raw_ksteps_forced() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("MOE_B200_GEMM_RAW_KSTEPS");
+    const int k = e ? atoi(e) : 0;
+    v = (k == 1 || k == 2 || k == 4) ? k : 0;
+  }
+  return v;
+}
+
 static bool pick_cfg(int bn, bool int4, int K, int G, GemmCfg* out) {
   static int optin = 0;
   if (!optin) optin = dev_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin, 227 * 1024);
   // first fit in order of preference: 3+ A + B stages, then wide raw boxes, then raw ring depth
-  const int sa_c[] = {4, 3, 2}, rk_c[] = {4, 2, 1}, sr_c[] = {3, 2};
+  const int sa_c[] = {4, 3, 2}, sr_c[] = {3, 2};
+  const int forced = int4 ? raw_ksteps_forced() : 0;
+  const int rk_pref[] = {4, 2, 1}, rk_one[] = {forced, forced, forced};
+  const int* rk_c = forced ? rk_one : rk_pref;
   for (int sa : sa_c)
-    for (int rk : rk_c)
+    for (int ri = 0; ri < 3; ++ri)
       for (int sr : sr_c) {
+        const int rk = rk_c[ri];
         const GemmCfg c = gemm_cfg(bn, int4, sa, sr, rk, K, G);
-        if ((int)c.total <= optin && (sa >= 3 || rk == 1)) {
+        if ((int)c.total <= optin && (sa >= 3 || rk == 1 || forced)) {
           *out = c;
           return true;
         }
