@@ -22,8 +22,10 @@
 // so the targets follow from its value at launch start) and bounded spins; stage waits are bounded by the global
 // timer. A wait that gives up records MOE_ERR_BARRIER in the error word; the CTA skips the remaining work, still
 // arrives at the grid barriers, and before returning waits (bounded) for every copy it issued. The launch is
-// cooperative, so all CTAs are co-resident. Per-job reductions and numerics are those of the three-kernel path
-// (moe_decode.cu).
+// cooperative, so all CTAs are co-resident, and a programmatic dependent launch: the entry (barrier setup and the
+// weight copies) overlaps the previous kernel's tail, everything that reads its outputs or the workspace follows
+// griddepcontrol.wait, and phase D lets the next kernel start its own entry. Per-job reductions and numerics are
+// those of the three-kernel path (moe_decode.cu).
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
