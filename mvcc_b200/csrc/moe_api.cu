@@ -20,6 +20,7 @@
 #include "moe_decode.h"
 #include "moe_ep.h"
 #include "moe_fused.h"
+#include "moe_lean.h"
 #include "moe_prefill.h"
 
 using namespace moe;
@@ -203,7 +204,8 @@ int block_forward_impl(const moe_layer_weights* w, void* workspace, size_t works
   }
   int fs = 0, frows = 0;
   size_t fsmem = 0;
-  if (fused_enabled() && fused_config(*w, T, &fs, &fsmem, &frows)) {
+  const bool lean = lean_config(*w, T);
+  if (lean || (fused_enabled() && fused_config(*w, T, &fs, &fsmem, &frows))) {
     const WsLayout L = layout_for(w, T);
     BlockArgs a = make_args(w, workspace, L, T);
     a.hidden = hidden;
@@ -212,7 +214,8 @@ int block_forward_impl(const moe_layer_weights* w, void* workspace, size_t works
     a.next_rms1 = next_rms1;
     unsigned long long* gbar = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) + L.gbar);
     cudaError_t e = events ? record_event(events[0], s) : cudaSuccess;
-    if (e == cudaSuccess) e = launch_fused_decode(a, gbar, next_rms1 != nullptr, s);
+    if (e == cudaSuccess)
+      e = lean ? launch_lean_decode(a, gbar, next_rms1 != nullptr, s) : launch_fused_decode(a, gbar, next_rms1 != nullptr, s);
     for (int k = 1; k < 4 && events && e == cudaSuccess; ++k) e = record_event(events[k], s);
     return (int)e;
   }

@@ -26,3 +26,19 @@ def decode_only():
     m.set_prefill_min_tokens(1 << 30)
     yield
     m.set_prefill_min_tokens(0)
+
+
+def pytest_terminal_summary(terminalreporter):
+    """Prints how many tokens the GPU parity tests left out of their value comparisons (near 8th/9th routing ties)."""
+    from tests import parity
+    if not parity.EXCLUDED:
+        return
+    tot = sum(n for _, _, n, _ in parity.EXCLUDED)
+    out = sum(x for _, x, _, _ in parity.EXCLUDED)
+    tr = terminalreporter
+    tr.write_sep("-", "parity: tokens left out near routing ties")
+    tr.write_line(f"{len(parity.EXCLUDED)} comparisons, {out} of {tot} tokens left out, smallest 8th/9th margin "
+                  f"{min(m for _, _, _, m in parity.EXCLUDED):.3g}")
+    for name, x, n, m in parity.EXCLUDED:
+        if x:
+            tr.write_line(f"  {name}: {x} of {n} left out (smallest margin {m:.3g})")

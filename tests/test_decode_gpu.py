@@ -7,6 +7,7 @@ import pytest
 import torch
 
 from oracle import oracle as O
+from tests import parity
 
 pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("decode_only")]
 
@@ -76,13 +77,14 @@ def check_routing(orc, s, gpu_logits, gpu_idx, gpu_wts, ref_logits, ref_idx, ref
 def stable_rows(s, ref_logits, logit_tol=2e-3, gpu_logits=None):
     """Tokens whose 8th/9th logit margin exceeds twice the logit error (the observed GPU-vs-oracle error when the
     GPU logits are given, else the tolerance): their routing cannot flip, so their outputs must match the
-    oracle; near-tie tokens are excluded from value comparisons."""
-    srt = np.sort(ref_logits, axis=1)[:, ::-1]
-    margin = srt[:, s.TOPK - 1] - srt[:, s.TOPK]
+    oracle; near-tie tokens are excluded from value comparisons (at most 10 %, recorded by tests/parity.py)."""
+    margin = parity.topk_margin(ref_logits, s.TOPK)
     if gpu_logits is not None:
         err = np.abs(gpu_logits - ref_logits).max(axis=1)
-        return margin > 2 * err + 1e-6
-    return margin > 4 * logit_tol * np.abs(ref_logits).max()
+        ok = margin > 2 * err + 1e-6
+    else:
+        ok = margin > 4 * logit_tol * np.abs(ref_logits).max()
+    return parity.keep_stable(ok, margin)
 
 
 def check_bf16_ulps(got, want, max_ulp=2, frac_one=0.999):
@@ -179,9 +181,18 @@ def test_block_forward(orc, name, T, with_next):
     nr = O.f32_to_bf16(1.0 + 0.1 * O.normal(61, 1, s.H)) if with_next else None
     blk, gh, gn = run_block(s, layer, hidden, attn, nr)
     ref = orc.block_forward(s, L, hidden, attn, next_rms1=nr, mode=0)
-    gl = blk.trace(T)["logits"].cpu().numpy() if T <= 16 else None
+    if T <= 16:
+        gl = blk.trace(T)["logits"].cpu().numpy()
+    else:
+        # the workspace keeps only the last decode chunk's logits: route the GPU's own router input (the normed
+        # output of a run without the next layer's norm) once more on the GPU to get every token's logits
+        _, _, gn0 = run_block(s, layer, hidden, attn)
+        lg = torch.zeros(T, s.E, device="cuda")
+        blk.router_topk(to_dev16(gn0), lg, torch.zeros(T, s.TOPK, dtype=torch.int32, device="cuda"),
+                        torch.zeros(T, s.TOPK, device="cuda"))
+        torch.cuda.synchronize()
+        gl = lg.cpu().numpy()
     ok = stable_rows(s, ref["logits"], gpu_logits=gl)
-    assert ok.mean() >= 0.5
     assert O.max_rel_err(gh[ok], ref["hidden"][ok]) < TOL_BF16
     assert O.max_rel_err(O.bf16_to_f32(gn[ok]), O.bf16_to_f32(ref["normed"][ok])) < TOL_BF16
     if T <= 16:
@@ -284,7 +295,6 @@ def test_full_size_block_against_oracle(orc, T):
     check_routing(orc, s, gl, tr["idx"].cpu().numpy(), tr["wts"].cpu().numpy(),
                   ref["logits"], ref["idx"], ref["wts"], logit_tol=2e-3)
     ok = stable_rows(s, ref["logits"], gpu_logits=gl)
-    assert ok.mean() >= 0.5
     assert O.max_rel_err(tr["routed"].cpu().numpy()[ok], ref["routed"][ok]) < TOL_INT4
     assert O.max_rel_err(gh[ok], ref["hidden"][ok]) < TOL_BF16
 
@@ -320,7 +330,6 @@ def test_full_geometry_decode_kernels(orc, T):
     check_routing(orc, s, gl, tr["idx"].cpu().numpy(), tr["wts"].cpu().numpy(), ref["logits"], ref["idx"],
                   ref["wts"], logit_tol=2e-3)
     ok = stable_rows(s, ref["logits"], gpu_logits=gl)
-    assert ok.mean() >= 0.5
     assert O.max_rel_err(hid.cpu().numpy()[ok], ref["hidden"][ok]) < TOL_BF16
     assert O.max_rel_err(O.bf16_to_f32(host16(normed)[ok]), O.bf16_to_f32(ref["normed"][ok])) < TOL_BF16
     assert blk.error_word() == 0
