@@ -408,7 +408,44 @@ def prefill_case(m, shape, K, W, stream, world, dev, peaks, cpu_seconds, do_cpu)
     return out
 
 
-def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
+def ep_parity(m, shape, layer, hidden0, attn, hidden_out, normed_out, world, rank, rows=64):
+    """Parity of one untimed expert-parallel step on this rank against the oracle's expert-parallel restatement
+    (oracle.ep_block_forward: tile numerics, per-rank slot-order partials summed in rank order), on a seeded sample
+    of this rank's tokens; each token's outputs depend on that token alone. The oracle is the checker here, outside
+    the timed region. Tokens whose 8th/9th router logits lie within twice the GPU-vs-oracle logit difference can
+    route differently and are left out of the value comparison (counted in `excluded`)."""
+    from oracle import oracle as O
+    T = hidden0.shape[0]
+    sel = np.sort(np.random.default_rng(1000 + rank).choice(T, min(rows, T), replace=False))
+    L = host_layer(layer)
+    orc = O.Oracle()
+    orc.set_threads(max(1, (os.cpu_count() or 1) // world))
+    s = oracle_shape(shape)
+    h_in = hidden0[sel].cpu().numpy()
+    a_in = attn[sel].cpu().numpy().view(np.uint16)
+    ref = orc.ep_block_forward(s, L, h_in, a_in, world)
+    # the GPU's own logits for the sample: the router on the GPU's normed rows (the step's router input)
+    n = len(sel)
+    blk = m.MoeBlock(layer, n)
+    lg = torch.zeros(n, shape.E, device=hidden0.device)
+    blk.router_topk(normed_out[sel].contiguous(), lg, torch.zeros(n, shape.TOPK, dtype=torch.int32,
+                                                                  device=hidden0.device),
+                    torch.zeros(n, shape.TOPK, device=hidden0.device))
+    torch.cuda.synchronize()
+    gl = lg.cpu().numpy()
+    srt = np.sort(ref["logits"], axis=1)[:, ::-1]
+    margin = srt[:, shape.TOPK - 1] - srt[:, shape.TOPK]
+    ok = margin > 2 * np.abs(gl - ref["logits"]).max(axis=1) + 1e-6
+    gh = hidden_out[sel].cpu().numpy()
+    gn = normed_out[sel].cpu().numpy().view(np.uint16)
+    err_h = float(O.max_rel_err(gh[ok], ref["hidden"][ok])) if ok.any() else None
+    err_n = float(O.max_rel_err(O.bf16_to_f32(gn[ok]), O.bf16_to_f32(ref["normed"][ok]))) if ok.any() else None
+    return {"rows": int(n), "excluded": int((~ok).sum()), "min_topk_margin": float(margin.min()),
+            "max_rel_err_hidden": err_h, "max_rel_err_normed": err_n,
+            "pass": bool(ok.mean() >= 0.9 and err_h is not None and err_h < 1e-2 and err_n < 1e-2)}
+
+
+def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers", parity=True):
     """Config 5: EP_TOKENS tokens per step over `world` ranks, experts sharded evenly, device time max over ranks."""
     T = EP_TOKENS // world
     peer_note = None
@@ -428,6 +465,10 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
         ms, clk = timed(graph_plan(step, K, stream), stream, world, ClockSampler(dev))
         how = "single GPU: moe_block_forward prefill path (CUDA graph)"
         recv = None
+        hidden.copy_(hidden0)
+        step(0)
+        torch.cuda.synchronize()
+        h_out, n_out = hidden.clone(), normed.clone()
     else:
         import mvcc_b200.ep as ep
         st = ep.EpRank(layer, rank, world, T)
@@ -484,6 +525,11 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
                    "shared expert on a side stream")
             recv = {"records_sent_per_step": float(np.mean([s for s, _ in sizes])),
                     "records_received_per_step": float(np.mean([r for _, r in sizes]))}
+        hidden.copy_(hidden0)
+        sizes.clear()
+        step(0)  # the untimed step whose outputs the parity check reads
+        torch.cuda.synchronize()
+        h_out, n_out = hidden.clone(), normed.clone()
         assert st.error_word() == 0
         barrier(world)
         st.close_peers()
@@ -503,6 +549,18 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers"):
         out["exchange_stats"] = recv
     if peer_note:
         out["note"] = peer_note
+    if parity:
+        try:
+            p = ep_parity(m, shape, layer, hidden0, attn, h_out, n_out, world, rank)
+        except Exception as e:  # noqa: BLE001 -- reported in the JSON line
+            p = {"error": f"{type(e).__name__}: {e}"}
+        if world > 1:  # every rank's result, gathered to rank 0
+            allp = [None] * world
+            torch.distributed.all_gather_object(allp, p)
+            out["parity"] = {"per_rank": allp,
+                             "pass": all(isinstance(q, dict) and q.get("pass") for q in allp)}
+        else:
+            out["parity"] = {"per_rank": [p], "pass": bool(p.get("pass"))}
     return out
 
 
@@ -548,6 +606,72 @@ def pack_load_case(m, shape, reps=3):
         return {"error": f"{type(e).__name__}: {e}"}
 
 
+def decode_config(shape, B, world, K, layer_copies):
+    """The `config` object of the headline line; the reference arm prints the identical dict."""
+    return {
+        "workload": f"BASELINE config 2: one MoE layer, int4 G=64 experts, decode batch {B}",
+        "H": shape.H, "E": shape.E, "topk": shape.TOPK, "I": shape.I, "Is": shape.Is, "G": shape.G,
+        "batch": B, "layer_copies": layer_copies,
+        "l2": f"inputs larger than L2: consecutive steps cycle over {layer_copies} layer copies "
+              f"({layer_copies * 0.428:.1f} GB of weights); no flush",
+        "parallelism": f"replicas x{world}" if world > 1 else "single",
+        "graph_steps": min(K, GRAPH_STEPS),
+    }
+
+
+def time_graph_us(fn, steps, stream, reps=5, min_seconds=0.25):
+    """Mean us per step over replays of a graph of `steps` calls of fn(i); doubles the replay count until the timed
+    region lasts min_seconds (CUDA events on the launching stream)."""
+    g = capture(fn, steps, stream)
+    run_graphs([(g, 3)], stream)
+    torch.cuda.synchronize()
+    while True:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run_graphs([(g, reps)], stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if ms >= min_seconds * 1e3 or reps >= 4096:
+            return ms * 1e3 / (reps * steps)
+        reps *= 2
+
+
+def g128_case(m, stream, copies=16, Ts=(1, 4, 8, 16), prefill_T=4096):
+    """This library at INT4 group 128 -- the group the reference's kernels hard-code (kernels.cuh:842) -- timed the
+    way the reference arm's `ref_gpu` object times the reference's own kernels: decode blocks warm (one layer, the
+    reference's time_ms method, qwen.cu:486-498) and cold (layer copies cycled), and the routed experts of a
+    4096-token prefill on its own router's routing of N(0,1) activations."""
+    shape = m.MoeShape(G=128)
+    with torch.cuda.stream(stream):
+        layers = [m.synth_layer(shape, seed=500 + i, stream=stream) for i in range(copies)]
+    torch.cuda.synchronize()
+    out = {"group": 128, "layer_copies": copies, "decode_us": {}}
+    for T in Ts:
+        hid, attn = m.synth_activations(shape, T, 3, stream=stream)
+        normed = torch.zeros(T, shape.H, dtype=torch.int16, device=hid.device)
+        blocks = [m.MoeBlock(l, T) for l in layers]
+        torch.cuda.synchronize()
+        out["decode_us"][str(T)] = {
+            "warm": time_graph_us(lambda i: blocks[0].forward(hid, attn, normed, stream=stream), 32, stream),
+            "cold": time_graph_us(lambda i: blocks[i % copies].forward(hid, attn, normed, stream=stream), 64, stream)}
+        del blocks
+    T = prefill_T
+    blk = m.MoeBlock(layers[0], T)
+    x = torch.empty(T, shape.H, dtype=torch.int16, device="cuda")
+    m._check(m._lib.moe_synth_normal_bf16(m._ptr(x), x.numel(), 9, 1, 0.0, 1.0, m._stream(stream)), "synth")
+    logits = torch.zeros(T, shape.E, device="cuda")
+    idx = torch.zeros(T, shape.TOPK, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(T, shape.TOPK, device="cuda")
+    routed = torch.zeros(T, shape.H, device="cuda")
+    blk.router_topk(x, logits, idx, wts, stream=stream)
+    torch.cuda.synchronize()
+    us = time_graph_us(lambda i: blk.routed_experts(x, idx, wts, routed, stream=stream), 2, stream, reps=3)
+    flops = 2.0 * T * shape.TOPK * 3 * shape.I * shape.H
+    out["prefill_routed"] = {"T": T, "us": us, "tflops": flops / (us * 1e-6) / 1e12}
+    return out
+
+
 def b200_arm(args, rank, world, local):
     import mvcc_b200 as m
     dev = torch.device("cuda", local)
@@ -568,11 +692,16 @@ def b200_arm(args, rank, world, local):
     step_us = ms / K * 1e3
     fused = B < 8
     if fused:
-        achieved = ab["block"] / (st[0] * 1e-6) / 1e9
+        # the step is one launch of the fused kernel, so its duration is bounded by the plain graph's step time
+        # (launch gaps included); events inside the graph would defeat the kernel's programmatic dependent launch
+        achieved = ab["block"] / (step_us * 1e-6) / 1e9
         roof = {"kernel": "moe_fused_decode_kernel (the whole block in one cooperative launch)",
                 "bound": "hbm", "achieved": achieved, "peak": peaks["hbm"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm"], "peak_kind": peaks["kind"], "bytes_per_launch": ab["block"],
-                "us_per_launch": st[0], "traffic": NCU_TRAFFIC["fused_b1"] if B == 1 else None}
+                "us_per_launch": step_us, "us_source": "plain graph step time (one launch per step)",
+                "expert_bytes_per_launch": ab["experts"],
+                "expert_frac": ab["experts"] / (step_us * 1e-6) / 1e9 / peaks["hbm"],
+                "traffic": NCU_TRAFFIC["fused_b1"] if B == 1 else None}
     else:
         fl = prefill_flops(shape, B)
         achieved = fl["gate_up"] / (st[1] * 1e-6) / 1e12
@@ -595,22 +724,14 @@ def b200_arm(args, rank, world, local):
         "vs_baseline": None,
         "dtype": DTYPE,
         "data": DATA,
-        "config": {
-            "workload": f"BASELINE config 2: one MoE layer, int4 G=64 experts, decode batch {B}",
-            "H": shape.H, "E": shape.E, "topk": shape.TOPK, "I": shape.I, "Is": shape.Is, "G": shape.G,
-            "batch": B, "layer_copies": args.layer_copies,
-            "l2": f"inputs larger than L2: consecutive steps cycle over {args.layer_copies} layer copies "
-                  f"({args.layer_copies * 0.428:.1f} GB of weights); no flush",
-            "parallelism": f"replicas x{world}" if world > 1 else "single",
-            "graph_steps": min(K, GRAPH_STEPS),
-        },
+        "config": decode_config(shape, B, world, K, args.layer_copies),
         "roofline": roof,
         "expert_gemv": {"bytes_per_step": ab["experts"], "unique_experts": head["U"], "gbs_over_step": exp_gbs,
                         "frac_over_step": exp_gbs / peaks["hbm"],
                         "note": "expert weight + scale bytes over the whole step time (router, shared expert and "
                                 "norms included in the time)"},
         "block": {"bytes_per_step": ab["block"], "gbs": blk_gbs, "frac": blk_gbs / peaks["hbm"], "us": step_us},
-        "kernels_us": {"fused_block": st[0]} if fused else
+        "kernels_us": {"fused_block_events": st[0]} if fused else
                       {"route": st[0], "gate_up": st[1], "down_combine": st[2]},
         "e2e": {"value": world * B * K / (head["ms_e2e"] / 1e3), "unit": "tok/s",
                 "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"]},
@@ -639,13 +760,16 @@ def b200_arm(args, rank, world, local):
     if world == 1 and not args.quick:
         result["pack_load"] = pack_load_case(m, shape)
         torch.cuda.empty_cache()
+        result["g128"] = g128_case(m, stream)
+        torch.cuda.empty_cache()
     if not args.no_prefill:
         do_cpu = world == 1 and rank == 0 and not args.no_cpu
         result["prefill"] = prefill_case(m, shape, args.prefill_steps, W, stream, world, dev, peaks,
                                          args.cpu_seconds / 2, do_cpu)
     if not args.no_ep and world <= 8 and shape.E % world == 0:
         torch.cuda.empty_cache()
-        result["ep_prefill"] = ep_case(m, shape, args.ep_steps, W, stream, world, rank, dev, peaks, args.ep_exchange)
+        result["ep_prefill"] = ep_case(m, shape, args.ep_steps, W, stream, world, rank, dev, peaks, args.ep_exchange,
+                                       parity=not args.no_ep_parity)
     if world == 1 and rank == 0 and not args.no_cpu:
         with torch.cuda.stream(stream):
             l0 = m.synth_layer(shape, seed=1000, stream=stream)
@@ -710,16 +834,132 @@ def cpu_prefill(layer, shape, bias, seconds, tokens=64):
                       f"bias) on one layer, {el:.1f} s, {n} threads ({os.cpu_count()} logical CPUs)"}
 
 
+class _Shape:
+    """The BASELINE config-2 geometry, for the reference arm (which loads nothing of this library)."""
+    H, E, TOPK, I, Is, G, eps = 2048, 256, 8, 512, 512, 64, 1e-6
+
+    def __init__(self, G=64):
+        self.G = G
+
+
+def fast_host_layer(shape, seed):
+    """A layer in the pack layout from numpy's generator: bf16 N(0, 0.02) dense weights and router (so routing is
+    spread as usual), one expert's uniform INT4 nibbles and fp16 group scales near absmax/7 of N(0, 0.02), repeated
+    for every expert. The oracle's cost does not depend on the weight values, so this stands in for the seeded
+    quantised layer, which takes a minute to build on the host."""
+    s = shape
+    rng = np.random.default_rng(seed)
+
+    def bf16(*shp):
+        a = (0.02 * rng.standard_normal(shp, dtype=np.float32)).view(np.uint32)
+        return ((a + 0x7FFF + ((a >> 16) & 1)) >> 16).astype(np.uint16)
+
+    def scales(*shp):
+        return (0.0083 * (1.0 + 0.1 * rng.standard_normal(shp, dtype=np.float32))).astype(np.float16).view(np.uint16)
+
+    def per_expert(a):
+        return np.ascontiguousarray(np.broadcast_to(a, (s.E,) + a.shape))
+
+    return {"rms2": np.full(s.H, 0x3F80, np.uint16), "router": bf16(s.E, s.H),
+            "exp_gu_q": per_expert(rng.integers(0, 256, (2 * s.I, s.H // 2), dtype=np.uint8)),
+            "exp_gu_s": per_expert(scales(2 * s.I, s.H // s.G)),
+            "exp_dn_q": per_expert(rng.integers(0, 256, (s.H, s.I // 2), dtype=np.uint8)),
+            "exp_dn_s": per_expert(scales(s.H, s.I // s.G)),
+            "shared_gate_up": bf16(2 * s.Is, s.H), "shared_down": bf16(s.H, s.Is), "shared_gate": bf16(s.H)}
+
+
+def ref_gpu_case(stream, copies=16, Ts=(1, 4, 8, 16), prefill_T=4096):
+    """The reference's own CUDA kernels on this GPU: examples/qwen/kernels.cuh compiled unchanged for sm_100a into
+    oracle/_ref/libqk_ref.so and launched in qwen.cu's order (oracle/ref/qk_ref_shim.cu). INT4 group 128, the
+    group it hard-codes (kernels.cuh:842). Decode blocks warm -- one layer, the reference's own time_ms method
+    (qwen.cu:486-498) -- and cold (layer copies cycled, weights from HBM); and its moe() (sort + tile GEMMs + slot
+    reduce) for a 4096-token prefill on its own router's routing of N(0,1) activations (qwen.cu:559-566). Weights
+    are random tensors of the pack layout made with torch; the library's `g128` object times the same cases."""
+    import ctypes
+    from oracle import ref_kernels as R
+    if not R.available():
+        return {"unavailable": "oracle/_ref/libqk_ref.so is not built (the reference tree was absent at build time)"}
+    lib = R.lib()
+    lib.qkref_block_forward.restype = ctypes.c_int
+    lib.qkref_moe.restype = ctypes.c_int
+    s = _Shape(G=128)
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(500)
+
+    def bf16(*shp):
+        return (0.02 * torch.randn(*shp, device=dev, generator=gen)).to(torch.bfloat16).view(torch.int16)
+
+    def q(*shp):
+        return torch.randint(0, 256, shp, device=dev, dtype=torch.uint8, generator=gen)
+
+    def sc(*shp):
+        return (0.0083 * (1 + 0.1 * torch.randn(*shp, device=dev, generator=gen))).to(torch.float16).view(torch.int16)
+
+    layers = []
+    for _ in range(copies):
+        layers.append({"rms2": torch.full((s.H,), 0x3F80, dtype=torch.int16, device=dev), "router": bf16(s.E, s.H),
+                       "exp_gu_q": q(s.E, 2 * s.I, s.H // 2), "exp_gu_s": sc(s.E, 2 * s.I, s.H // s.G),
+                       "exp_dn_q": q(s.E, s.H, s.I // 2), "exp_dn_s": sc(s.E, s.H, s.I // s.G),
+                       "shared_gate_up": bf16(2 * s.Is, s.H), "shared_down": bf16(s.H, s.Is),
+                       "shared_gate": bf16(s.H)})
+
+    def vp(t):
+        return ctypes.c_void_p(t.data_ptr())
+
+    def structs(t, T):
+        Tp = (T + 127) // 128 * 128
+        z = {"device": dev}
+        buf = {"logits_r": torch.zeros(Tp, s.E, **z), "topk_i": torch.zeros(Tp, s.TOPK, dtype=torch.int32, **z),
+               "topk_w": torch.zeros(Tp, s.TOPK, **z), "inter": torch.zeros(Tp, s.TOPK, s.I, dtype=torch.int16, **z),
+               "routed": torch.zeros(Tp, s.H, **z), "moe_off": torch.zeros(s.E + 1, dtype=torch.int32, **z),
+               "moe_sorted": torch.zeros(Tp * s.TOPK, dtype=torch.int32, **z),
+               "slot_out": torch.zeros(Tp * s.TOPK, s.H, **z),
+               "sgu": torch.zeros(Tp, 2 * s.Is, dtype=torch.int16, **z),
+               "sinter": torch.zeros(Tp, s.Is, dtype=torch.int16, **z),
+               "sout": torch.zeros(Tp, s.H, dtype=torch.int16, **z)}
+        L = R._Layer(*[vp(t[n]) for n, _ in R._Layer._fields_[:9]], s.H, s.E, s.TOPK, s.I, s.Is, s.eps)
+        W = R._Work(*[vp(buf[n]) for n, _ in R._Work._fields_])
+        return L, W, buf
+
+    st = ctypes.c_void_p(stream.cuda_stream)
+    out = {"group": 128, "layer_copies": copies, "decode_us": {},
+           "how": "reference kernels (kernels.cuh) built unchanged for sm_100a; CUDA graphs of calls, CUDA events"}
+    for T in Ts:
+        Tp = (T + 127) // 128 * 128
+        h = torch.randn(Tp, s.H, device=dev, generator=gen)
+        a = torch.randn(Tp, s.H, device=dev, generator=gen).to(torch.bfloat16).view(torch.int16)
+        normed = torch.zeros(Tp, s.H, dtype=torch.int16, device=dev)
+        refs = [structs(t, T) for t in layers]
+        torch.cuda.synchronize()
+
+        def step(i, cyc):
+            L, W, _ = refs[i % copies if cyc else 0]
+            rc = lib.qkref_block_forward(ctypes.byref(L), ctypes.byref(W), vp(h), vp(a), vp(normed), None, T, st)
+            if rc != 0:
+                raise RuntimeError(f"reference block: cudaError {rc}")
+
+        out["decode_us"][str(T)] = {"warm": time_graph_us(lambda i: step(i, False), 32, stream),
+                                    "cold": time_graph_us(lambda i: step(i, True), 64, stream)}
+        del refs
+    T = prefill_T
+    x = torch.randn(T, s.H, device=dev, generator=gen).to(torch.bfloat16).view(torch.int16)
+    L, W, buf = structs(layers[0], T)
+    with torch.cuda.stream(stream):
+        lib.qkref_dense_f32(vp(x), vp(layers[0]["router"]), vp(buf["logits_r"]), T, s.E, s.H, st)
+        lib.qkref_router_topk(vp(buf["logits_r"]), vp(buf["topk_i"]), vp(buf["topk_w"]), T, s.E, s.TOPK, st)
+    torch.cuda.synchronize()
+    us = time_graph_us(lambda i: lib.qkref_moe(ctypes.byref(L), ctypes.byref(W), vp(x), T, st), 2, stream, reps=3)
+    flops = 2.0 * T * s.TOPK * 3 * s.I * s.H
+    out["prefill_routed"] = {"T": T, "us": us, "tflops": flops / (us * 1e-6) / 1e12}
+    return out
+
+
 def reference_arm(args, rank, world, local):
     if rank != 0:
         return None
-    import mvcc_b200 as m
-    shape = m.MoeShape()
+    shape = _Shape()
     B = args.batch
-    layer = m.synth_layer(shape, seed=1000)
-    torch.cuda.synchronize()
-    L = host_layer(layer)
-    del layer
+    L = fast_host_layer(shape, 1000)
     from oracle import oracle as O
     orc = O.Oracle()
     orc.set_threads(orc.max_threads())
@@ -735,13 +975,12 @@ def reference_arm(args, rank, world, local):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": el / steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": DTYPE, "data": DATA,
-        "config": {"workload": f"BASELINE config 2: one MoE layer, int4 G=64 experts, decode batch {B}",
-                   "H": shape.H, "E": shape.E, "topk": shape.TOPK, "I": shape.I, "Is": shape.Is, "G": shape.G,
-                   "batch": B},
+        "config": decode_config(shape, B, world, args.steps, args.layer_copies),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": n, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference implements the block only as GPU kernels (examples/qwen/kernels.cuh); its CPU "
-                "arm is the oracle's scalar restatement of those kernels",
+                "arm is the oracle's scalar restatement of those kernels; `ref_gpu` times those kernels themselves",
+        "ref_gpu": ref_gpu_case(torch.cuda.Stream()) if torch.cuda.is_available() and not args.no_ref_gpu else None,
     }
 
 
@@ -758,12 +997,14 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
     ap.add_argument("--ep-steps", type=int, default=20)
     ap.add_argument("--no-ep", action="store_true", help="skip the config-5 expert-parallel measurement")
+    ap.add_argument("--no-ep-parity", action="store_true", help="skip the expert-parallel parity check")
     ap.add_argument("--ep-exchange", choices=["peers", "nccl"], default="peers",
                     help="expert-parallel exchange: kernels' peer-memory stores (default) or NCCL all-to-all")
     ap.add_argument("--quick", action="store_true", help="headline batch only (no decode_batches sweep)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--no-ref-gpu", action="store_true", help="reference arm: skip timing the reference's GPU kernels")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

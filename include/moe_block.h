@@ -126,11 +126,16 @@ MOE_API int moe_shared_expert(const moe_layer_weights* w, void* workspace, size_
 
 /* moe_router_topk without a workspace, for callers that cannot allocate device memory: a host runtime that owns all
  * device memory through its own allocator and forbids allocations after start-up has no workspace of ours to pass.
- * No counterpart in the reference. Same outputs as moe_router_topk; its scratch (ticket, error word, unique-expert
- * table: at most 3.6 KiB for E <= 256, TOPK <= 8) lives in a fixed 8 KiB array in the library's device memory,
- * held on every GPU that loads the library until exit; shapes whose scratch would not fit are rejected with
- * cudaErrorInvalidValue. The first call on each device looks up the array's device address (cudaGetSymbolAddress),
- * so make it before any stream capture. All calls share the array: calls that overlap on the GPU race and must be
+ * No counterpart in the reference. It always runs the decode router kernels, in chunks of the decode chunk: below
+ * the prefill threshold its outputs equal moe_router_topk's; at or above it moe_router_topk takes the tensor-core
+ * router, whose fp32 sums run in another order, so logits can differ in the last bits and picks at a near tie of
+ * the 8th and 9th logits can differ. Its scratch (ticket, error word, unique-expert table: at most 3.6 KiB for
+ * E <= 256, TOPK <= 8) lives in a fixed 8 KiB array in the library's device memory, held on every GPU that loads
+ * the library until exit; shapes whose scratch would not fit are rejected with cudaErrorInvalidValue. Each call
+ * looks up the array's device address on the current device (cudaGetSymbolAddress); the first call on a device
+ * loads the library's device code there, so make it before any stream capture. Errors are reported through the
+ * return code only: the scratch error word is not readable by the caller (the router's own top-k never produces the
+ * invalid-expert condition it records). All calls share the array: calls that overlap on the GPU race and must be
  * serialised by the caller. Allocates nothing. */
 MOE_API int moe_router_topk_noalloc(const moe_layer_weights* w, const uint16_t* normed, float* logits, int32_t* idx,
                                     float* wts, int T, moe_stream_t stream);

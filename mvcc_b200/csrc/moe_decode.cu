@@ -194,8 +194,9 @@ __global__ void __launch_bounds__(256) route_kernel(BlockArgs a, int flags) {
   __syncthreads();
   if (tid == 0) {
     __threadfence();
-    // atomicInc wraps to 0 after gridDim.x - 1 arrivals, so the counter needs no reset and recovers by itself
-    // from any stale value within one launch.
+    // atomicInc wraps to 0 after gridDim.x - 1 arrivals, so a counter that starts the launch at zero ends it at
+    // zero. It must start at zero (moe_workspace_init, or the clear in the allocation-free router): a stale value
+    // would shift which CTA sees gridDim.x - 1, and that CTA would not be the last to arrive.
     const unsigned tk = atomicInc(&a.ticket[TICKET_ROUTE], gridDim.x - 1);
     is_last = (tk == gridDim.x - 1);
   }

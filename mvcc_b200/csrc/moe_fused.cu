@@ -323,6 +323,12 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     }
     if (h0 < h1) bulk_g2s(sdn_s, a.w.shared_down + (int64_t)h0 * Is, (h1 - h0) * Is * 2, &sbar);
   }
+  uint2 pre_w[2];  // the norm weights: read only weights, so requested before griddepcontrol.wait
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int i = tid + r * kFThreads;
+    if (i < H / 4) pre_w[r] = reinterpret_cast<const uint2*>(a.w.rms2)[i];
+  }
   cta_sync();
   pdl_wait();
   unsigned long long gb = 0;  // thread 0: the barrier counter at entry, consumed before the first arrival
@@ -366,7 +372,7 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     for (int r = 0; r < 2; ++r) {
       const int i = tid + r * kFThreads;
       if (i < H / 4) {
-        const uint2 wr = reinterpret_cast<const uint2*>(a.w.rms2)[i];
+        const uint2 wr = pre_w[r];
         const uint32_t y0 = f2bf(hv[r].x * inv * lo_bf(wr.x)), y1 = f2bf(hv[r].y * inv * hi_bf(wr.x));
         const uint32_t y2 = f2bf(hv[r].z * inv * lo_bf(wr.y)), y3 = f2bf(hv[r].w * inv * hi_bf(wr.y));
         *reinterpret_cast<float4*>(xs + t * H + xperm(i * 4, nch)) =

@@ -7,13 +7,17 @@
 // device memory instead of a caller-owned workspace. Logits, indices and weights still go to the caller's buffers.
 //
 // The array is a file-scope static __device__ object: every GPU that loads the library holds it (8 KiB) until the
-// process exits. Host code cannot use the array's name as a device address (it is a host-side stand-in), so the
-// first call on each device looks the address up with cudaGetSymbolAddress, with that device current, and caches
-// it; that first call should therefore come before any stream capture. All calls share the array and it keeps the
-// last call's contents; each call clears the ticket and error word before its launches. Calls that overlap on the
+// process exits. Host code cannot use the array's name as a device address (it is a host-side stand-in), so each
+// call looks the address up with cudaGetSymbolAddress on the current device and checks the result; nothing is
+// cached, so a device reset cannot leave a stale address behind. The first call on a device also loads the
+// library's device code there, so it should come before any stream capture. All calls share the array and it keeps
+// the last call's contents; each call clears the ticket and error word before its launches. Calls that overlap on the
 // GPU (concurrent streams, or several host threads) race on the array and must be serialised by the caller.
+//
+// The router always runs the decode kernels (route_kernel: GEMV + the reference's top-k), chunk by chunk, whatever
+// the prefill threshold. The error word it clears is not read back: the caller gets errors through the return code,
+// and the route kernel's own top-k cannot produce the invalid-expert index the word records.
 #include <cstring>
-#include <mutex>
 
 #include "moe_common.cuh"
 #include "moe_decode.h"
@@ -21,7 +25,6 @@
 namespace {
 
 constexpr size_t kScratchBytes = 8192;  // the stated maximum; see moe_router_topk_noalloc
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_router_scratch[kScratchBytes];
 
@@ -43,23 +46,12 @@ ScratchLayout scratch_layout(int E, int pairs) {
   return L;
 }
 
-std::mutex g_mu;
-uint8_t* g_addr[kMaxDevices] = {};
-
-// Device address of g_router_scratch on the current device, looked up once per device.
+// Device address of g_router_scratch on the current device.
 cudaError_t scratch_address(uint8_t** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_router_scratch);
-    if (e != cudaSuccess) return e;
-    g_addr[dev] = static_cast<uint8_t*>(p);
-  }
-  *out = g_addr[dev];
+  *out = static_cast<uint8_t*>(p);
   return cudaSuccess;
 }
 

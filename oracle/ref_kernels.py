@@ -1,5 +1,5 @@
 """ref_kernels.py -- runs the reference's own CUDA kernels (examples/qwen/kernels.cuh, built into
-oracle/_ref/libqk_ref.so by `make -C oracle ref`) on numpy inputs.
+oracle/_ref/libqk_ref.so by `make -C oracle ref REF=<reference checkout>`) on numpy inputs.
 
 TEST INFRASTRUCTURE, NOT PRODUCT CODE: used by the GPU pinning tests and by tests/golden/make_golden.py to
 produce golden vectors from the reference itself. torch provides the device buffers. The reference's limits
@@ -26,8 +26,8 @@ def lib():
     global _lib
     if _lib is None:
         if not available():
-            raise FileNotFoundError(f"{O.REF_LIB_PATH} missing: build with `make -C oracle ref` where the reference "
-                                    "tree is present")
+            raise FileNotFoundError(f"{O.REF_LIB_PATH} missing: build it with "
+                                    "`make -C oracle ref REF=<reference checkout>`")
         _lib = ctypes.CDLL(O.REF_LIB_PATH)
     return _lib
 

@@ -1,6 +1,6 @@
 """Generates the golden vectors in tests/golden/ by running the reference's own CUDA kernels.
 
-    make -C oracle ref                       # where the reference tree is present: builds oracle/_ref/libqk_ref.so
+    make -C oracle ref REF=<reference checkout>   # builds oracle/_ref/libqk_ref.so
     python tests/golden/make_golden.py --out tests/golden   # on a machine with a B200
 
 The reference's MoE block (examples/qwen/kernels.cuh launched in the order of qwen.cu:429-448, through

@@ -1,6 +1,6 @@
 """Writes the .mvccq pack fixtures in tests/golden/ with the reference's own pack writer.
 
-    python tests/golden/make_pack_fixture.py --out tests/golden    # where the reference tree is present
+    python tests/golden/make_pack_fixture.py --reference <reference checkout> --out tests/golden
 
 The reference's converter (examples/qwen/convert.py: `Writer`, `pack_nibbles`, `quant_int8_rows`) writes two tiny
 two-layer packs from the seeded arrays of `entries()` below:
@@ -101,7 +101,7 @@ def _reference_convert(ref_root):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path to the reference checkout (holds examples/qwen)")
     args = ap.parse_args()
     conv = _reference_convert(args.reference)
     manifest = {"seed": SEED, "geometry": GEOM, "files": {}}

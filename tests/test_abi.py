@@ -188,7 +188,8 @@ def build_block_host(out_dir):
 
 
 def test_cpp_block_host_builds(tmp_path):
-    """The C++ driver of the INTEGRATION.md sequence compiles and links; without arguments it prints its usage."""
+    """The C++ driver of the integration sequence (pack -> HBM -> workspace -> forward -> error word) compiles and
+    links; without arguments it prints its usage."""
     import subprocess
     exe = build_block_host(tmp_path)
     run = subprocess.run([exe], capture_output=True, text=True, timeout=60)

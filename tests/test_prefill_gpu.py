@@ -19,6 +19,7 @@ SHAPES = {
     "h512_g32_k4": O.Shape(H=512, E=16, TOPK=4, I=256, Is=256, G=32),
 }
 
+PREFILL_T = 4096
 _cache = {}
 
 
@@ -214,4 +215,52 @@ def test_full_size_prefill_rows_against_oracle(orc, T):
     ok = stable_rows(s, ref["logits"], gpu_logits=gl)
     assert O.max_rel_err(tr["routed"].cpu().numpy()[rows][ok], ref["routed"][ok]) < TOL_INT4
     assert O.max_rel_err(hid.cpu().numpy()[rows][ok], ref["hidden"][ok]) < TOL_BF16
+    assert blk.error_word() == 0
+
+
+def test_config4_zipf_full_geometry_against_oracle(orc):
+    """BASELINE config 4 exactly as benchmarked: H=2048, E=256, top-8, I=Is=512, INT4 G=64, 4096 tokens, router
+    logits plus the Zipf(1.1) per-expert bias, so one expert takes nearly every token. The expert sort (offsets and
+    permutation) is checked whole and bit for bit; every token's outputs are compared with the oracle's tile
+    numerics, all the pairs of the hottest expert included."""
+    m = mb()
+    ms = m.MoeShape()
+    T = PREFILL_T
+    base = m.synth_layer(ms, seed=2000)
+    bias = m.zipf_bias(ms.E, seed=0)
+    t = dict(base.t)
+    t["router_bias"] = torch.from_numpy(bias).cuda()
+    layer = m.MoeLayer(ms, t)
+    hid, att = m.synth_activations(ms, T, 17)
+    torch.cuda.synchronize()
+    hidden = hid.cpu().numpy()
+    attn = att.cpu().numpy().view(np.uint16)
+    blk = m.MoeBlock(layer, T)
+    normed = torch.zeros(T, ms.H, dtype=torch.int16, device="cuda")
+    blk.forward(hid, att, normed)
+    torch.cuda.synchronize()
+    tr = blk.trace(T)
+    gidx = tr["idx"].cpu().numpy()
+    off, srt = orc.sort(gidx, ms.E)
+    assert np.array_equal(tr["offsets"].cpu().numpy(), off)
+    assert np.array_equal(tr["sorted"].cpu().numpy(), srt)
+    load = np.bincount(gidx.ravel(), minlength=ms.E)
+    hot = int(load.argmax())
+    assert load[hot] > T // 2  # the skew the benchmark measures
+    s = O.Shape()
+    L = {n: (v.cpu().numpy() if v.dtype == torch.uint8 else v.cpu().numpy().view(np.uint16))
+         for n, v in base.t.items()}
+    L["router_bias"] = bias
+    del base, t
+    ref = orc.block_forward(s, L, hidden, attn, mode=1)
+    gl = tr["logits"].cpu().numpy()
+    check_routing(orc, s, gl, gidx, tr["wts"].cpu().numpy(), ref["logits"], ref["idx"], ref["wts"], logit_tol=2e-3)
+    ok = stable_rows(s, ref["logits"], gpu_logits=gl)
+    on_hot = (gidx == hot).any(axis=1)
+    assert (ok & on_hot).sum() >= 0.9 * on_hot.sum()
+    assert O.max_rel_err(tr["routed"].cpu().numpy()[ok], ref["routed"][ok]) < TOL_INT4
+    assert O.max_rel_err(tr["routed"].cpu().numpy()[ok & on_hot], ref["routed"][ok & on_hot]) < TOL_INT4
+    assert O.max_rel_err(O.bf16_to_f32(host16(tr["sout"])), O.bf16_to_f32(ref["sout"])) < TOL_BF16
+    assert O.max_rel_err(hid.cpu().numpy()[ok], ref["hidden"][ok]) < TOL_BF16
+    assert O.max_rel_err(O.bf16_to_f32(host16(normed)[ok]), O.bf16_to_f32(ref["normed"][ok])) < TOL_BF16
     assert blk.error_word() == 0

@@ -17,7 +17,8 @@ SHAPE = O.Shape(H=1024, E=32, TOPK=8, I=512, Is=512, G=128)
 def ref():
     from oracle import ref_kernels as R
     if not R.available():
-        pytest.fail("oracle/_ref/libqk_ref.so is missing: build it with `make -C oracle ref` before shipping")
+        pytest.fail("oracle/_ref/libqk_ref.so is missing: build it with "
+                    "`make -C oracle ref REF=<reference checkout>` before shipping")
     return R
 
 
