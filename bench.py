@@ -672,6 +672,44 @@ def g128_case(m, stream, copies=16, Ts=(1, 4, 8, 16), prefill_T=4096):
     return out
 
 
+def decode_stack_case(m, stream, world, peaks, tokens=16, W=3):
+    """a 40-layer decode step at batch 1 -- per layer RMSNorm -> GQA attention (16 q heads, 2 kv
+    heads, head_dim 256, bf16 caches of 4096 tokens ~N(0,1)) -> RMSNorm -> the int4 G=64 MoE block; final RMSNorm and
+    the bf16 LM head of 2048 x 151936 with argmax. The caches hold 4096 positions and every step decodes position
+    4095, so each step reads all 4096 keys. Steps captured in one CUDA graph, CUDA events on the launching stream;
+    every step restores the residual input first (an 8 KB device copy)."""
+    from mvcc_b200 import stack as st
+    stk = st.DecodeStack(L=40, ctx=4096, vocab=151936, seed=5)
+    hidden0, _ = m.synth_activations(stk.moe_shape, 1, seed=41, stream=stream)
+    hidden = hidden0.clone()
+    torch.cuda.synchronize()
+
+    def step(i):
+        hidden.copy_(hidden0)
+        stk.step(hidden, 4095, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(W):
+            step(i)
+    torch.cuda.synchronize()
+    per = counted_launches(m, lambda: step(0))
+    ms, clk = timed(graph_plan(step, tokens, stream), stream, world, ClockSampler(torch.device("cuda")))
+    us = ms / tokens * 1e3
+    nb = stk.weight_bytes()
+    gbs = nb / (us * 1e-6) / 1e9
+    out = {"workload": "BASELINE config 3: 40 x (RMSNorm, GQA attention Hq 16 / Hkv 2 / D 256 over a 4096-token bf16 "
+                       "cache, RMSNorm, int4 G=64 MoE block), final RMSNorm, bf16 LM head 2048 x 151936 + argmax; "
+                       "batch 1",
+           "value": world * 1e6 / us, "unit": "tok/s", "ms_per_token": us / 1e3, "tokens": tokens,
+           "bytes_per_token": nb, "hbm_gbs": gbs, "frac": gbs / peaks["hbm"], "peak_kind": peaks["kind"],
+           "roofline_ms_per_token": nb / (peaks["hbm"] * 1e9) * 1e3,
+           "gpu_launches_per_token": per, "next_token": int(stk.next.item()), "clocks": clk,
+           "how": "mvcc_b200.stack.DecodeStack.step: moe_rmsnorm, 40 x (moe_attn_forward, moe_block_forward with the "
+                  "next layer's norm), moe_lm_head_argmax; one CUDA graph of the token steps"}
+    del stk
+    return out
+
+
 def b200_arm(args, rank, world, local):
     import mvcc_b200 as m
     dev = torch.device("cuda", local)
@@ -761,6 +799,9 @@ def b200_arm(args, rank, world, local):
         result["pack_load"] = pack_load_case(m, shape)
         torch.cuda.empty_cache()
         result["g128"] = g128_case(m, stream)
+        torch.cuda.empty_cache()
+    if not args.quick and not args.no_stack:
+        result["decode_stack"] = decode_stack_case(m, stream, world, peaks)
         torch.cuda.empty_cache()
     if not args.no_prefill:
         do_cpu = world == 1 and rank == 0 and not args.no_cpu
@@ -998,6 +1039,7 @@ def main():
     ap.add_argument("--ep-steps", type=int, default=20)
     ap.add_argument("--no-ep", action="store_true", help="skip the config-5 expert-parallel measurement")
     ap.add_argument("--no-ep-parity", action="store_true", help="skip the expert-parallel parity check")
+    ap.add_argument("--no-stack", action="store_true", help="skip the config-3 40-layer decode-stack measurement")
     ap.add_argument("--ep-exchange", choices=["peers", "nccl"], default="peers",
                     help="expert-parallel exchange: kernels' peer-memory stores (default) or NCCL all-to-all")
     ap.add_argument("--quick", action="store_true", help="headline batch only (no decode_batches sweep)")

@@ -50,6 +50,17 @@ typedef struct moe_layer_weights {
    * logits, indices and weights all carry it. No reference counterpart: it expresses the skewed expert load of
    * the prefill benchmark (router logits plus a per-expert Zipf bias). */
   const float* router_bias;
+  /* Optional (NULL = none): the shared expert as stored by the reference converter's --dense int8 (convert.py:159-169,
+   * 379-385): int8 rows with one fp16 scale per group of shared_group inputs. When present, the single-launch decode
+   * kernel reads these instead of the bf16 matrices (half the bytes) with the reference's int8 GEMV numerics
+   * (gemv_i8_kernel, kernels.cuh:215-274: per 32 inputs an fp32 dot of the raw int8 values, scaled once by its
+   * group's scale); the other paths read the bf16 matrices, which must then hold bf16(q * scale). shared_group is a
+   * multiple of 32 dividing H and Is. */
+  const int8_t* shared_gate_up_q8;   /* i8  [2Is, H] */
+  const uint16_t* shared_gate_up_s8; /* f16 [2Is, H/shared_group] */
+  const int8_t* shared_down_q8;      /* i8  [H, Is] */
+  const uint16_t* shared_down_s8;    /* f16 [H, Is/shared_group] */
+  int32_t shared_group;
 } moe_layer_weights;
 
 /* Shapes the kernels accept: H % 256 == 0 and H <= 4096, I % 128 == 0 and I <= 2048, Is % 128 == 0 and

@@ -21,7 +21,10 @@
  * placed where the bf16 tensors would go. These are the weights the reference's tensor-core int8 GEMM multiplies
  * (gemm_i8_tc_kernel dequantises each K step to the same bf16 values, kernels.cuh:363-400; used for T >= 32,
  * qwen.cu:321-329); its GEMV and small-T paths multiply the fp32 products unrounded (kernels.cuh:215-330), which
- * the bf16 weights match within the bf16 tolerance.
+ * the bf16 weights match within the bf16 tolerance. When both matrices share one group size that is a multiple of
+ * 32, the int8 rows and scales are also handed to the block as stored (moe_layer_weights.shared_*_q8 / _s8 /
+ * shared_group): the single-launch decode kernel then reads the int8 shared expert with the GEMV numerics, half the
+ * bytes of the bf16 copy, and the other paths read the bf16 rows.
  *
  * Errors: every call returns a cudaError_t value as int. A pack that cannot be used (missing tensor, wrong shape or
  * dtype, a blob outside the file) gives cudaErrorInvalidValue (1). The reason is kept as text
@@ -69,11 +72,13 @@ MOE_API int moe_pack_tensor(moe_pack* pack, const char* name, moe_pack_tensor_in
 MOE_API const char* moe_pack_tensor_name(const moe_pack* pack, int i);
 
 /* Layer `layer`'s block weights as HOST pointers, with the pack's geometry (router_bias NULL): every tensor checked
- * for presence, dtype and shape. The pointers lie in the mapping, except an int8 shared expert's, which point to its
- * dequantised bf16 rows held by the pack; all stay valid until moe_pack_close. For host-side checkers. */
+ * for presence, dtype and shape. The pointers lie in the mapping, except an int8 shared expert's bf16 pointers,
+ * which point to its dequantised rows held by the pack (its int8 pointers lie in the mapping); all stay valid until
+ * moe_pack_close. For host-side checkers. */
 MOE_API int moe_pack_layer_host(moe_pack* pack, int layer, moe_layer_weights* w);
-/* Device bytes that moe_pack_upload_layer needs for `layer` (each tensor at a 256-byte aligned offset); 0 if the
- * layer cannot be loaded (the reason in moe_pack_last_error). */
+/* Device bytes that moe_pack_upload_layer needs for `layer` (each tensor at a 256-byte aligned offset, an int8
+ * shared expert's int8 rows and scales after the nine block tensors); 0 if the layer cannot be loaded (the reason
+ * in moe_pack_last_error). */
 MOE_API size_t moe_pack_layer_bytes(moe_pack* pack, int layer);
 /* Copies layer `layer`'s block tensors into `dev` (device memory, 256-byte aligned, dev_bytes >=
  * moe_pack_layer_bytes) with one host-to-device copy per tensor on `stream`, and fills `w` with device pointers

@@ -42,7 +42,20 @@ class MoeLayerWeights(ctypes.Structure):
         ("G", ctypes.c_int32),
         ("eps", ctypes.c_float),
         ("router_bias", ctypes.c_void_p),
+        ("shared_gate_up_q8", ctypes.c_void_p),
+        ("shared_gate_up_s8", ctypes.c_void_p),
+        ("shared_down_q8", ctypes.c_void_p),
+        ("shared_down_s8", ctypes.c_void_p),
+        ("shared_group", ctypes.c_int32),
     ]
+
+
+class MoeAttnWeights(ctypes.Structure):
+    """ctypes mirror of `moe_attn_weights` (include/moe_stack.h)."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n in ("qkv", "gate", "o", "q_norm", "k_norm")] + \
+               [(n, ctypes.c_int32) for n in ("H", "Hq", "Hkv", "D", "rope_dim")] + \
+               [("theta", ctypes.c_float), ("eps", ctypes.c_float)]
 
 
 class MoeTrace(ctypes.Structure):
@@ -97,6 +110,12 @@ _SIGS = {
     "moe_ipc_handle": (_I, [_P, _P]),
     "moe_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
     "moe_ipc_close": (_I, [_P]),
+    # attention layer, first-layer norm and LM head of a decode step (include/moe_stack.h)
+    "moe_attn_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeAttnWeights), _I, _I]),
+    "moe_attn_forward": (_I, [ctypes.POINTER(MoeAttnWeights), _P, _P, _I, _I, _P, _P, _I, _P, ctypes.c_size_t, _P]),
+    "moe_rmsnorm": (_I, [_P, _P, _P, _I, _I, ctypes.c_float, _P]),
+    "moe_lm_head_workspace_bytes": (ctypes.c_size_t, [_I, _I]),
+    "moe_lm_head_argmax": (_I, [_P, _P, _I, _I, _P, _P, _P, ctypes.c_size_t, _P]),
     # weight pack reader (include/moe_pack.h); the structures are declared in mvcc_b200/pack.py
     "moe_pack_open": (_P, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
     "moe_pack_close": (None, [_P]),
@@ -193,6 +212,7 @@ class MoeLayer:
 
     NAMES = ("rms2", "router", "exp_gu_q", "exp_gu_s", "exp_dn_q", "exp_dn_s", "shared_gate_up", "shared_down",
              "shared_gate")
+    INT8_NAMES = ("shared_gate_up_q8", "shared_gate_up_s8", "shared_down_q8", "shared_down_s8")
 
     def __init__(self, shape: MoeShape, tensors: dict):
         self.shape = shape
@@ -218,6 +238,26 @@ class MoeLayer:
         self.c = MoeLayerWeights(*[ctypes.c_void_p(self.t[n].data_ptr()) for n in self.NAMES],
                                  s.H, s.E, s.TOPK, s.I, s.Is, s.G, s.eps,
                                  None if bias is None else ctypes.c_void_p(bias.data_ptr()))
+        # optional int8 shared expert (--dense int8 packs): int8 rows and fp16 group scales as stored
+        i8 = [self.t.get(n) for n in self.INT8_NAMES]
+        if any(v is not None for v in i8):
+            gq, gs, dq, ds = i8
+            if any(v is None for v in i8):
+                raise ValueError("int8 shared expert: all of " + ", ".join(self.INT8_NAMES) + " are needed")
+            g8 = s.H // gs.shape[1] if gs.dim() == 2 and gs.shape[1] else 0
+            want = {"shared_gate_up_q8": ((2 * s.Is, s.H), torch.int8),
+                    "shared_gate_up_s8": ((2 * s.Is, s.H // max(g8, 1)), torch.int16),
+                    "shared_down_q8": ((s.H, s.Is), torch.int8),
+                    "shared_down_s8": ((s.H, s.Is // max(g8, 1)), torch.int16)}
+            for n, (shp, dt) in want.items():
+                v = self.t[n]
+                if tuple(v.shape) != shp or v.dtype != dt or not v.is_contiguous() or not v.is_cuda:
+                    raise ValueError(f"{n}: expected contiguous cuda {dt} {shp}, got {v.dtype} {tuple(v.shape)}")
+            self.c.shared_gate_up_q8 = gq.data_ptr()
+            self.c.shared_gate_up_s8 = gs.data_ptr()
+            self.c.shared_down_q8 = dq.data_ptr()
+            self.c.shared_down_s8 = ds.data_ptr()
+            self.c.shared_group = g8
         _check(_lib.moe_check_shape(ctypes.byref(self.c)), "moe_check_shape")
 
 

@@ -47,6 +47,14 @@ bool shape_ok(const moe_layer_weights* w) {
   if (H % G || I % G) return false;
   if (K > 8 || E > 256 || K > E) return false;
   if (H > 4096 || I > 2048 || Is > 2048) return false;
+  // the optional int8 shared expert: all four arrays, one group size (a multiple of 32) dividing H and Is
+  const int n8 = (w->shared_gate_up_q8 != nullptr) + (w->shared_gate_up_s8 != nullptr) +
+                 (w->shared_down_q8 != nullptr) + (w->shared_down_s8 != nullptr);
+  if (n8 != 0 && n8 != 4) return false;
+  if (n8 == 4) {
+    const int g8 = w->shared_group;
+    if (g8 <= 0 || g8 % 32 || H % g8 || Is % g8) return false;
+  }
   return true;
 }
 

@@ -256,6 +256,17 @@ __device__ __forceinline__ void fused_gate_job2(const BlockArgs& a, const float*
   }
 }
 
+// d += sum over the 4 signed bytes of w (k ascending) of byte * x[i], as gemv_i8_kernel's char4 loop
+// (kernels.cuh:250-256) accumulates one 32-input chunk.
+__device__ __forceinline__ float i8x4_dot(uint32_t w, const float* x, float d) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d = fmaf((float)((int32_t)(w << (24 - 8 * i)) >> 24), x[i], d);
+  return d;
+}
+
+// Shared-memory slot of a 16-byte aligned superset of `rows` scale rows of `bytes` each.
+__host__ __device__ inline int scale_slot(int rows, int bytes) { return a16(rows * bytes) + 16; }
+
 // Chunk list entry: kind 0 = gate/up jobs i0 .. i0 + n - 1 of unique expert a; kind 1 = down rows of unique experts
 // a .. a + n - 1.
 struct Chunk {
@@ -294,6 +305,14 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
   const int nrows = E + 1;
   const uint8_t* gscale = reinterpret_cast<const uint8_t*>(a.w.exp_gu_s);
   const uint8_t* dscale = reinterpret_cast<const uint8_t*>(a.w.exp_dn_s);
+  // int8 shared expert (optional): rows, scales, scale bytes per row of gate/up and down, 32-input chunks per group
+  const bool sh8 = a.w.shared_gate_up_q8 != nullptr;
+  const uint8_t* q8g = reinterpret_cast<const uint8_t*>(a.w.shared_gate_up_q8);
+  const uint8_t* s8g = reinterpret_cast<const uint8_t*>(a.w.shared_gate_up_s8);
+  const uint8_t* q8d = reinterpret_cast<const uint8_t*>(a.w.shared_down_q8);
+  const uint8_t* s8d = reinterpret_cast<const uint8_t*>(a.w.shared_down_s8);
+  const int g8 = sh8 ? a.w.shared_group : 32;
+  const int sgs8 = (H / g8) * 2, dss8 = (Is / g8) * 2, cshift8 = __ffs(g8) - 6;
 
   // Entry: barriers and the routing-independent weight copies touch only this CTA's shared memory and read only
   // weights, so under programmatic dependent launch they overlap the previous kernel's tail; everything after
@@ -316,12 +335,35 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     if (r1 > re) bulk_g2s(router_s + (size_t)(re - r0) * H * 2, a.w.shared_gate, H * 2, &rbar);
     // shared-expert pairs [j0, j1): gate rows j0 .. j1 - 1 and up rows Is + j0 .. Is + j1 - 1, one copy each
     const int j0 = min(Is, kSgu * cta), j1 = min(Is, j0 + kSgu);
-    expect_tx(&sbar, (uint32_t)(2 * (j1 - j0) * H * 2 + (h0 < h1 ? (h1 - h0) * Is * 2 : 0)));
-    if (j1 > j0) {
-      bulk_g2s(sgu_s, a.w.shared_gate_up + (int64_t)j0 * H, (j1 - j0) * H * 2, &sbar);
-      bulk_g2s(sgu_s + (size_t)kSgu * H * 2, a.w.shared_gate_up + (int64_t)(Is + j0) * H, (j1 - j0) * H * 2, &sbar);
+    if (sh8) {
+      // int8 shared expert: gate q rows [kSgu][H], up q rows [kSgu][H], then their scale rows (aligned supersets);
+      // down q rows [rpc][Is], then their scale rows
+      uint32_t tx = 0;
+      if (j1 > j0)
+        tx += 2 * (j1 - j0) * H + span_bytes(s8g + (int64_t)j0 * sgs8, (j1 - j0) * sgs8) +
+              span_bytes(s8g + (int64_t)(Is + j0) * sgs8, (j1 - j0) * sgs8);
+      if (h0 < h1) tx += (h1 - h0) * Is + span_bytes(s8d + (int64_t)h0 * dss8, (h1 - h0) * dss8);
+      expect_tx(&sbar, tx);
+      if (j1 > j0) {
+        bulk_g2s(sgu_s, q8g + (int64_t)j0 * H, (j1 - j0) * H, &sbar);
+        bulk_g2s(sgu_s + (size_t)kSgu * H, q8g + (int64_t)(Is + j0) * H, (j1 - j0) * H, &sbar);
+        bulk_span(sgu_s + (size_t)2 * kSgu * H, s8g + (int64_t)j0 * sgs8, (j1 - j0) * sgs8, &sbar);
+        bulk_span(sgu_s + (size_t)2 * kSgu * H + scale_slot(kSgu, sgs8), s8g + (int64_t)(Is + j0) * sgs8,
+                  (j1 - j0) * sgs8, &sbar);
+      }
+      if (h0 < h1) {
+        bulk_g2s(sdn_s, q8d + (int64_t)h0 * Is, (h1 - h0) * Is, &sbar);
+        bulk_span(sdn_s + (size_t)rpc * Is, s8d + (int64_t)h0 * dss8, (h1 - h0) * dss8, &sbar);
+      }
+    } else {
+      expect_tx(&sbar, (uint32_t)(2 * (j1 - j0) * H * 2 + (h0 < h1 ? (h1 - h0) * Is * 2 : 0)));
+      if (j1 > j0) {
+        bulk_g2s(sgu_s, a.w.shared_gate_up + (int64_t)j0 * H, (j1 - j0) * H * 2, &sbar);
+        bulk_g2s(sgu_s + (size_t)kSgu * H * 2, a.w.shared_gate_up + (int64_t)(Is + j0) * H, (j1 - j0) * H * 2,
+                 &sbar);
+      }
+      if (h0 < h1) bulk_g2s(sdn_s, a.w.shared_down + (int64_t)h0 * Is, (h1 - h0) * Is * 2, &sbar);
     }
-    if (h0 < h1) bulk_g2s(sdn_s, a.w.shared_down + (int64_t)h0 * Is, (h1 - h0) * Is * 2, &sbar);
   }
   uint2 pre_w[2];  // the norm weights: read only weights, so requested before griddepcontrol.wait
 #pragma unroll
@@ -429,6 +471,44 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
         if (lane == 0) {
           atomicOr(a.err, (uint32_t)MOE_ERR_BARRIER);
           abort_s = 1;
+        }
+      } else if (sh8) {
+        // gemv_i8_kernel's numerics: per 32-input chunk an fp32 dot of the raw int8 values, scaled once by the
+        // chunk's group scale
+        const uint8_t* grow = sgu_s + (size_t)r * H;
+        const uint8_t* urow = sgu_s + (size_t)(kSgu + r) * H;
+        const uint16_t* gsc = reinterpret_cast<const uint16_t*>(sgu_s + (size_t)2 * kSgu * H +
+                                                                span_delta(s8g + (int64_t)(kSgu * cta) * sgs8) + r * sgs8);
+        const uint16_t* usc = reinterpret_cast<const uint16_t*>(
+            sgu_s + (size_t)2 * kSgu * H + scale_slot(kSgu, sgs8) + span_delta(s8g + (int64_t)(Is + kSgu * cta) * sgs8) +
+            r * sgs8);
+        for (int t = 0; t < T; ++t) {
+          const float4* xs4 = reinterpret_cast<const float4*>(xs + t * H);
+          float g = 0.f, u = 0.f;
+          for (int c = lane; c < nch; c += 32) {
+            const uint4 ga = *reinterpret_cast<const uint4*>(grow + c * 32);
+            const uint4 gb = *reinterpret_cast<const uint4*>(grow + c * 32 + 16);
+            const uint4 ua = *reinterpret_cast<const uint4*>(urow + c * 32);
+            const uint4 ub = *reinterpret_cast<const uint4*>(urow + c * 32 + 16);
+            const uint32_t gw[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+            const uint32_t uw[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+            float dg = 0.f, du = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float x[8];
+              x_word(xs4, nch, c, q, x);
+              dg = i8x4_dot(gw[2 * q], x, dg);
+              dg = i8x4_dot(gw[2 * q + 1], x + 4, dg);
+              du = i8x4_dot(uw[2 * q], x, du);
+              du = i8x4_dot(uw[2 * q + 1], x + 4, du);
+            }
+            g = fmaf(dg, h2f(gsc[c >> cshift8]), g);
+            u = fmaf(du, h2f(usc[c >> cshift8]), u);
+          }
+          g = warp_sum(g);
+          u = warp_sum(u);
+          if (lane == 0) a.sinter[(int64_t)t * Is + j] = f2bf(silu(bf2f(f2bf(g))) * bf2f(f2bf(u)));
+          __syncwarp();
         }
       } else {
         const uint8_t* grow = sgu_s + (size_t)r * H * 2;
@@ -693,8 +773,31 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
       const float v = warp_sum(acc_w[t * 32 + lane]);
       if (lane == t) routed_t = v;
     }
-    const uint8_t* srow = sdn_s + (size_t)(hw - h0) * Is * 2;
-    for (int t = 0; t < T; ++t) {
+    const uint8_t* srow = sdn_s + (size_t)(hw - h0) * Is * (sh8 ? 1 : 2);
+    const uint16_t* dsc8 = reinterpret_cast<const uint16_t*>(sdn_s + (size_t)rpc * Is +
+                                                             span_delta(s8d + (int64_t)h0 * dss8) + (hw - h0) * dss8);
+    for (int t = 0; t < T && sh8; ++t) {
+      // gemv_i8_kernel over the Is shared intermediates: lane l takes inputs 32 l .. 32 l + 31 of each 1024
+      float acc = 0.f;
+      for (int k0 = lane * 32; k0 < Is; k0 += 1024) {
+        const uint4 wa = *reinterpret_cast<const uint4*>(srow + k0);
+        const uint4 wb = *reinterpret_cast<const uint4*>(srow + k0 + 16);
+        const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        float d = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(sinter_s + t * Is + k0 + q * 8);
+          const float x[8] = {lo_bf(xv.x), hi_bf(xv.x), lo_bf(xv.y), hi_bf(xv.y),
+                              lo_bf(xv.z), hi_bf(xv.z), lo_bf(xv.w), hi_bf(xv.w)};
+          d = i8x4_dot(ww[2 * q], x, d);
+          d = i8x4_dot(ww[2 * q + 1], x + 4, d);
+        }
+        acc = fmaf(d, h2f(dsc8[k0 / g8]), acc);
+      }
+      const float v = bf2f(f2bf(warp_sum(acc)));
+      if (lane == t) shared_t = v;
+    }
+    for (int t = 0; t < T && !sh8; ++t) {
       float acc = 0.f;
       for (int v = lane; v < nvs; v += 32) {
         const uint4 wv = *reinterpret_cast<const uint4*>(srow + v * 16);
@@ -802,6 +905,11 @@ static bool fused_plan(const moe_layer_weights& w, int T, FusedCfg* out) {
       !aligned16(w.shared_down) || !aligned16(w.exp_gu_q) || !aligned16(w.exp_dn_q) || !aligned16(w.exp_gu_s) ||
       !aligned16(w.exp_dn_s))
     return false;
+  if (w.shared_gate_up_q8) {  // int8 shared expert: rows copied whole, scales as aligned supersets
+    if (!aligned16(w.shared_gate_up_q8) || !aligned16(w.shared_down_q8) || w.shared_group % 32 != 0 ||
+        w.shared_group <= 0 || w.H % w.shared_group != 0 || w.Is % w.shared_group != 0)
+      return false;
+  }
   const int rpc = (w.H + grid - 1) / grid;
   if (rpc > kFW) return false;  // one output row per warp
   // gate/up jobs per chunk: two per warp at the smallest batches (their activation loads are shared), else one

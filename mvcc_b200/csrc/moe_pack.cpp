@@ -460,6 +460,16 @@ void dequant_i8_rows(const int8_t* q, const uint16_t* sc, int64_t rows, int64_t 
     }
 }
 
+// Whether the shared expert of a --dense int8 pack can also be handed to the block as int8 (both matrices stored as
+// q8 + s8 with one group size, a multiple of 32); its group size in *group. False for a bf16 pack.
+bool int8_shared(const Src src[kBlockTensors], int64_t* group) {
+  const Src& gu = src[6];
+  const Src& dn = src[7];
+  if (!gu.q8 || !dn.q8 || gu.group != dn.group || gu.group % 32 || gu.group <= 0) return false;
+  *group = gu.group;
+  return true;
+}
+
 void fill_weights(const moe_pack_geometry& g, const void* const ptr[kBlockTensors], moe_layer_weights* w) {
   memset(w, 0, sizeof *w);
   w->rms2 = static_cast<const uint16_t*>(ptr[0]);
@@ -599,6 +609,14 @@ int moe_pack_layer_host(moe_pack* pk, int layer, moe_layer_weights* w) {
   const void* ptr[kBlockTensors];
   for (int i = 0; i < kBlockTensors; ++i) ptr[i] = host_block_bytes(pk, layer, i, src[i]);
   fill_weights(pk->geo, ptr, w);
+  int64_t g8 = 0;
+  if (int8_shared(src, &g8)) {  // the int8 rows and scales as stored, in the mapping
+    w->shared_gate_up_q8 = reinterpret_cast<const int8_t*>(pk->bytes() + src[6].q8->off);
+    w->shared_gate_up_s8 = reinterpret_cast<const uint16_t*>(pk->bytes() + src[6].s8->off);
+    w->shared_down_q8 = reinterpret_cast<const int8_t*>(pk->bytes() + src[7].q8->off);
+    w->shared_down_s8 = reinterpret_cast<const uint16_t*>(pk->bytes() + src[7].s8->off);
+    w->shared_group = (int32_t)g8;
+  }
   return 0;
 }
 
@@ -609,6 +627,9 @@ size_t moe_pack_layer_bytes(moe_pack* pk, int layer) {
   if (find_block(pk, layer, src)) return 0;
   size_t total = 0;
   for (int i = 0; i < kBlockTensors; ++i) total += align_up((size_t)src[i].nbytes());
+  int64_t g8 = 0;
+  if (int8_shared(src, &g8))
+    for (int i = 6; i <= 7; ++i) total += align_up(src[i].q8->nbytes) + align_up(src[i].s8->nbytes);
   return total;
 }
 
@@ -620,6 +641,10 @@ int moe_pack_upload_layer(moe_pack* pk, int layer, void* dev, size_t dev_bytes, 
   if (int rc = find_block(pk, layer, src)) return rc;
   size_t need = 0;
   for (int i = 0; i < kBlockTensors; ++i) need += align_up((size_t)src[i].nbytes());
+  int64_t g8 = 0;
+  const bool i8 = int8_shared(src, &g8);
+  if (i8)
+    for (int i = 6; i <= 7; ++i) need += align_up(src[i].q8->nbytes) + align_up(src[i].s8->nbytes);
   if (!dev || reinterpret_cast<uintptr_t>(dev) % kDevAlign)
     return pk->set_err(kInvalid, "device region must be %zu-byte aligned", kDevAlign);
   if (dev_bytes < need) return pk->set_err(kInvalid, "device region holds %zu bytes, layer needs %zu", dev_bytes, need);
@@ -640,6 +665,26 @@ int moe_pack_upload_layer(moe_pack* pk, int layer, void* dev, size_t dev_bytes, 
     moe::note_pack_bytes(n);
   }
   fill_weights(pk->geo, ptr, w);
+  if (i8) {
+    // the int8 shared expert as stored (its bf16 rows above serve the paths that read bf16): q8 then s8 of gate_up,
+    // then of down, each 256-byte aligned after the nine block tensors
+    const void* dst8[4];
+    const Entry* e8[4] = {src[6].q8, src[6].s8, src[7].q8, src[7].s8};
+    for (int j = 0; j < 4; ++j) {
+      uint8_t* dst = static_cast<uint8_t*>(dev) + at;
+      const cudaError_t e =
+          cudaMemcpyAsync(dst, pk->bytes() + e8[j]->off, e8[j]->nbytes, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+      if (e != cudaSuccess) return pk->set_err((int)e, "host-to-device copy failed: %s", cudaGetErrorString(e));
+      dst8[j] = dst;
+      at += align_up(e8[j]->nbytes);
+      moe::note_pack_bytes(e8[j]->nbytes);
+    }
+    w->shared_gate_up_q8 = static_cast<const int8_t*>(dst8[0]);
+    w->shared_gate_up_s8 = static_cast<const uint16_t*>(dst8[1]);
+    w->shared_down_q8 = static_cast<const int8_t*>(dst8[2]);
+    w->shared_down_s8 = static_cast<const uint16_t*>(dst8[3]);
+    w->shared_group = (int32_t)g8;
+  }
   return 0;
 }
 

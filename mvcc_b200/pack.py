@@ -150,6 +150,15 @@ class MoePack:
             off = getattr(w, field) - base
             n = int(np.prod(shape)) * np.dtype(_NUMPY[dt]).itemsize
             t[field] = buf[off:off + n].view(_TORCH[dt]).view(shape)
+        if w.shared_gate_up_q8:  # the int8 shared expert as stored, beside its bf16 rows
+            s, g8 = self.shape, w.shared_group
+            for field, shape, dtype in (("shared_gate_up_q8", (2 * s.Is, s.H), torch.int8),
+                                        ("shared_gate_up_s8", (2 * s.Is, s.H // g8), torch.int16),
+                                        ("shared_down_q8", (s.H, s.Is), torch.int8),
+                                        ("shared_down_s8", (s.H, s.Is // g8), torch.int16)):
+                off = getattr(w, field) - base
+                n = int(np.prod(shape)) * torch.empty((), dtype=dtype).element_size()
+                t[field] = buf[off:off + n].view(dtype).view(shape)
         ml = MoeLayer(self.shape, t)
         ml.storage = buf  # the tensors are views of this buffer
         return ml

@@ -122,6 +122,32 @@ def make_layer(shape, seed, std=0.02, exact=False):
     return {k: np.ascontiguousarray(v) for k, v in L.items()}
 
 
+def gemv_i8(x_bits, q8, s8):
+    """gemv_i8_kernel (kernels.cuh:215-274): y[t, n] = sum over 32-input chunks c of s8[n, c * 32 / group] times the
+    chunk's dot of the raw int8 row values with x (bf16 bits); float64 here, so the kernel's fp32 summation order is
+    matched within tolerance. q8 int8 [N, K], s8 fp16 [N, K / group]."""
+    x = bf16_to_f32(np.asarray(x_bits, np.uint16)).astype(np.float64)
+    q = np.asarray(q8, np.int8).astype(np.float64)
+    sc = np.asarray(s8).view(np.float16).astype(np.float64)
+    N, K = q.shape
+    group = K // sc.shape[1]
+    chunks = (x[:, None, :] * q[None, :, :]).reshape(x.shape[0], N, K // 32, 32).sum(axis=3)
+    return (chunks * np.repeat(sc, group // 32, axis=1)[None, :, :]).sum(axis=2)
+
+
+def shared_i8(shape, q8_gu, s8_gu, q8_dn, s8_dn, normed):
+    """The shared expert on int8 weights with the reference's GEMV numerics (qwen.cu:436-438 with --dense int8): sgu
+    = bf16(gemv_i8(normed)), sinter = bf16(silu(g) * u), sout = bf16(gemv_i8(sinter)). Returns (sinter, sout) bf16
+    bits."""
+    s = shape
+    sgu = f32_to_bf16(gemv_i8(normed, q8_gu, s8_gu).astype(np.float32))
+    g = bf16_to_f32(sgu[:, :s.Is]).astype(np.float64)
+    u = bf16_to_f32(sgu[:, s.Is:]).astype(np.float64)
+    sinter = f32_to_bf16((g / (1.0 + np.exp(-g)) * u).astype(np.float32))
+    sout = f32_to_bf16(gemv_i8(sinter, q8_dn, s8_dn).astype(np.float32))
+    return sinter, sout
+
+
 def make_activations(shape, T, seed, exact=False):
     """hidden fp32 [T,H] and attn_out bf16 [T,H], seeded (N(0,1), or small exact values)."""
     if exact:

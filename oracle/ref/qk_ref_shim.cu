@@ -3,13 +3,15 @@
 // TEST INFRASTRUCTURE, NOT PRODUCT CODE. oracle/Makefile compiles this file against the reference sources where
 // they lie (-I <reference>/examples/qwen, and an include dir whose only entry is a symlink to
 // <reference>/include/mvcc), into oracle/_ref/libqk_ref.so. Tests and tests/golden/make_golden.py use it to run
-// the reference's kernels on a B200 and pin the CPU oracle to their outputs; oracle/ref_gpu_bench.py times them.
+// the reference's kernels on a B200 and pin the CPU oracle to their outputs; bench.py's reference arm times them.
 // Nothing here is shipped or called by the product path.
 //
 // The launch sequences restate the reference host code, which is static in qwen.cu and cannot be linked:
 //   ref_dense_*        dense() dispatch, qwen.cu:298-319 (bf16 weights only)
 //   ref_moe            moe(), qwen.cu:345-363, with the default QWEN_MOE_TK=32, QWEN_MOE_NB=128 (qwen.cu:27-33)
 //   ref_block_forward  the MoE block of forward(), qwen.cu:429-448
+//   ref_attn_forward   the attention branch of forward(), qwen.cu:413-425, with attention() of qwen.cu:52-64
+//   ref_lm_head        the final norm, dense() and two-stage argmax of forward(), qwen.cu:451-456
 // Buffers follow Work::alloc (qwen.cu:258-292): activation buffers read by the tensor-core GEMMs hold
 // round_up(T, 128) rows (qwen.cu:259).
 #include <cuda_runtime.h>
@@ -135,6 +137,40 @@ int qkref_block_forward(const qkref_layer* l, qkref_work* w, float* hidden, cons
                                                              next_rms1, normed, H, l->eps);
   else
     qk::shared_gate_combine_kernel<<<T, 256, 0, s>>>(hidden, w->routed, w->sout, normed, l->shared_gate, H);
+  return (int)cudaGetLastError();
+}
+
+// The attention branch of forward() (qwen.cu:413-425) for T tokens at pos0. Buffers: qkv [T, (Hq + 2 Hkv) D],
+// z [T, Hq D] (if gate), q [T, Hq, D], o [T, Hq D], part [T Hq 32][D + 2] (kMaxSplit = 32), caches [Hkv][ctx][D].
+int qkref_attn_forward(const uint16_t* normed, const uint16_t* Wqkv, const uint16_t* Wgate, const uint16_t* Wo,
+                       const uint16_t* q_norm, const uint16_t* k_norm, uint16_t* kc, uint16_t* vc, uint16_t* qkv,
+                       uint16_t* z, uint16_t* q, uint16_t* o, float* part, uint16_t* attn_out, int T, int H, int Hq,
+                       int Hkv, int D, int rope_dim, float theta, int pos0, int ctx, float eps, cudaStream_t s) {
+  const int heads = Hq + 2 * Hkv;
+  dense<qk::bf16>(normed, Wqkv, qkv, T, heads * D, H, s);
+  if (Wgate) dense<qk::bf16>(normed, Wgate, z, T, Hq * D, H, s);
+  qk::attn_qk_norm_rope_kernel<<<cdiv(T * heads, 8), 256, 0, s>>>(qkv, q_norm, k_norm, q, kc, vc, T, Hq, Hkv, D,
+                                                                  rope_dim, theta, pos0, ctx, eps);
+  // attention(), qwen.cu:52-64
+  const int blocks = T * Hkv, jobs = T * Hq, nkeys = pos0 + T;
+  const int nsplit = std::max(1, std::min({32, cdiv(nkeys, 32), cdiv(64, blocks)}));
+  qk::attn_partial_kernel<256><<<dim3(blocks, nsplit), 256, 0, s>>>(q, kc, vc, part, T, Hq, Hkv, ctx, pos0, nsplit,
+                                                                    1.f / sqrtf((float)D));
+  qk::attn_combine_kernel<256><<<cdiv(jobs, 8), 256, 0, s>>>(part, o, jobs, nsplit);
+  if (Wgate)
+    qk::sigmoid_gate_kernel<<<std::min(cdiv((int64_t)T * Hq * D, 256), 4096), 256, 0, s>>>(o, z, (int64_t)T * Hq * D);
+  dense<qk::bf16>(o, Wo, attn_out, T, H, Hq * D, s);
+  return (int)cudaGetLastError();
+}
+
+// The LM head of forward() (qwen.cu:451-456) for the last token's fp32 residual: final RMSNorm, logits (fp32 [V]),
+// argmax. Buffers: normed [H] bf16, pmax / pidx [1024].
+int qkref_lm_head(const float* hidden_last, const uint16_t* final_norm, const uint16_t* lm_head, uint16_t* normed,
+                  float* logits, float* pmax, int32_t* pidx, int32_t* next, int V, int H, float eps, cudaStream_t s) {
+  qk::rmsnorm_kernel<<<1, 256, 0, s>>>(hidden_last, final_norm, normed, H, eps);
+  dense<float>(normed, lm_head, logits, 1, V, H, s);
+  qk::argmax_partial_kernel<<<1024, 256, 0, s>>>(logits, V, pmax, pidx);
+  qk::argmax_final_kernel<<<1, 256, 0, s>>>(pmax, pidx, 1024, next);
   return (int)cudaGetLastError();
 }
 

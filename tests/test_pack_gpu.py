@@ -81,3 +81,38 @@ def test_upload_into_a_short_region_fails_cleanly(tmp_path):
                                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         assert rc == 1
         assert w.router is None  # nothing filled in
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_decode_reads_the_int8_shared_expert(tmp_path, orc, T):
+    """An int8 pack (group 128, the reference converter's --dense int8) on the single-launch decode kernel: its shared
+    expert comes from the int8 rows with gemv_i8_kernel's numerics, half the bytes of the bf16 copy. To show which copy
+    is read, the bf16 copy on the device is zeroed first: sout must still match the oracle's int8 GEMV numerics
+    (bf16 bar 1e-2) and the block's output the oracle block on the dequantised weights."""
+    import mvcc_b200 as m
+    from mvcc_b200 import pack
+    s = O.Shape(H=1024, E=32, TOPK=8, I=512, Is=512, G=64)
+    path, layers = _write(tmp_path, s, (31, 32), 128)
+    with pack.MoePack(path) as pk:
+        layer = pk.layer(1)
+        q8g, s8g = pk.tensor("L1.shared.gate_up.q8"), pk.tensor("L1.shared.gate_up.s8")
+        q8d, s8d = pk.tensor("L1.shared.down.q8"), pk.tensor("L1.shared.down.s8")
+    assert layer.c.shared_gate_up_q8 and layer.c.shared_group == 128
+    layer.t["shared_gate_up"].zero_()
+    layer.t["shared_down"].zero_()
+    hidden, attn = O.make_activations(s, T, 90 + T)
+    blk = m.MoeBlock(layer, T)
+    h = torch.from_numpy(hidden.copy()).cuda()
+    n = torch.zeros(T, s.H, dtype=torch.int16, device="cuda")
+    blk.forward(h, torch.from_numpy(attn.view(np.int16)).cuda(), n)
+    torch.cuda.synchronize()
+    tr = blk.trace(T)
+    ref = orc.block_forward(s, layers[1], hidden, attn, mode=0)
+    _, sout8 = O.shared_i8(s, q8g, s8g, q8d, s8d, ref["normed"])
+    gs = tr["sout"].cpu().numpy().view(np.uint16)
+    assert O.max_rel_err(O.bf16_to_f32(gs), O.bf16_to_f32(sout8)) < TOL_BF16
+    gl = tr["logits"].cpu().numpy()
+    margin = parity.topk_margin(ref["logits"], s.TOPK)
+    ok = parity.keep_stable(margin > 2 * np.abs(gl - ref["logits"]).max(axis=1) + 1e-6, margin)
+    assert O.max_rel_err(h.cpu().numpy()[ok], ref["hidden"][ok]) < TOL_BF16
+    assert blk.error_word() == 0
