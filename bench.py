@@ -465,6 +465,7 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers", p
         ms, clk = timed(graph_plan(step, K, stream), stream, world, ClockSampler(dev))
         how = "single GPU: moe_block_forward prefill path (CUDA graph)"
         recv = None
+        stages = None
         hidden.copy_(hidden0)
         step(0)
         torch.cuda.synchronize()
@@ -525,6 +526,13 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers", p
                    "shared expert on a side stream")
             recv = {"records_sent_per_step": float(np.mean([s for s, _ in sizes])),
                     "records_received_per_step": float(np.mean([r for _, r in sizes]))}
+        stages = None
+        if exchange == "peers":  # one untimed step with events between its stages, max over ranks per stage
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            hidden.copy_(hidden0)
+            ep.ep_step_peers(st, hidden, attn, normed, stream=stream, flag=flag, events=evs)
+            torch.cuda.synchronize()
+            stages = {n: max_over_ranks(evs[i].elapsed_time(evs[i + 1]), world) for i, n in enumerate(ep.EP_STAGES)}
         hidden.copy_(hidden0)
         sizes.clear()
         step(0)  # the untimed step whose outputs the parity check reads
@@ -547,6 +555,10 @@ def ep_case(m, shape, K, W, stream, world, rank, dev, peaks, exchange="peers", p
            "clocks": clk}
     if recv:
         out["exchange_stats"] = recv
+    if stages:
+        out["stages_ms"] = stages
+        out["stages_note"] = ("one untimed step with CUDA events between its stages on the launching stream, each stage "
+                              "the max over ranks; the barriers include waiting for the slowest rank")
     if peer_note:
         out["note"] = peer_note
     if parity:

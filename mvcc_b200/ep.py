@@ -298,20 +298,37 @@ def ep_step(rank_state, exchange, hidden, attn_out, normed, next_rms1=None, stre
     return S, R
 
 
-def ep_step_peers(rank_state, hidden, attn_out, normed, next_rms1=None, stream=None, group=None, flag=None):
+EP_STAGES = ("dispatch", "barrier_1", "experts", "barrier_2", "combine")
+
+
+def ep_step_peers(rank_state, hidden, attn_out, normed, next_rms1=None, stream=None, group=None, flag=None,
+                  events=None):
     """One expert-parallel step of one rank with the peer-memory exchange: the dispatch kernel stores the records
     into the destination ranks' buffers and the expert stage stores the partial rows into the source ranks' buffers
-    (NVLink); a one-element all-reduce after each publishes the stores to every rank. No host synchronisation."""
+    (NVLink); a one-element all-reduce after each publishes the stores to every rank. No host synchronisation.
+    `events` (optional, 6 CUDA events) are recorded on the stream before the step and after each of its stages
+    (EP_STAGES) for a per-stage time split."""
     import torch.distributed as dist
     st = torch.cuda.current_stream(rank_state.device) if stream is None else stream
     if flag is None:
         flag = torch.zeros(1, device=rank_state.device)
+
+    def mark(i):
+        if events is not None:
+            events[i].record(st)
+
     with torch.cuda.stream(st):
+        mark(0)
         rank_state.dispatch_peers(hidden, attn_out, normed, st)
+        mark(1)
         dist.all_reduce(flag, group=group)
+        mark(2)
         rank_state.experts_peers(st)
+        mark(3)
         dist.all_reduce(flag, group=group)
+        mark(4)
         rank_state.combine_peers(hidden, attn_out, normed, next_rms1, st)
+        mark(5)
 
 
 class ExpertParallelMoe:

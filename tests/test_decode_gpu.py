@@ -69,8 +69,17 @@ def check_routing(orc, s, gpu_logits, gpu_idx, gpu_wts, ref_logits, ref_idx, ref
     srt = np.sort(ref_logits, axis=1)[:, ::-1]
     margin = srt[:, s.TOPK - 1] - srt[:, s.TOPK] if s.E > s.TOPK else np.full(len(srt), np.inf)
     ok = margin > 4 * tol
-    assert np.array_equal(gpu_idx[ok], ref_idx[ok])
-    assert np.allclose(gpu_wts[ok], ref_wts[ok], rtol=1e-3, atol=1e-6)
+    # the chosen set is equal wherever the 8th/9th margin is safe; the order of the picks (value desc) only where
+    # every gap between consecutive picks is safe too (two picks closer than the logit error may swap places)
+    order = np.argsort(gpu_idx, axis=1)
+    ref_order = np.argsort(ref_idx, axis=1)
+    g_set, r_set = np.take_along_axis(gpu_idx, order, 1), np.take_along_axis(ref_idx, ref_order, 1)
+    assert np.array_equal(g_set[ok], r_set[ok])
+    assert np.allclose(np.take_along_axis(gpu_wts, order, 1)[ok], np.take_along_axis(ref_wts, ref_order, 1)[ok],
+                       rtol=1e-3, atol=1e-6)
+    gaps = (srt[:, :s.TOPK] - srt[:, 1:s.TOPK + 1]).min(axis=1) if s.E > s.TOPK else np.full(len(srt), np.inf)
+    strict = gaps > 4 * tol
+    assert np.array_equal(gpu_idx[strict], ref_idx[strict])
     return float(margin.min())
 
 
