@@ -33,6 +33,9 @@ constexpr int kGemvU = 4;          // 16-byte loads per lane per row per iterati
 constexpr int kStackMaxT = 4;
 constexpr int kAttnMaxChunk = 64;  // keys per split (shared memory: 2 x 64 x 512 B)
 constexpr int kArgmaxMaxCtas = 1024;
+// Floats per split-K partial: acc [D], max, sum, padded to a multiple of 4 so that every partial starts on a 16-byte
+// boundary (its acc is stored as float4).
+__host__ __device__ constexpr int part_stride(int D) { return D + 4; }
 
 enum { EPI_BF16 = 0, EPI_ARGMAX = 1 };
 
@@ -286,7 +289,7 @@ struct AttnArgs {
   const uint16_t* q;
   const uint16_t* kc;
   const uint16_t* vc;
-  float* part;  // [(t * Hq + h) * nsplit + sp][D + 2]: acc, max, sum
+  float* part;  // [(t * Hq + h) * nsplit + sp][part_stride(D)]: acc, max, sum
   uint32_t* err;
   int T, Hq, Hkv, ctx, pos0, nsplit;
   float scale;
@@ -390,7 +393,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const __grid_constant__
       m = m_new;
     }
   }
-  float* dst = a.part + (((int64_t)t * a.Hq + h) * a.nsplit + sp) * (D + 2);
+  float* dst = a.part + (((int64_t)t * a.Hq + h) * a.nsplit + sp) * part_stride(D);
   *reinterpret_cast<float4*>(dst + lane * 8) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   *reinterpret_cast<float4*>(dst + lane * 8 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
   if (lane == 0) {
@@ -410,13 +413,14 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
   pdl_launch_dependents();
   const int job = blockIdx.x >> 2, quarter = blockIdx.x & 3;
   const int grp = threadIdx.x >> 6, d = quarter * 64 + (threadIdx.x & 63);
-  const float* src = part + (int64_t)job * nsplit * (D + 2);
+  constexpr int PS = part_stride(D);
+  const float* src = part + (int64_t)job * nsplit * PS;
   // global max over all splits (every thread computes it; the reads are broadcasts)
   float gm = -1e30f;
-  for (int s = 0; s < nsplit; ++s) gm = fmaxf(gm, __ldcg(src + s * (D + 2) + D));
+  for (int s = 0; s < nsplit; ++s) gm = fmaxf(gm, __ldcg(src + s * PS + D));
   float acc = 0.f, gl = 0.f;
   for (int s = grp; s < nsplit; s += 4) {
-    const float* p = src + s * (D + 2);
+    const float* p = src + s * PS;
     const float pl = __ldcg(p + D + 1);
     const float c = pl > 0.f ? __expf(__ldcg(p + D) - gm) : 0.f;
     gl += pl * c;
@@ -505,7 +509,7 @@ AttnWs attn_ws(const moe_attn_weights* w, int max_T, int ctx) {
   L.z = off;    off = ws_align(off + (w->gate ? (size_t)max_T * nq * 2 : 0));
   L.q = off;    off = ws_align(off + (size_t)max_T * nq * 2);
   L.o = off;    off = ws_align(off + (size_t)max_T * nq * 2);
-  L.part = off; off = ws_align(off + (size_t)max_T * w->Hq * L.nsplit_max * (w->D + 2) * 4);
+  L.part = off; off = ws_align(off + (size_t)max_T * w->Hq * L.nsplit_max * part_stride(w->D) * 4);
   L.err = off;  off = ws_align(off + 4);
   L.total = off;
   return L;

@@ -16,10 +16,12 @@ rsqrtf) and its split-K summation order are therefore matched within tolerance, 
   * lm_head_argmax     qwen.cu:451-456,         final RMSNorm of the last token, logits = x . W^T (fp32), argmax
                        kernels.cuh:1124-1164    with ties to the lowest index (NaN never wins; all-NaN gives 0)
 
-Parity of this module is unpinned: the reference's tests hold no golden vectors for these kernels and its CPU loops
-for attention (tests/kernels/qwen_attention.cu) live inside a GPU test program. The pin is to come from running the
-reference's own kernels (built from examples/qwen/kernels.cuh as oracle/Makefile's `ref` target does for the MoE
-block) on the same inputs on a B200.
+Pinning: the reference's tests hold no golden vectors for these kernels and its CPU loops for attention
+(tests/kernels/qwen_attention.cu) live inside a GPU test program, so the pin comes from the reference's own kernels:
+tests/golden/make_golden_stack.py ran its attention branch and LM head (examples/qwen/kernels.cuh built by
+oracle/Makefile's `ref` target, launched in qwen.cu's order by oracle/ref/qk_ref_shim.cu) on seeded inputs on a B200,
+and tests/test_golden_stack.py checks this module against those outputs (tests/test_stack_ref_pin_gpu.py repeats the
+comparison live).
 """
 import numpy as np
 
