@@ -709,13 +709,46 @@ def decode_stack_case(m, stream, world, peaks, tokens=16, W=3):
     us = ms / tokens * 1e3
     nb = stk.weight_bytes()
     gbs = nb / (us * 1e-6) / 1e9
+    next_token = int(stk.next.item())
+
+    # the same pieces timed apart (each its own graph of `tokens` repetitions): the 40 attention layers, the 40 MoE
+    # blocks, the LM head with argmax; their sum exceeds the step by the overlap programmatic launch gives across
+    # the pieces' boundaries
+    a_sh = stk.attn_shape
+    normed, attn_out = stk.normed[:1], stk.attn_out[:1]
+
+    def attn_only(i):
+        for j in range(stk.L):
+            stk.attn[j].forward(normed, attn_out, 4095, T=1, stream=stream)
+
+    def moe_only(i):
+        hidden.copy_(hidden0)
+        for j in range(stk.L):
+            nxt = stk.rms1[j + 1] if j + 1 < stk.L else stk.final_norm
+            stk.moe[j].forward(hidden, attn_out, normed, next_rms1=nxt, T=1, stream=stream)
+
+    def head_only(i):
+        stk.head.argmax(stk.normed[0], stk.next, stream=stream)
+
+    split = {}
+    for name, fn in (("attention", attn_only), ("moe", moe_only), ("lm_head", head_only)):
+        sms, _ = timed(graph_plan(fn, tokens, stream), stream, world)
+        split[name] = sms / tokens
+    kv = 2 * a_sh.Hkv * stk.ctx * a_sh.D * 2
+    attn_bytes = stk.L * (a_sh.weight_bytes() + kv)
+    head_bytes = stk.V * a_sh.H * 2
+    stage_frac = {"attention": attn_bytes / (split["attention"] * 1e-3) / 1e9 / peaks["hbm"],
+                  "moe": (nb - attn_bytes - head_bytes) / (split["moe"] * 1e-3) / 1e9 / peaks["hbm"],
+                  "lm_head": head_bytes / (split["lm_head"] * 1e-3) / 1e9 / peaks["hbm"]}
+    hidden.copy_(hidden0)
     out = {"workload": "BASELINE config 3: 40 x (RMSNorm, GQA attention Hq 16 / Hkv 2 / D 256 over a 4096-token bf16 "
                        "cache, RMSNorm, int4 G=64 MoE block), final RMSNorm, bf16 LM head 2048 x 151936 + argmax; "
                        "batch 1",
            "value": world * 1e6 / us, "unit": "tok/s", "ms_per_token": us / 1e3, "tokens": tokens,
            "bytes_per_token": nb, "hbm_gbs": gbs, "frac": gbs / peaks["hbm"], "peak_kind": peaks["kind"],
            "roofline_ms_per_token": nb / (peaks["hbm"] * 1e9) * 1e3,
-           "gpu_launches_per_token": per, "next_token": int(stk.next.item()), "clocks": clk,
+           "stage_ms_per_token": split, "stage_hbm_frac": stage_frac,
+           "gpu_launches_per_token": per, "next_token": next_token, "clocks": clk,
            "how": "mvcc_b200.stack.DecodeStack.step: moe_rmsnorm, 40 x (moe_attn_forward, moe_block_forward with the "
                   "next layer's norm), moe_lm_head_argmax; one CUDA graph of the token steps"}
     del stk

@@ -92,10 +92,13 @@ BlockArgs make_args(const moe_layer_weights* w, void* ws, const WsLayout& L, int
     a.offsets = reinterpret_cast<int32_t*>(b + L.offsets);
     a.tiles = b + L.tiles;
     a.ntiles = reinterpret_cast<int32_t*>(b + L.ntiles);
+    a.tiles2 = b + L.tiles2;
+    a.ntiles2 = reinterpret_cast<int32_t*>(b + L.ntiles2);
     a.sorted = reinterpret_cast<int32_t*>(b + L.sorted);
     a.slot = reinterpret_cast<float*>(b + L.slot);
     a.nwp = L.nwp;
     a.max_tiles = L.max_tiles;
+    a.max_tiles2 = L.max_tiles2;
   }
   return a;
 }

@@ -135,18 +135,21 @@ struct WsLayout {
   size_t ticket, err, gbar, logits, idx, wts, gate, nuniq, uniq, uoff, upairs, inter, sinter, routed, sout;
   // prefill sections (present when maxT >= kPrefillMinT): per-expert pair bitmaps and their word prefixes, expert
   // counts and offsets, the grouped-GEMM tile list, the pairs sorted by expert, the per-pair down partials
-  size_t bits, wpre, counts, offsets, tiles, ntiles, sorted, slot;
+  size_t bits, wpre, counts, offsets, tiles, ntiles, tiles2, ntiles2, sorted, slot;
   size_t total;
-  int maxT, nwp, max_tiles;
+  int maxT, nwp, max_tiles, max_tiles2;
 };
 
 // The reference switches moe() to its sort + tile path at T >= 8 (qwen.cu:347); so does this library.
 constexpr int kPrefillMinT = 8;
 
 // Rows (sorted pairs of one expert) per grouped-GEMM tile, and the upper bound of the tiles for P pairs over E
-// experts: sum_e ceil(n_e / kTileRows).
+// experts: sum_e ceil(n_e / rows). Two lists are built: tiles of kTileRows rows and double tiles of 2 kTileRows
+// rows (the expert GEMMs that run two 128-row sub-tiles against one dequantised B stage).
 constexpr int kTileRows = 128;
-__host__ __device__ inline int prefill_max_tiles(int P, int E) { return P / kTileRows + (E < P ? E : P) + 1; }
+__host__ __device__ inline int prefill_max_tiles(int P, int E, int rows = kTileRows) {
+  return P / rows + (E < P ? E : P) + 1;
+}
 
 // Launch accounting behind moe_stats_get: `launched(e)` passes a launch's status through and counts the launch when
 // it succeeded (the counters live in moe_api.cu).
@@ -194,7 +197,8 @@ __host__ __device__ inline WsLayout ws_layout(int H, int E, int TOPK, int I, int
   L.sout = o;   o = ws_align(o + sizeof(uint16_t) * (size_t)maxT * H);
   L.nwp = (int)((pairs + 31) / 32);
   L.max_tiles = prefill_max_tiles((int)pairs, E);
-  L.bits = L.wpre = L.counts = L.offsets = L.tiles = L.ntiles = L.sorted = L.slot = o;
+  L.max_tiles2 = prefill_max_tiles((int)pairs, E, 2 * kTileRows);
+  L.bits = L.wpre = L.counts = L.offsets = L.tiles = L.ntiles = L.tiles2 = L.ntiles2 = L.sorted = L.slot = o;
   if (maxT >= kPrefillMinT) {
     L.bits = o;    o = ws_align(o + sizeof(uint32_t) * (size_t)E * L.nwp);
     L.wpre = o;    o = ws_align(o + sizeof(uint32_t) * (size_t)E * L.nwp);
@@ -202,6 +206,8 @@ __host__ __device__ inline WsLayout ws_layout(int H, int E, int TOPK, int I, int
     L.offsets = o; o = ws_align(o + sizeof(int32_t) * ((size_t)E + 1));
     L.tiles = o;   o = ws_align(o + 16 * (size_t)L.max_tiles);
     L.ntiles = o;  o = ws_align(o + sizeof(int32_t));
+    L.tiles2 = o;  o = ws_align(o + 16 * (size_t)L.max_tiles2);
+    L.ntiles2 = o; o = ws_align(o + sizeof(int32_t));
     L.sorted = o;  o = ws_align(o + sizeof(int32_t) * pairs);
     L.slot = o;    o = ws_align(o + sizeof(float) * pairs * H);
   }
@@ -243,9 +249,11 @@ struct BlockArgs {
   int32_t* offsets;
   void* tiles;
   int32_t* ntiles;
+  void* tiles2;  // double tiles (2 kTileRows rows)
+  int32_t* ntiles2;
   int32_t* sorted;
   float* slot;
-  int nwp, max_tiles;
+  int nwp, max_tiles, max_tiles2;
   // row stride (elements) of `normed` as the routed gate/up operand; 0 = H (expert-parallel records are wider)
   int xstride;
   // expert-parallel combine (null otherwise): routed[t] = sum over ranks d < ep_world, ascending, with

@@ -2,24 +2,29 @@
 // shared-expert GEMMs (dense(), qwen.cu:298-319) and the grouped INT4 expert GEMMs (moe_gate_up_tile_kernel,
 // moe_down_tile_kernel, kernels.cuh:942-1057).
 //
-// One CTA per SM walks work items (tile of up to 128 A rows) x (n-tile of BN B rows), K in steps of 64. Stage s
-// of the ring holds one step's A rows and bf16 B rows; full[s] completes when both are in, empty[s] when the MMAs
-// that read them are done -- one wait and one commit per step for the issuing thread, whose shared-memory round
-// trips (a few hundred cycles per barrier operation) must stay under a step's MMA time (512 cycles at N = 256).
-// 8 + NDW warps (NDW = 8 dequantisation warps by default, 16 optionally):
+// One CTA per SM walks work items (tile of up to MS x 128 A rows) x (n-tile of BN B rows), K in steps of 64. Stage
+// s of the ring holds one step's A rows (MS sub-tiles of 128) and bf16 B rows; full[s] completes when both are in,
+// empty[s] when the MMAs that read them are done -- one wait and one commit per step for the issuing thread, whose
+// shared-memory round trips (a few hundred cycles per barrier operation) must stay under a step's MMA time (512
+// cycles per sub-tile at N = 256). MS = 2 (double tiles of the routed expert GEMMs) runs two 128-row sub-tiles
+// against each dequantised B stage: half the dequantisation and barrier work per MMA.
+// 4 + 4 MS + NDW warps (NDW = 8 dequantisation warps by default, 16 optionally):
 //   warps 0-1   A producers: contiguous A rows come in as one 2D TMA tile (box 64 x 128, 128-byte swizzle) per
 //               step; gathered rows (one per (token, slot) pair of the sorted pair list) come in by cp.async,
 //               eight lanes per row so that each row is one 128-byte line request, into the same swizzled K-major
 //               layout (cp.async.mbarrier.arrive.noinc on full[s]);
 //   warp 2      B producer, one lane: TMA tiles of the step's bf16 B rows into stage s, or of INT4 rows (rk
 //               k-steps of each row per box) into the raw ring (fullR) and, once per item, of the item's fp16 group
-//               scales; completion by transaction count (mbarrier expect_tx). Every load targets this CTA's own shared memory only;
-//   warp 3      allocates TMEM (two accumulator buffers of BN fp32 columns) and, from one lane, issues the
-//               tcgen05.mma of each step (M=128, N=BN, K=16 x 4), committing to empty[s] and, after an item's last
-//               step, to acc_full[buffer];
-//   warps 4-7   epilogue: wait acc_full, tcgen05.ld the accumulator rows of their TMEM lane quarter, apply the
-//               epilogue, store, release the buffer (acc_empty) -- overlapping the next item's main loop;
-//   warps 8+    INT4 only: each thread owns (row, K half) jobs of the tile (two at BN = 256 with 8 warps, one
+//               scales (double-buffered, or single where shared memory is short); completion by transaction count
+//               (mbarrier expect_tx). Every load targets this CTA's own shared memory only;
+//   warp 3      allocates TMEM (NB accumulator buffers of MS x BN fp32 columns: NB = 2 where they fit in 512
+//               columns, else 1) and, from one lane, issues the tcgen05.mma of each step (M=128, N=BN, K=16 x 4
+//               per sub-tile that holds rows), committing to empty[s] and, after an item's last step, to
+//               acc_full[buffer];
+//   warps 4..   4 MS epilogue warps: wait acc_full, tcgen05.ld the accumulator rows of their TMEM lane quarter
+//               (warp % 4) of their sub-tile, apply the epilogue, store, release the buffer (acc_empty) --
+//               overlapping the next item's main loop when NB = 2;
+//   last NDW    INT4 only: each thread owns (row, K half) jobs of the tile (two at BN = 256 with 8 warps, one
 //               with 16) and converts their 32 nibbles per step from the raw ring into the swizzled bf16 B of
 //               stage s as dequant32_bf16 does
 //               (kernels.cuh:925-940: bf16((q - 8) * scale), one rounding), fences the writes to the async proxy and
@@ -52,24 +57,30 @@ namespace moe {
 using namespace tc;
 
 constexpr int kBK = 64, kTileM = 128;
-// Warps 0-7 have fixed roles; NDW dequantisation warps follow (8 by default, 16 with MOE_B200_GEMM_DEQ_WARPS=16
-// for the routed INT4 GEMMs: twice the warps to hide the conversion's latency, one job per thread at BN = 256).
-constexpr int kDeqWarp0 = 8;
-__host__ __device__ constexpr int gemm_threads(int ndw) { return (kDeqWarp0 + ndw) * 32; }
+// Warps 0-3 and the 4 MS epilogue warps have fixed roles; NDW dequantisation warps follow (8 by default, 16 with
+// MOE_B200_GEMM_DEQ_WARPS=16 for the routed INT4 GEMMs at MS = 1: twice the warps to hide the conversion's latency,
+// one job per thread at BN = 256).
+__host__ __device__ constexpr int deq_warp0(int ms) { return 4 + 4 * ms; }
+__host__ __device__ constexpr int gemm_threads(int ndw, int ms) { return (deq_warp0(ms) + ndw) * 32; }
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far beyond any item's main loop
 
 struct GemmCfg {
   int bn, sa;            // BN, A + B ring depth
+  int ms, nb, nsc;       // 128-row sub-tiles per item, TMEM accumulator buffers, scale buffers
   int sr, rk;            // INT4: raw ring depth, k-steps per raw stage (a row's 32 * rk bytes per box)
   int ksc, sstride;      // INT4: scales per B row, their bytes per row in shared memory
   int a_tma, s_tma;      // A by TMA tiles (contiguous rows); scales by TMA (rows of at least 16 bytes)
   size_t a, b, raw, sc, bar, total;
 };
 
-__host__ __device__ inline GemmCfg gemm_cfg(int bn, bool int4, int sa, int sr, int rk, int K, int G) {
+__host__ __device__ inline GemmCfg gemm_cfg(int bn, bool int4, int sa, int sr, int rk, int K, int G, int ms,
+                                            int nsc) {
   GemmCfg c;
   c.bn = bn;
   c.sa = sa;
+  c.ms = ms;
+  c.nb = 2 * ms * bn <= 512 ? 2 : 1;
+  c.nsc = int4 ? nsc : 0;
   const int nk = K / kBK;
   while (rk > 1 && nk % rk) rk >>= 1;
   c.rk = rk;
@@ -79,10 +90,10 @@ __host__ __device__ inline GemmCfg gemm_cfg(int bn, bool int4, int sa, int sr, i
   c.a_tma = 0;
   c.s_tma = int4 && c.sstride >= 16;
   size_t o = 0;
-  c.a = o;   o += (size_t)sa * kTileM * 128;  // 16 KiB per stage (1024-byte aligned)
+  c.a = o;   o += (size_t)sa * ms * kTileM * 128;  // 16 KiB per sub-tile and stage (1024-byte aligned)
   c.b = o;   o += (size_t)sa * bn * 128;
   c.raw = o; o += (size_t)c.sr * bn * 32 * rk;
-  c.sc = o;  o += int4 ? 2 * (size_t)bn * c.sstride : 0;
+  c.sc = o;  o += int4 ? (size_t)c.nsc * bn * c.sstride : 0;
   c.bar = (o + 127) / 128 * 128;
   o = c.bar + 8 * (size_t)(2 * sa + 2 * c.sr + 8) + 16;
   c.total = o + 1024;  // the dynamic base is aligned up to 1024 bytes at run time
@@ -246,30 +257,33 @@ __device__ __forceinline__ int64_t b_row(const GemmParams& p, int e, int nt, int
   return (int64_t)e * p.b_rows_per_e + row;
 }
 
+template <int MS>
 __device__ __forceinline__ GemmTile load_tile(const GemmParams& p, int ti) {
   GemmTile t;
   if (p.tiles) {
     t = p.tiles[ti];
   } else {
     t.e = 0;
-    t.m0 = ti * kTileM;
+    t.m0 = ti * MS * kTileM;
     t.mcount = p.M - t.m0;
   }
   t.e = min(max(t.e, 0), p.E - 1);
-  t.mcount = max(0, min(t.mcount, kTileM));
+  t.mcount = max(0, min(t.mcount, MS * kTileM));
   if (t.m0 < 0) t.mcount = 0;
   return t;
 }
 
-template <int BN, bool INT4, int EPI, int NDW>
-__global__ void __launch_bounds__(gemm_threads(NDW), 1)
+template <int BN, bool INT4, int EPI, int NDW, int MS>
+__global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
     moe_gemm_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS, const GemmCfg c) {
-  constexpr int kDeqThreads = NDW * 32;
+  constexpr int kDeqThreads = NDW * 32, kDeqWarp0 = deq_warp0(MS);
+  constexpr int NB = 2 * MS * BN <= 512 ? 2 : 1;  // TMEM accumulator buffers
+  constexpr uint32_t kSubBytes = kTileM * 128;    // one 128-row A sub-tile of a stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int SA = c.sa, SR = c.sr;
+  const int SA = c.sa, SR = c.sr, NSC = c.nsc;
   const int nN = p.N / BN, nk = p.K / kBK;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + c.bar);
@@ -277,13 +291,14 @@ __global__ void __launch_bounds__(gemm_threads(NDW), 1)
   uint64_t* empty = full + SA;
   uint64_t* fullR = empty + SA;
   uint64_t* freeR = fullR + SR;
-  uint64_t* sc_full = freeR + SR;      // [2]
-  uint64_t* sc_free = sc_full + 2;     // [2]
-  uint64_t* acc_full = sc_free + 2;    // [2]
-  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint64_t* sc_full = freeR + SR;      // [NSC <= 2]
+  uint64_t* sc_free = sc_full + 2;     // [NSC <= 2]
+  uint64_t* acc_full = sc_free + 2;    // [NB <= 2]
+  uint64_t* acc_empty = acc_full + 2;  // [NB <= 2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  constexpr uint32_t cols = 2u * BN;  // 128, 256 or 512
+  constexpr uint32_t cols = (uint32_t)(NB * MS * BN);  // 128, 256 or 512
+  static_assert(cols == 128 || cols == 256 || cols == 512, "TMEM allocation");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
@@ -298,14 +313,14 @@ __global__ void __launch_bounds__(gemm_threads(NDW), 1)
       mbar_init(&sc_full[i], c.s_tma ? 1 : 32);
       mbar_init(&sc_free[i], kDeqThreads / 32);
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], 4 * MS);
     }
     *abort_flag = 0;
     mbar_fence_init();
   }
   // everything above touches only this CTA's shared memory: it overlaps the previous kernel under PDL
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int ntiles = p.tiles ? min(*p.ntiles, 1 << 20) : (p.M + kTileM - 1) / kTileM;
+  const int ntiles = p.tiles ? min(*p.ntiles, 1 << 20) : (p.M + MS * kTileM - 1) / (MS * kTileM);
   const int n_items = ntiles * nN;
   if ((int)blockIdx.x >= n_items) return;  // uniform for the CTA, before any TMEM is held
   if (warp == 3) tmem_alloc(tmem_slot, cols);
@@ -321,26 +336,29 @@ __global__ void __launch_bounds__(gemm_threads(NDW), 1)
         int g = 0;
         bool ok = true;
         for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-          const GemmTile t = load_tile(p, it / nN);
+          const GemmTile t = load_tile<MS>(p, it / nN);
+          const int nsub = MS > 1 && t.mcount > kTileM ? MS : 1;
           for (int kt = 0; kt < nk; ++kt, ++g) {
             const int s = g % SA;
             if (g >= SA && !wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
-            mbar_expect_tx(&full[s], 16384u);
-            tma_load_2d(smem + c.a + (size_t)s * 16384, &tmA, kt * kBK, t.m0, &full[s]);
+            mbar_expect_tx(&full[s], (uint32_t)nsub * kSubBytes);
+            for (int u = 0; u < nsub; ++u)
+              tma_load_2d(smem + c.a + ((size_t)s * MS + u) * kSubBytes, &tmA, kt * kBK, t.m0 + u * kTileM,
+                          &full[s]);
           }
         }
       }
     } else {
-      // gathered rows: lane l of the 64 fetches 16-byte chunk l % 8 of rows l / 8 + 8 i (i < 16), so that each
-      // warp instruction covers four whole 128-byte rows
+      // gathered rows: lane l of the 64 fetches 16-byte chunk l % 8 of rows l / 8 + 8 i (i < 16 MS), so that each
+      // warp instruction covers four whole 128-byte rows; sub-tile u's rows land kSubBytes further on
       const int t64 = threadIdx.x, ch = t64 & 7, r0 = t64 >> 3;
       int g = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-        const GemmTile t = load_tile(p, it / nN);
-        int soff[16];  // element offset of the source row of rows r0 + 8 i, or -1
+        const GemmTile t = load_tile<MS>(p, it / nN);
+        int soff[16 * MS];  // element offset of the source row of rows r0 + 8 i, or -1
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 16 * MS; ++i) {
           const int r = r0 + 8 * i;
           soff[i] = -1;
           if (r < t.mcount) {
@@ -352,9 +370,9 @@ __global__ void __launch_bounds__(gemm_threads(NDW), 1)
         for (int kt = 0; kt < nk; ++kt, ++g) {
           const int s = g % SA;
           if (g >= SA && !wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
-          uint8_t* dst = smem + c.a + (size_t)s * 16384;
+          uint8_t* dst = smem + c.a + (size_t)s * MS * kSubBytes;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < 16 * MS; ++i) {
             // rows past the tile are never loaded nor stored: their stale values are harmless
             if (soff[i] < 0) continue;
             cp_async16(dst + sw128_chunk(r0 + 8 * i, ch), p.A + soff[i] + kt * kBK);
@@ -370,13 +388,13 @@ __global__ void __launch_bounds__(gemm_threads(NDW), 1)
     int g = 0, j = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
-      const GemmTile t = load_tile(p, it / nN);
+      const GemmTile t = load_tile<MS>(p, it / nN);
       const int nt = it % nN;
       const int y0 = (int)((int64_t)t.e * p.b_rows_per_e + nt * BN);
       if constexpr (INT4) {
-        const int sb = j & 1;
+        const int sb = j % NSC;
         int freed = 1;  // one lane waits, the warp follows its verdict
-        if (lane == 0 && j >= 2) freed = wait_bar(&sc_free[sb], ((j >> 1) - 1) & 1, abort_flag, p.err) ? 1 : 0;
+        if (lane == 0 && j >= NSC) freed = wait_bar(&sc_free[sb], ((j / NSC) - 1) & 1, abort_flag, p.err) ? 1 : 0;
         if (!__shfl_sync(0xffffffffu, freed, 0)) break;
         uint8_t* sdst = smem + c.sc + (size_t)sb * BN * c.sstride;
         if (c.s_tma) {
@@ -436,20 +454,27 @@ __global__ void __launch_bounds__(gemm_threads(NDW), 1)
       int g = 0, j = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
-        const int ab = j & 1;
-        if (j >= 2 && !wait_bar(&acc_empty[ab], ((j >> 1) - 1) & 1, abort_flag, p.err)) break;
+        const int ab = j % NB, use = j / NB;
+        if (use >= 1 && !wait_bar(&acc_empty[ab], (use - 1) & 1, abort_flag, p.err)) break;
         fence_after_sync();
-        const uint32_t d = tmem + (uint32_t)(ab * BN);
+        // sub-tiles past the tile's rows are neither loaded nor multiplied (their epilogue warps skip them)
+        const int nsub = MS > 1 && load_tile<MS>(p, it / nN).mcount > kTileM ? MS : 1;
+        const uint32_t d = tmem + (uint32_t)(ab * MS * BN);
         for (int kt = 0; kt < nk; ++kt, ++g) {
           const int s = g % SA;
           ok = wait_bar(&full[s], (g / SA) & 1, abort_flag, p.err);
           if (!ok) break;
           fence_after_sync();
-          const uint32_t a_addr = smem_u32(smem + c.a + (size_t)s * 16384);
+          const uint32_t a_addr = smem_u32(smem + c.a + (size_t)s * MS * kSubBytes);
           const uint32_t b_addr = smem_u32(smem + c.b + (size_t)s * BN * 128);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_bf16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc, (kt | kk) != 0);
+          for (int u = 0; u < MS; ++u) {
+            if (u >= nsub) break;
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              mma_bf16(d + (uint32_t)(u * BN), sw128_desc(a_addr + u * kSubBytes + kk * 32),
+                       sw128_desc(b_addr + kk * 32), idesc, (kt | kk) != 0);
+          }
           mma_commit(&empty[s]);
         }
         if (ok) mma_commit(&acc_full[ab]);
@@ -457,18 +482,21 @@ __global__ void __launch_bounds__(gemm_threads(NDW), 1)
     }
     __syncwarp();
   } else if (warp < kDeqWarp0) {
-    // ---- epilogue: warp (w % 4) reads TMEM lanes 32 (w % 4) .. + 31 = tile rows
-    const int q = warp & 3;
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 of sub-tile (w - 4) / 4 = tile rows
+    // 128 (w - 4) / 4 + 32 (w % 4) ..
+    const int q = warp & 3, u = (warp - 4) >> 2;
     int j = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++j) {
-      const GemmTile t = load_tile(p, it / nN);
-      const int nt = it % nN, ab = j & 1;
-      if (!wait_bar(&acc_full[ab], (j >> 1) & 1, abort_flag, p.err)) break;
+      const GemmTile t = load_tile<MS>(p, it / nN);
+      const int nt = it % nN, ab = j % NB;
+      if (!wait_bar(&acc_full[ab], (j / NB) & 1, abort_flag, p.err)) break;
       __syncwarp();  // lane 0's arrive of the previous item can leave the warp split until here
       fence_after_sync();
-      const int r = q * 32 + lane;
+      const int r = u * kTileM + q * 32 + lane;
       const bool valid = r < t.mcount;
-      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+      // warp-uniform: a lane quarter without rows is not read (a sub-tile past the rows was not computed)
+      const bool any = u * kTileM + q * 32 < t.mcount;
+      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((ab * MS + u) * BN);
       int64_t orow = t.m0 + r;
       float rs = 1.f;
       if constexpr (EPI == EPI_SLOT) {
@@ -478,7 +506,9 @@ __global__ void __launch_bounds__(gemm_threads(NDW), 1)
       } else {
         orow = min(orow, (int64_t)p.out_nrows - 1);
       }
-      if constexpr (EPI == EPI_SILU_TILE || EPI == EPI_SILU_ROUND) {
+      if (!any) {
+        // nothing to store
+      } else if constexpr (EPI == EPI_SILU_TILE || EPI == EPI_SILU_ROUND) {
         uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * (BN / 2);
 #pragma unroll 1
         for (int c0 = 0; c0 < BN / 2; c0 += 16) {
@@ -561,8 +591,8 @@ __global__ void __launch_bounds__(gemm_threads(NDW), 1)
     int g = 0, j = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
-      const int sbuf = j & 1;
-      if (!wait_bar(&sc_full[sbuf], (j >> 1) & 1, abort_flag, p.err)) break;
+      const int sbuf = j % NSC;
+      if (!wait_bar(&sc_full[sbuf], (j / NSC) & 1, abort_flag, p.err)) break;
       __syncwarp();
       const uint8_t* scb = smem + c.sc + (size_t)sbuf * BN * c.sstride;
       for (int kt = 0; kt < nk; ++kt, ++g) {
@@ -627,25 +657,28 @@ static int raw_ksteps_forced() {
   return v;
 }
 
-static bool pick_cfg(int bn, bool int4, int K, int G, GemmCfg* out) {
+static bool pick_cfg(int bn, bool int4, int K, int G, int ms, GemmCfg* out) {
   static int optin = 0;
   if (!optin) optin = dev_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin, 227 * 1024);
-  // first fit in order of preference: 3+ A + B stages, then wide raw boxes, then raw ring depth
+  // first fit in order of preference: 3+ A + B stages, double-buffered scales (single ones only for double tiles,
+  // whose A stages are twice as large), wide raw boxes, raw ring depth
   const int sa_c[] = {4, 3, 2}, sr_c[] = {3, 2};
   const int forced = int4 ? raw_ksteps_forced() : 0;
   const int rk_pref[] = {4, 2, 1}, rk_one[] = {forced, forced, forced};
   const int* rk_c = forced ? rk_one : rk_pref;
+  const int n_nsc = int4 && ms > 1 ? 2 : 1;
   for (int sa : sa_c)
-    for (int ri = 0; ri < 3; ++ri)
-      for (int sr : sr_c) {
-        const int rk = rk_c[ri];
-        const GemmCfg c = gemm_cfg(bn, int4, sa, sr, rk, K, G);
-        if ((int)c.total <= optin && (sa >= 3 || rk == 1 || forced)) {
-          *out = c;
-          return true;
+    for (int ni = 0; ni < n_nsc; ++ni)
+      for (int ri = 0; ri < 3; ++ri)
+        for (int sr : sr_c) {
+          const int rk = rk_c[ri];
+          const GemmCfg c = gemm_cfg(bn, int4, sa, sr, rk, K, G, ms, 2 - ni);
+          if ((int)c.total <= optin && (sa >= 3 || rk == 1 || forced)) {
+            *out = c;
+            return true;
+          }
+          if (!int4) break;
         }
-        if (!int4) break;
-      }
   return false;
 }
 
@@ -697,10 +730,10 @@ static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, bool INT4, int EPI, int NDW = 8>
+template <int BN, bool INT4, int EPI, int NDW = 8, int MS = 1>
 static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaStream_t st) {
   GemmCfg c;
-  if (!pick_cfg(BN, INT4, p.K, p.G, &c)) return cudaErrorInvalidValue;
+  if (!pick_cfg(BN, INT4, p.K, p.G, MS, &c)) return cudaErrorInvalidValue;
   c.a_tma = p.a_rows ? 0 : 1;
   CUtensorMap tmA, tmB, tmS;
   memset(&tmA, 0, sizeof tmA);
@@ -734,7 +767,7 @@ static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaSt
   }
   static size_t granted = 0;
   if (c.total > granted) {
-    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<BN, INT4, EPI, NDW>,
+    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<BN, INT4, EPI, NDW, MS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.total);
     if (e != cudaSuccess) return e;
     granted = c.total;
@@ -745,7 +778,7 @@ static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaSt
   if (items <= 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)std::min<int64_t>(items, sms));
-  cfg.blockDim = dim3(gemm_threads(NDW));
+  cfg.blockDim = dim3(gemm_threads(NDW, MS));
   cfg.dynamicSmemBytes = c.total;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -753,7 +786,7 @@ static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return launched(cudaLaunchKernelEx(&cfg, moe_gemm_kernel<BN, INT4, EPI, NDW>, p, tmA, tmB, tmS, c));
+  return launched(cudaLaunchKernelEx(&cfg, moe_gemm_kernel<BN, INT4, EPI, NDW, MS>, p, tmA, tmB, tmS, c));
 }
 
 // Dequantisation warps of the routed INT4 GEMMs: 8, or 16 when the environment sets MOE_B200_GEMM_DEQ_WARPS=16
@@ -768,7 +801,14 @@ static int deq_warps() {
 }
 
 template <int BN, bool INT4>
-static cudaError_t launch_epi(const GemmParams& p, int epi, int max_tiles, bool pdl, cudaStream_t st) {
+static cudaError_t launch_epi(const GemmParams& p, int epi, int max_tiles, bool pdl, cudaStream_t st, int ms) {
+  if (ms == 2) {  // double tiles: the routed INT4 expert GEMMs at BN = 256
+    if constexpr (BN == 256 && INT4) {
+      if (epi == EPI_SILU_TILE) return launch_t<256, true, EPI_SILU_TILE, 8, 2>(p, max_tiles, pdl, st);
+      if (epi == EPI_SLOT) return launch_t<256, true, EPI_SLOT, 8, 2>(p, max_tiles, pdl, st);
+    }
+    return cudaErrorInvalidValue;
+  }
   switch (epi) {
     case EPI_F32: return launch_t<BN, INT4, EPI_F32>(p, max_tiles, pdl, st);
     case EPI_BF16: return launch_t<BN, INT4, EPI_BF16>(p, max_tiles, pdl, st);
@@ -788,7 +828,8 @@ static cudaError_t launch_epi(const GemmParams& p, int epi, int max_tiles, bool 
 cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, int tile_rows, bool int4, int max_tiles, bool pdl,
                         cudaStream_t st) {
   if (p.K <= 0 || p.K % kBK || p.N <= 0 || p.N % bn || p.lda % 8 || p.ldo % 8 || !p.A || !p.out) return cudaErrorInvalidValue;
-  if (tile_rows != kTileM) return cudaErrorInvalidValue;
+  if (tile_rows != kTileM && tile_rows != 2 * kTileM) return cudaErrorInvalidValue;
+  const int ms = tile_rows / kTileM;
   if (p.n_valid <= 0 || p.n_valid > p.N || (p.paired && p.n_valid != p.N)) return cudaErrorInvalidValue;
   const void* ptrs[5] = {p.A, p.Bh, p.Bq, p.Bs, p.out};
   for (const void* q : ptrs)
@@ -807,13 +848,14 @@ cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, int tile_rows, boo
   }
   switch (bn) {
     case 64:
-      return int4 ? launch_epi<64, true>(p, epi, max_tiles, pdl, st) : launch_epi<64, false>(p, epi, max_tiles, pdl, st);
+      return int4 ? launch_epi<64, true>(p, epi, max_tiles, pdl, st, ms)
+                  : launch_epi<64, false>(p, epi, max_tiles, pdl, st, ms);
     case 128:
-      return int4 ? launch_epi<128, true>(p, epi, max_tiles, pdl, st)
-                  : launch_epi<128, false>(p, epi, max_tiles, pdl, st);
+      return int4 ? launch_epi<128, true>(p, epi, max_tiles, pdl, st, ms)
+                  : launch_epi<128, false>(p, epi, max_tiles, pdl, st, ms);
     case 256:
-      return int4 ? launch_epi<256, true>(p, epi, max_tiles, pdl, st)
-                  : launch_epi<256, false>(p, epi, max_tiles, pdl, st);
+      return int4 ? launch_epi<256, true>(p, epi, max_tiles, pdl, st, ms)
+                  : launch_epi<256, false>(p, epi, max_tiles, pdl, st, ms);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -1,6 +1,6 @@
 // moe_gemm.h -- host interface of the tcgen05 tile GEMM (moe_gemm.cu) behind the prefill path.
 //
-// D[m][n] = sum_k A[row(m)][k] * B[row(n)][k] over tiles of up to 128 A rows and BN B rows, both K-major bf16 in
+// D[m][n] = sum_k A[row(m)][k] * B[row(n)][k] over tiles of up to 128 or 256 A rows and BN B rows, K-major bf16 in
 // shared memory (B optionally dequantized there from INT4), fp32 accumulators in TMEM, one of five epilogues.
 #pragma once
 #include <cuda_runtime.h>
@@ -17,7 +17,7 @@ enum GemmEpi {
 };
 
 // One M tile of the grouped problem: B matrix (expert) e, first A row m0 (in the tile-row space), rows mcount
-// (at most 128).
+// (at most tile_rows: 128, or 256 for double tiles).
 struct GemmTile {
   int e, m0, mcount, pad;
 };
@@ -55,10 +55,11 @@ struct GemmParams {
 };
 
 // Persistent launch over min(SMs, max_tiles x N/BN) CTAs; work item i = (tile i / (N/BN), n-tile i % (N/BN)),
-// items past *ntiles x N/BN are skipped. bn in {64, 128, 256}; tile_rows must be 128 (the row count the tile list
-// was built with); int4 selects the INT4 B path. pdl: launched as a programmatic dependent of the previous kernel
-// on the stream (its prologue overlaps that kernel's tail). Returns cudaErrorInvalidValue for unsupported
-// parameters.
+// items past *ntiles x N/BN are skipped. bn in {64, 128, 256}; tile_rows is the row count the tile list was built
+// with (or of the dense M tiles): 128, or 256 (two 128-row sub-tiles per dequantised B stage; INT4 at bn = 256 with
+// the EPI_SILU_TILE or EPI_SLOT epilogue only); int4 selects the INT4 B path. pdl: launched as a programmatic
+// dependent of the previous kernel on the stream (its prologue overlaps that kernel's tail). Returns
+// cudaErrorInvalidValue for unsupported parameters.
 cudaError_t launch_gemm(const GemmParams& p, int epi, int bn, int tile_rows, bool int4, int max_tiles, bool pdl,
                         cudaStream_t s);
 

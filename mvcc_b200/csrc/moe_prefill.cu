@@ -9,7 +9,8 @@
 //   topk        the reference's top-k rule per token (router_topk_kernel, kernels.cuh:774-809); marks bit p of
 //               expert e's bitmap for every pair p = t * TOPK + slot
 //   scan        per expert: popcounts and word prefixes of its bitmap; the last CTA turns the counts into the
-//               expert offsets and the grouped-GEMM tile list (kTileRows = 128 pairs per tile)
+//               expert offsets and the grouped-GEMM tile lists (kTileRows = 128 pairs per tile, and double tiles
+//               of 256 pairs)
 //   scatter     pair p of expert e goes to offsets[e] + (pairs of e before p): a stable counting sort by pair
 //               index, bit-exact and deterministic (moe_sort_kernel, kernels.cuh:906-923, orders ties arbitrarily)
 //   gate_up     grouped INT4 GEMM, A rows gathered per sorted pair, epilogue bf16(silu(g) * u) -> inter (sorted)
@@ -21,6 +22,7 @@
 // Numerics are the reference's tile numerics: fp32 accumulation of bf16 activations times bf16-dequantized INT4
 // weights, bf16 inter, fp32 per-slot partials reduced in slot order.
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 
@@ -134,24 +136,27 @@ __global__ void __launch_bounds__(kPT) prefill_scan_kernel(const BlockArgs a) {
   const int cnt = tid < E ? __ldcg(a.counts + tid) : 0;
   int npairs;
   const int off = block_excl_scan(cnt, sm, &npairs);
-  const int nt = (cnt + kTileRows - 1) / kTileRows;
-  int ntiles;
-  const int tbase = block_excl_scan(nt, sm, &ntiles);
-  GemmTile* tiles = static_cast<GemmTile*>(a.tiles);
-  if (tid < E) {
-    a.offsets[tid] = off;
-    for (int j = 0; j < nt && tbase + j < a.max_tiles; ++j) {
-      GemmTile g;
-      g.e = tid;
-      g.m0 = off + kTileRows * j;
-      g.mcount = min(kTileRows, cnt - kTileRows * j);
-      g.pad = 0;
-      tiles[tbase + j] = g;
+  if (tid < E) a.offsets[tid] = off;
+  if (tid == 0) a.offsets[E] = npairs;
+  // the tile list (kTileRows rows) and the double-tile list (2 kTileRows rows) over the same sorted pairs
+#pragma unroll 1
+  for (int li = 0; li < 2; ++li) {
+    const int rows = kTileRows << li, cap = li ? a.max_tiles2 : a.max_tiles;
+    GemmTile* tiles = static_cast<GemmTile*>(li ? a.tiles2 : a.tiles);
+    const int nt = (cnt + rows - 1) / rows;
+    int ntiles;
+    const int tbase = block_excl_scan(nt, sm, &ntiles);
+    if (tid < E) {
+      for (int j = 0; j < nt && tbase + j < cap; ++j) {
+        GemmTile g;
+        g.e = tid;
+        g.m0 = off + rows * j;
+        g.mcount = min(rows, cnt - rows * j);
+        g.pad = 0;
+        tiles[tbase + j] = g;
+      }
     }
-  }
-  if (tid == 0) {
-    a.offsets[E] = npairs;
-    *a.ntiles = min(ntiles, a.max_tiles);
+    if (tid == 0) *(li ? a.ntiles2 : a.ntiles) = min(ntiles, cap);
   }
 }
 
@@ -250,8 +255,28 @@ __global__ void __launch_bounds__(kPT) prefill_combine_kernel(const BlockArgs a,
 bool prefill_supported(const moe_layer_weights& w) { return w.E % 16 == 0; }
 
 // 256 B rows per tile: the most MMA work per pipeline step for the issuing thread's fixed barrier cost.
-static cudaError_t launch_wide(const GemmParams& p, int epi, bool int4, int max_tiles, cudaStream_t s) {
-  return launch_gemm(p, epi, 256, kTileRows, int4, max_tiles, false, s);
+static cudaError_t launch_wide(const GemmParams& p, int epi, bool int4, int tile_rows, int max_tiles, cudaStream_t s) {
+  return launch_gemm(p, epi, 256, tile_rows, int4, max_tiles, false, s);
+}
+
+// Rows per tile of the routed gate/up and down GEMMs: 2 kTileRows (double tiles: two 128-row sub-tiles per
+// dequantised B stage) unless the environment sets MOE_B200_GEMM_TILE_ROWS to 128 (both GEMMs) or to "G,D" with
+// G, D in {128, 256} (read once per process).
+static void expert_tile_rows(int* gu, int* dn) {
+  static int v[2] = {0, 0};
+  if (!v[0]) {
+    int r[2] = {2 * kTileRows, 2 * kTileRows};
+    if (const char* e = getenv("MOE_B200_GEMM_TILE_ROWS")) {
+      int x = 0, y = 0;
+      const int n = sscanf(e, "%d,%d", &x, &y);
+      if (n >= 1 && (x == kTileRows || x == 2 * kTileRows)) r[0] = r[1] = x;
+      if (n == 2 && (y == kTileRows || y == 2 * kTileRows)) r[1] = y;
+    }
+    v[1] = r[1];
+    v[0] = r[0];
+  }
+  *gu = v[0];
+  *dn = v[1];
 }
 
 static GemmParams base_params(const BlockArgs& a) {
@@ -302,7 +327,9 @@ static cudaError_t run_sort(const BlockArgs& a, int from, cudaStream_t s) {
 
 static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s, void* mark = nullptr) {
   const int P = a.T * a.w.TOPK;
-  const GemmTile* tiles = static_cast<const GemmTile*>(a.tiles);
+  int rows_gu, rows_dn;
+  expert_tile_rows(&rows_gu, &rows_dn);
+  const bool dgu = rows_gu > kTileRows, ddn = rows_dn > kTileRows;
   // gate/up: A = normed rows of the sorted pairs' tokens, B = expert gate rows i and up rows I + i
   GemmParams g = base_params(a);
   g.A = a.normed;
@@ -320,12 +347,12 @@ static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s, void* mark = 
   g.n_valid = g.N;
   g.K = a.w.H;
   g.E = a.w.E;
-  g.tiles = tiles;
-  g.ntiles = a.ntiles;
+  g.tiles = static_cast<const GemmTile*>(dgu ? a.tiles2 : a.tiles);
+  g.ntiles = dgu ? a.ntiles2 : a.ntiles;
   g.out = a.inter;
   g.ldo = a.w.I;
   g.out_nrows = P;
-  cudaError_t e = launch_wide(g, EPI_SILU_TILE, true, a.max_tiles, s);
+  cudaError_t e = launch_wide(g, EPI_SILU_TILE, true, rows_gu, dgu ? a.max_tiles2 : a.max_tiles, s);
   if (e == cudaSuccess) e = record_event(mark, s);
   if (e != cudaSuccess) return e;
   // down: A = inter rows in sorted order, B = expert down rows; epilogue weights by w[pair] into slot[pair]
@@ -340,15 +367,15 @@ static cudaError_t run_experts(const BlockArgs& a, cudaStream_t s, void* mark = 
   d.n_valid = d.N;
   d.K = a.w.I;
   d.E = a.w.E;
-  d.tiles = tiles;
-  d.ntiles = a.ntiles;
+  d.tiles = static_cast<const GemmTile*>(ddn ? a.tiles2 : a.tiles);
+  d.ntiles = ddn ? a.ntiles2 : a.ntiles;
   d.out = a.slot;
   d.ldo = a.w.H;
   d.out_rows = a.sorted;
   d.list_len = P;
   d.row_scale = a.wts;
   d.out_nrows = P;
-  return launch_wide(d, EPI_SLOT, true, a.max_tiles, s);
+  return launch_wide(d, EPI_SLOT, true, rows_dn, ddn ? a.max_tiles2 : a.max_tiles, s);
 }
 
 cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s) {
@@ -366,7 +393,7 @@ cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s) {
   g.out = a.sinter;
   g.ldo = a.w.Is;
   g.out_nrows = a.T;
-  cudaError_t e = launch_wide(g, EPI_SILU_ROUND, false, (a.T + 127) / 128, s);
+  cudaError_t e = launch_wide(g, EPI_SILU_ROUND, false, kTileRows, (a.T + 127) / 128, s);
   if (e != cudaSuccess) return e;
   GemmParams d = base_params(a);
   d.A = a.sinter;
@@ -380,7 +407,7 @@ cudaError_t prefill_shared(const BlockArgs& a, cudaStream_t s) {
   d.out = a.sout;
   d.ldo = a.w.H;
   d.out_nrows = a.T;
-  return launch_wide(d, EPI_BF16, false, (a.T + 127) / 128, s);
+  return launch_wide(d, EPI_BF16, false, kTileRows, (a.T + 127) / 128, s);
 }
 
 static cudaError_t clear_bits(const BlockArgs& a, cudaStream_t s) {
