@@ -9,14 +9,16 @@
  *   1. moe_ep_dispatch   (every rank, its own T tokens)  residual RMSNorm, router + top-k over all E experts, and
  *                        one dispatch record per (token, rank owning >= 1 of its experts) in `send`;
  *   2. all-to-all of the records (send_count per destination), then moe_ep_experts on the R records received:
- *                        one fp32 partial row per record (its local slots, in slot order, weighted);
+ *                        one bf16 partial row per record (its local slots, in slot order, weighted, summed in fp32
+ *                        and rounded once);
  *   3. all-to-all of the partial rows back (the reverse counts), then moe_ep_combine: per token the partials in rank
  *                        order, plus the gated shared expert (moe_shared_expert on the rank's own tokens).
  *
  * Numerics: those of the prefill path (tile numerics, per-slot fp32 partials) except that a token's routed sum is
- * taken per rank in slot order and then over ranks in rank order; with world = 1 it equals moe_block_forward's prefill
- * path bit for bit. Same conventions and error rules as moe_block.h; every call is asynchronous on `stream` and
- * allocates nothing.
+ * taken per rank in slot order, rounded to bf16 (the partial row that crosses the exchange: 2 H bytes instead of
+ * 4 H), and then summed over ranks in rank order in fp32; with world = 1 it equals moe_block_forward's prefill path
+ * with the routed row rounded to bf16. Same conventions and error rules as moe_block.h; every call is asynchronous
+ * on `stream` and allocates nothing.
  */
 #ifndef MOE_EP_H
 #define MOE_EP_H
@@ -44,26 +46,26 @@ MOE_API int moe_ep_dispatch(const moe_layer_weights* w, void* workspace, size_t 
                             int32_t* send_count, int32_t* tok_pos, moe_stream_t stream);
 
 /* Stage 2 on each rank. w_local: this rank's shard (E = E / world, the exp_* pointers at its first expert; router
- * and shared pointers unused). recv: R records (R = 0 launches nothing). part fp32 [R,H]: per record the sum, over
+ * and shared pointers unused). recv: R records (R = 0 launches nothing). part bf16 [R,H]: per record the sum, over
  * its slots whose id is a local expert and in slot order, of weight * down(bf16(silu(gate) * up)) with the prefill
- * path's tile numerics. Ids outside [-1, E) are flagged (MOE_ERR_EXPERT_INDEX) and skipped. The workspace is sized
+ * path's tile numerics, accumulated in fp32 and rounded to bf16. Ids outside [-1, E) are flagged (MOE_ERR_EXPERT_INDEX) and skipped. The workspace is sized
  * by moe_workspace_bytes(w_local, max(R_max, 8)). */
 MOE_API int moe_ep_experts(const moe_layer_weights* w_local, void* workspace, size_t workspace_bytes, const void* recv,
-                           int R, float* part, moe_stream_t stream);
+                           int R, uint16_t* part, moe_stream_t stream);
 
-/* Stage 3 on each rank, on the workspace of its moe_ep_dispatch call. ret fp32 [sum of send_count, H]: the partial
+/* Stage 3 on each rank, on the workspace of its moe_ep_dispatch call. ret bf16 [sum of send_count, H]: the partial
  * rows returned for this rank's records, in record order; sout bf16 [T,H] the shared expert of normed
  * (moe_shared_expert). hidden += attn_out + routed + sigmoid(gate) * sout with routed[t] the sum over ranks d
- * ascending of ret[tok_pos[t, d]] (tok_pos >= 0); then normed = rms(hidden) * next_rms1 when next_rms1 != NULL. */
+ * ascending of ret[tok_pos[t, d]] (tok_pos >= 0), in fp32; then normed = rms(hidden) * next_rms1 when next_rms1 != NULL. */
 MOE_API int moe_ep_combine(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
                            const uint16_t* attn_out, const uint16_t* sout, uint16_t* normed,
-                           const uint16_t* next_rms1, int T, int world, const int32_t* tok_pos, const float* ret,
+                           const uint16_t* next_rms1, int T, int world, const int32_t* tok_pos, const uint16_t* ret,
                            moe_stream_t stream);
 
 /* ---- peer-memory exchange: the same three stages with the data moved by the kernels themselves over NVLink.
  *
  * Every rank owns a receive buffer of moe_ep_recv_bytes(w, world, cap) bytes (records [world][cap][record], source
- * s's block at s * cap, then int32 counts [world]) and a return buffer of moe_ep_ret_bytes bytes (fp32 rows
+ * s's block at s * cap, then int32 counts [world]) and a return buffer of moe_ep_ret_bytes bytes (bf16 rows
  * [world][cap][H], destination d's block at d * cap), cap = the most tokens any rank passes per call. `peers` holds
  * every rank's buffers as addresses valid on the calling device (moe_ipc_open of the peers' handles; the local
  * buffers for this rank). moe_ep_dispatch_peers stores this rank's records and counts straight into the destination
@@ -76,7 +78,7 @@ MOE_API int moe_ep_combine(const moe_layer_weights* w, void* workspace, size_t w
 typedef struct moe_ep_peers {
   void* recv[8];
   int32_t* rcount[8];  /* inside each recv buffer (its counts) */
-  float* ret[8];
+  uint16_t* ret[8];  /* bf16 partial rows */
   int32_t rank, cap;
 } moe_ep_peers;
 MOE_API size_t moe_ep_recv_bytes(const moe_layer_weights* w, int world, int cap);

@@ -438,7 +438,7 @@ int moe_ep_dispatch(const moe_layer_weights* w, void* workspace, size_t workspac
 }
 
 int moe_ep_experts(const moe_layer_weights* w_local, void* workspace, size_t workspace_bytes, const void* recv, int R,
-                   float* part, moe_stream_t stream) {
+                   uint16_t* part, moe_stream_t stream) {
   NvtxRange nvtx("moe_ep_experts");
   if (!shape_ok(w_local) || !prefill_supported(*w_local) || !workspace || R < 0) return (int)cudaErrorInvalidValue;
   if (!weights_present(w_local, false, true, false)) return (int)cudaErrorInvalidValue;
@@ -451,7 +451,7 @@ int moe_ep_experts(const moe_layer_weights* w_local, void* workspace, size_t wor
   BlockArgs a = make_args(w_local, workspace, L, R);
   a.normed = static_cast<uint16_t*>(const_cast<void*>(recv));
   a.xstride = ep_record_bytes(w_local->H, w_local->TOPK) / 2;
-  a.routed = part;
+  a.routed16 = part;
   cudaError_t e = prefill_bits_clear(a, s);
   if (e == cudaSuccess) e = ep_mark(a, static_cast<const uint8_t*>(recv), nullptr, 0, s);
   if (e == cudaSuccess) e = prefill_routed_marked(a, s);
@@ -460,7 +460,7 @@ int moe_ep_experts(const moe_layer_weights* w_local, void* workspace, size_t wor
 
 int moe_ep_combine(const moe_layer_weights* w, void* workspace, size_t workspace_bytes, float* hidden,
                    const uint16_t* attn_out, const uint16_t* sout, uint16_t* normed, const uint16_t* next_rms1,
-                   int T, int world, const int32_t* tok_pos, const float* ret, moe_stream_t stream) {
+                   int T, int world, const int32_t* tok_pos, const uint16_t* ret, moe_stream_t stream) {
   NvtxRange nvtx("moe_ep_combine");
   if (!ep_geometry_ok(w, world) || !workspace || T < 1) return (int)cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(workspace) % 256 || workspace_bytes < layout_for(w, T).total)
@@ -490,7 +490,7 @@ size_t moe_ep_rcount_offset(const moe_layer_weights* w, int world, int cap) {
 
 size_t moe_ep_ret_bytes(const moe_layer_weights* w, int world, int cap) {
   if (!ep_geometry_ok(w, world) || cap < 1) return 0;
-  return (size_t)world * cap * w->H * sizeof(float);
+  return (size_t)world * cap * w->H * sizeof(uint16_t);
 }
 
 static bool peers_ok(const moe_ep_peers* p, int world) {

@@ -257,10 +257,13 @@ struct BlockArgs {
   // row stride (elements) of `normed` as the routed gate/up operand; 0 = H (expert-parallel records are wider)
   int xstride;
   // expert-parallel combine (null otherwise): routed[t] = sum over ranks d < ep_world, ascending, with
-  // ep_pos[t * ep_world + d] >= 0 of the returned partial row ep_ret[ep_pos[...]]
+  // ep_pos[t * ep_world + d] >= 0 of the returned bf16 partial row ep_ret[ep_pos[...]], in fp32
   const int32_t* ep_pos;
-  const float* ep_ret;
+  const uint16_t* ep_ret;
   int ep_world;
+  // expert-parallel experts stage (null otherwise): the routed rows of the records, rounded to bf16, go here
+  // instead of into routed
+  uint16_t* routed16;
 };
 
 }  // namespace moe

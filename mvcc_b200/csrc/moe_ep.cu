@@ -4,7 +4,9 @@
 // d * E / world. A token goes once to every rank that owns at least one of its TOPK experts, as one record: its
 // normed activations plus, per slot, the expert's id on that rank (-1 when the slot's expert lives elsewhere) and
 // the routing weight. The receiving rank runs its experts over the records (the prefill GEMMs) and returns one
-// fp32 partial row per record; the source sums the partials of a token in rank order (moe_prefill.cu's combine).
+// partial row per record (its slots summed in slot order in fp32, then rounded to bf16: half the bytes of an fp32
+// row on the return exchange); the source sums the partials of a token in rank order in fp32 (moe_prefill.cu's
+// combine).
 // The exchange either packs the records into one send buffer grouped by destination (for an all-to-all library
 // call), or, in peer mode, stores each record straight into the destination rank's receive buffer and each partial
 // row straight into the source rank's return buffer through peer-memory mappings (NVLink), every such store
@@ -137,7 +139,8 @@ __global__ void __launch_bounds__(256) ep_mark_kernel(const BlockArgs a, const u
 }
 
 // One CTA per record row r = src * cap + j of the receive buffer (peer mode): rows with a record sum their valid
-// slots in slot order (as prefill_combine_kernel's mode 1) and store the fp32 row into rank src's return buffer.
+// slots in slot order (as prefill_combine_kernel's mode 1) and store the row, rounded to bf16, into rank src's
+// return buffer.
 __global__ void __launch_bounds__(256) ep_return_kernel(const BlockArgs a, int world, EpPeers peers) {
   const int r = blockIdx.x, tid = threadIdx.x, H = a.w.H, K = a.w.TOPK;
   const int src = r / peers.cap, j = r - src * peers.cap;
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const BlockArgs a, int w
   bool ok[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) ok[k] = k < K && (unsigned)a.idx[(int64_t)r * K + k] < (unsigned)a.w.E;
-  float4* dst = reinterpret_cast<float4*>(peers.ret[src] + ((int64_t)peers.rank * peers.cap + j) * H);
+  uint2* dst = reinterpret_cast<uint2*>(peers.ret[src] + ((int64_t)peers.rank * peers.cap + j) * H);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const int i = tid + q * 256;
@@ -160,7 +163,8 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const BlockArgs a, int w
       acc.z += v.z;
       acc.w += v.w;
     }
-    dst[i] = acc;
+    dst[i] = make_uint2((uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16),
+                        (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16));
   }
   __threadfence_system();
 }

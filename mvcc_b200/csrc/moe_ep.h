@@ -12,7 +12,7 @@ constexpr int kEpMaxWorld = 8;
 struct EpPeers {
   uint8_t* recv[kEpMaxWorld];
   int32_t* rcount[kEpMaxWorld];
-  float* ret[kEpMaxWorld];
+  uint16_t* ret[kEpMaxWorld];  // bf16 partial rows
   int rank, cap;
 };
 

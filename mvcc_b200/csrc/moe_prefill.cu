@@ -186,9 +186,9 @@ __global__ void __launch_bounds__(kPT) prefill_unsort_kernel(const BlockArgs a, 
 }
 
 // ---- slot-order reduction and gated residual combine, one CTA per token.
-// mode: 1 = write routed, 2 = combine into hidden (+ next-layer RMSNorm when a.next_rms1 is set).
-// The routed sum is over the token's slots with a valid expert, in slot order, or, on the expert-parallel source
-// side (a.ep_pos set), over the partial rows the ranks returned, in rank order.
+// mode: 1 = write routed (fp32, or bf16 into a.routed16 when set), 2 = combine into hidden (+ next-layer RMSNorm when
+// a.next_rms1 is set). The routed sum is over the token's slots with a valid expert, in slot order, or, on the
+// expert-parallel source side (a.ep_pos set), over the bf16 partial rows the ranks returned, in rank order.
 __global__ void __launch_bounds__(kPT) prefill_combine_kernel(const BlockArgs a, int mode) {
   __shared__ float red[32];
   const int t = blockIdx.x, tid = threadIdx.x, H = a.w.H, K = a.w.TOPK;
@@ -210,14 +210,24 @@ __global__ void __launch_bounds__(kPT) prefill_combine_kernel(const BlockArgs a,
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       if (ep ? ok[k] < 0 : !ok[k]) continue;
-      const float* src = ep ? a.ep_ret + (int64_t)ok[k] * H : a.slot + ((int64_t)t * K + k) * H;
-      const float4 v = __ldcs(reinterpret_cast<const float4*>(src) + i);
+      float4 v;
+      if (ep) {
+        const uint2 u = __ldcs(reinterpret_cast<const uint2*>(a.ep_ret + (int64_t)ok[k] * H) + i);
+        v = make_float4(lo_bf(u.x), hi_bf(u.x), lo_bf(u.y), hi_bf(u.y));
+      } else {
+        v = __ldcs(reinterpret_cast<const float4*>(a.slot + ((int64_t)t * K + k) * H) + i);
+      }
       acc.x += v.x;
       acc.y += v.y;
       acc.z += v.z;
       acc.w += v.w;
     }
-    if (mode & 1) reinterpret_cast<float4*>(a.routed + (int64_t)t * H)[i] = acc;
+    if ((mode & 1) && a.routed16)
+      reinterpret_cast<uint2*>(a.routed16 + (int64_t)t * H)[i] =
+          make_uint2((uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16),
+                     (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16));
+    else if (mode & 1)
+      reinterpret_cast<float4*>(a.routed + (int64_t)t * H)[i] = acc;
     if (mode & 2) {
       const float4 h = reinterpret_cast<const float4*>(a.hidden + (int64_t)t * H)[i];
       const uint2 d = reinterpret_cast<const uint2*>(a.attn_out + (int64_t)t * H)[i];

@@ -5,7 +5,8 @@ expert. One step on each rank (include/moe_ep.h):
 
   1. dispatch: residual RMSNorm, router + top-k, one record per (token, rank owning >= 1 of its experts);
   2. the shared expert of the rank's own tokens on a side stream, overlapping 3-4;
-  3. the records reach their ranks, which run their experts over them -> one fp32 partial row per record;
+  3. the records reach their ranks, which run their experts over them -> one bf16 partial row per record (summed
+     in fp32, rounded once);
   4. the partial rows return to their source ranks; combine: per token the partials in rank order + the gated shared
      expert into hidden.
 
@@ -108,12 +109,13 @@ class EpRank:
         self.send_count = torch.zeros(world, dtype=torch.int32, device=dev)
         self.recv_count = torch.zeros(world, dtype=torch.int32, device=dev)
         self.tok_pos = torch.empty(max_tokens, world, dtype=torch.int32, device=dev)
-        self.part = torch.empty(cap, s.H, dtype=torch.float32, device=dev)
-        self.ret = torch.empty(cap, s.H, dtype=torch.float32, device=dev)
+        self.part = torch.empty(cap, s.H, dtype=torch.int16, device=dev)  # bf16 partial rows
+        self.ret = torch.empty(cap, s.H, dtype=torch.int16, device=dev)
         self.sout = torch.empty(max_tokens, s.H, dtype=torch.int16, device=dev)
         self.side = torch.cuda.Stream(device=dev)
         self._shared_done = None
-        # peer-mode exchange buffers: records in ([world][cap][record] + counts), partial rows back ([world][cap][H])
+        # peer-mode exchange buffers: records in ([world][cap][record] + counts), bf16 partial rows back
+        # ([world][cap][H])
         lc = ctypes.byref(layer.c)
         self.recv_bytes = _lib.moe_ep_recv_bytes(lc, world, max_tokens)
         self.ret_bytes = _lib.moe_ep_ret_bytes(lc, world, max_tokens)

@@ -323,8 +323,9 @@ class Oracle:
 
     def ep_routed(self, shape, layer, normed, idx, wts, world):
         """Routed output of the expert-parallel layer over `world` ranks (rank d owns experts [d*E/world,
-        (d+1)*E/world)): per rank the partial of its slots summed in slot order, then the partials summed in rank
-        order, in fp32 (mvcc_b200/csrc/moe_ep.cu and the source-side combine of moe_prefill.cu)."""
+        (d+1)*E/world)): per rank the partial of its slots summed in slot order in fp32 and rounded to bf16 (the row
+        that crosses the return exchange), then the partials summed in rank order in fp32 (mvcc_b200/csrc/moe_ep.cu
+        and the source-side combine of moe_prefill.cu)."""
         s = shape
         slot = self.slot_partials(shape, layer, normed, idx, wts)
         El = s.E // world
@@ -337,7 +338,7 @@ class Oracle:
                 on = owner[:, k] == d
                 part[on] = part[on] + slot[on, k]
             sent = (owner == d).any(axis=1)
-            routed[sent] = routed[sent] + part[sent]
+            routed[sent] = routed[sent] + bf16_to_f32(f32_to_bf16(part[sent]))
         return routed
 
     def ep_block_forward(self, shape, layer, hidden, attn_out, world, next_rms1=None):

@@ -108,7 +108,7 @@ def test_expert_parallel_entry_points_check_before_launch():
         if ok:
             off = lib.moe_ep_rcount_offset(wp, world, 64)
             assert off % 256 == 0 and off >= world * 64 * rec and nb >= off + 4 * world
-            assert lib.moe_ep_ret_bytes(wp, world, 64) == world * 64 * 2048 * 4
+            assert lib.moe_ep_ret_bytes(wp, world, 64) == world * 64 * 2048 * 2  # bf16 rows
     ws = ctypes.c_void_p(1 << 20)  # never dereferenced: every call below fails its checks first
     assert lib.moe_ep_dispatch(wp, ws, 1 << 30, None, None, None, 4, 3, None, None, None, None) == 1
     assert lib.moe_ep_dispatch(wp, None, 1 << 30, None, None, None, 4, 2, None, None, None, None) == 1

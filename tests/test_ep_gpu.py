@@ -1,9 +1,10 @@
 """GPU parity tests of the expert-parallel stages (include/moe_ep.h, mvcc_b200/ep.py) on one GPU: every rank's
 dispatch, experts and combine run in one process (`emulated_step`, the all-to-alls as device copies in the order
 NCCL would deliver), so the multi-rank numerics are checked without a second GPU. Bars: routing as for the block;
-outputs against the oracle's expert-parallel restatement (per-rank slot-order partials summed in rank order) within
-1e-2 (bf16) and 2e-2 (int4); world = 1 equals the single-GPU prefill block bit for bit; world = W equals world = 1
-up to fp32 summation order."""
+outputs against the oracle's expert-parallel restatement (per-rank slot-order partials rounded to bf16 -- the rows
+that cross the return exchange -- and summed in rank order) within 1e-2 (bf16) and 2e-2 (int4); world = 1 equals the
+single-GPU prefill block up to that one bf16 rounding of the routed row; world = W equals world = 1 up to the
+per-rank roundings and fp32 summation order."""
 import numpy as np
 import pytest
 import torch
@@ -42,7 +43,9 @@ def run_emulated(layer, world, Ts, seed, next_rms1=None, s=S128):
     return ranks, acts, hid, nrm, C
 
 
-def test_world1_equals_block_prefill():
+def test_world1_equals_block_prefill_up_to_the_bf16_return_row():
+    """One rank: the block's prefill path, except that the routed row is rounded to bf16 once (half a bf16 ulp of
+    |routed|, below one ulp of the largest hidden value)."""
     m = mb()
     L, layer = layer128()
     T = 300
@@ -51,12 +54,12 @@ def test_world1_equals_block_prefill():
     n0 = torch.zeros(T, S128.H, dtype=torch.int16, device="cuda")
     m.MoeBlock(layer, T).forward(h0, to_dev16(acts[0][1]), n0)
     torch.cuda.synchronize()
-    assert np.array_equal(hid[0].cpu().numpy(), h0.cpu().numpy())
-    assert np.array_equal(host16(nrm[0]), host16(n0))
+    assert O.max_rel_err(hid[0].cpu().numpy(), h0.cpu().numpy()) < 2.0 ** -8
+    assert O.max_rel_err(O.bf16_to_f32(host16(nrm[0])), O.bf16_to_f32(host16(n0))) < TOL_BF16
     assert ranks[0].error_word() == 0
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_emulated_ranks_against_oracle(orc, world):
     L, layer = layer128()
     Ts = [40 + 13 * r for r in range(world)]
@@ -96,7 +99,7 @@ def test_emulated_routed_against_oracle_int4(orc):
         ref = orc.ep_block_forward(S128, L, hidden, attn, world)
         S = int(ranks[r].send_count.sum())
         pos = ranks[r].tok_pos[:Ts[r]].cpu().numpy()
-        ret = ranks[r].ret[:S].cpu().numpy()
+        ret = O.bf16_to_f32(host16(ranks[r].ret[:S]))
         routed = np.zeros((Ts[r], S128.H), np.float32)
         for d in range(world):
             on = pos[:, d] >= 0
@@ -108,7 +111,8 @@ def test_emulated_routed_against_oracle_int4(orc):
 
 def test_world8_matches_world1_full_geometry():
     """BASELINE geometry (H=2048, E=256, top-8, I=Is=512, G=64) on the device generator: the same 1024 tokens on one
-    rank and split over 8 ranks give the same block output up to fp32 summation order of the routed partials."""
+    rank and split over 8 ranks give the same block output up to the bf16 rounding of the returned partial rows (one
+    per rank) and the fp32 summation order."""
     m = mb()
     E = ep()
     ms = m.MoeShape()
@@ -129,8 +133,8 @@ def test_world8_matches_world1_full_geometry():
         del ranks
     h1, n1 = outs[1]
     h8, n8 = outs[8]
-    assert O.max_rel_err(h8, h1) < 1e-5
-    assert np.mean(n8 == n1) > 0.999
+    assert O.max_rel_err(h8, h1) < 2.0 ** -8
+    assert O.max_rel_err(O.bf16_to_f32(n8.view(np.uint16)), O.bf16_to_f32(n1.view(np.uint16))) < TOL_BF16
 
 
 def test_all_tokens_on_one_shard():

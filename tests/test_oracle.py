@@ -187,19 +187,22 @@ def test_router_bias_is_added_to_fp32_logits(orc):
 
 
 def test_ep_oracle_one_rank_equals_block_and_ranks_only_reorder_sums(orc):
-    """The expert-parallel restatement with one rank is the tile-numerics block bit for bit; with W ranks it differs
-    only by the fp32 order of the routed sum (per rank in slot order, then over ranks)."""
+    """The expert-parallel restatement with one rank is the tile-numerics block with its routed row rounded to bf16
+    (the row that crosses the return exchange); with W ranks it differs further only by the per-rank roundings and
+    the fp32 order of the routed sum (per rank in slot order, then over ranks)."""
     s = O.Shape(H=512, E=32, TOPK=4, I=256, Is=256, G=32)
     L = O.make_layer(s, 5)
     h, a = O.make_activations(s, 6, 9)
     ref = orc.block_forward(s, L, h, a, mode=1)
     one = orc.ep_block_forward(s, L, h, a, 1)
-    assert np.array_equal(one["hidden"], ref["hidden"]) and np.array_equal(one["normed"], ref["normed"])
+    assert np.array_equal(one["routed"], O.bf16_to_f32(O.f32_to_bf16(ref["routed"])))
+    assert O.max_rel_err(one["hidden"], ref["hidden"]) < 2.0 ** -8
     for world in (2, 4):
         ep = orc.ep_block_forward(s, L, h, a, world)
-        assert O.max_rel_err(ep["routed"], ref["routed"]) < 1e-5
-        assert O.max_rel_err(ep["hidden"], ref["hidden"]) < 1e-5
+        assert O.max_rel_err(ep["routed"], ref["routed"]) < 2.0 ** -8
+        assert O.max_rel_err(ep["hidden"], ref["hidden"]) < 2.0 ** -8
     nr = O.f32_to_bf16(1.0 + 0.1 * O.normal(7, 1, s.H))
     ref_n = orc.block_forward(s, L, h, a, next_rms1=nr, mode=1)
     one_n = orc.ep_block_forward(s, L, h, a, 1, next_rms1=nr)
-    assert np.array_equal(one_n["hidden"], ref_n["hidden"]) and np.array_equal(one_n["normed"], ref_n["normed"])
+    assert O.max_rel_err(one_n["hidden"], ref_n["hidden"]) < 2.0 ** -8
+    assert O.max_rel_err(O.bf16_to_f32(one_n["normed"]), O.bf16_to_f32(ref_n["normed"])) < 1e-2
