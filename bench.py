@@ -837,6 +837,24 @@ def b200_arm(args, rank, world, local):
                              "path": "fused decode kernel" if b < 8 else "prefill (tile GEMMs)",
                              "stages_us": list(r["stage_us"]),
                              "e2e_tok_s": world * b * kb / (r["ms_e2e"] / 1e3)}
+        # batches 8 and 16 on the decode kernels (decode numerics), which the default sends to the prefill path (the
+        # reference's T >= 8 switch, qwen.cu:347, whose tile numerics the default keeps)
+        m.set_prefill_min_tokens(17)
+        try:
+            for b in (8, 16):
+                kb = min(K, 4096)
+                r = decode_case(m, shape, blocks, b, kb, W, stream, world, dev)
+                u = r["ms"] / kb * 1e3
+                bb = decode_bytes(shape, r["U"], b)
+                extra[f"{b}_decode_kernels"] = {
+                    "tok_s": world * b * kb / (r["ms"] / 1e3), "us_per_step": u, "steps": kb,
+                    "unique_experts": r["U"], "block_gbs": bb["block"] / (u * 1e-6) / 1e9,
+                    "block_frac": bb["block"] / (u * 1e-6) / 1e9 / peaks["hbm"],
+                    "path": ("fused decode kernel" if b <= 8 else "three-kernel decode path") +
+                            " (moe_set_prefill_min_tokens(17): decode numerics)",
+                    "stages_us": list(r["stage_us"]), "e2e_tok_s": world * b * kb / (r["ms_e2e"] / 1e3)}
+        finally:
+            m.set_prefill_min_tokens(0)
         result["decode_batches"] = extra
     del blocks, layers
     torch.cuda.empty_cache()

@@ -58,8 +58,8 @@ using namespace tc;
 
 constexpr int kBK = 64, kTileM = 128;
 // Warps 0-3 and the 4 MS epilogue warps have fixed roles; NDW dequantisation warps follow (8 by default, 16 with
-// MOE_B200_GEMM_DEQ_WARPS=16 for the routed INT4 GEMMs at MS = 1: twice the warps to hide the conversion's latency,
-// one job per thread at BN = 256).
+// MOE_B200_GEMM_DEQ_WARPS=16 for the routed INT4 GEMMs: twice the warps to hide the conversion's latency, one job per
+// thread at BN = 256).
 __host__ __device__ constexpr int deq_warp0(int ms) { return 4 + 4 * ms; }
 __host__ __device__ constexpr int gemm_threads(int ndw, int ms) { return (deq_warp0(ms) + ndw) * 32; }
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far beyond any item's main loop
@@ -513,8 +513,7 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
 #pragma unroll 1
         for (int c0 = 0; c0 < BN / 2; c0 += 16) {
           float gv[16], uv[16];
-          tmem_ld16(tb + c0, gv);
-          tmem_ld16(tb + BN / 2 + c0, uv);
+          tmem_ld16x2(tb + c0, tb + BN / 2 + c0, gv, uv);
           if (valid) {
             uint32_t o[8];
 #pragma unroll
@@ -537,44 +536,54 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
         uint16_t* out = static_cast<uint16_t*>(p.out) + orow * p.ldo + nt * BN;
         const int ncol = min(BN, p.n_valid - nt * BN);
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          float v[16];
-          tmem_ld16(tb + c0, v);
-          if (valid && c0 + 16 <= ncol) {
-            uint32_t o[8];
+        for (int c2 = 0; c2 < BN; c2 += 32) {
+          float vv[2][16];
+          tmem_ld16x2(tb + c2, tb + c2 + 16, vv[0], vv[1]);
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) o[jj] = (uint32_t)f2bf(v[2 * jj]) | ((uint32_t)f2bf(v[2 * jj + 1]) << 16);
-            reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
-          } else if (valid) {
+          for (int h = 0; h < 2; ++h) {
+            const int c0 = c2 + 16 * h;
+            const float* v = vv[h];
+            if (valid && c0 + 16 <= ncol) {
+              uint32_t o[8];
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj)
-              if (c0 + jj < ncol) out[c0 + jj] = f2bf(v[jj]);
+              for (int jj = 0; jj < 8; ++jj) o[jj] = (uint32_t)f2bf(v[2 * jj]) | ((uint32_t)f2bf(v[2 * jj + 1]) << 16);
+              reinterpret_cast<uint4*>(out + c0)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+              reinterpret_cast<uint4*>(out + c0)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            } else if (valid) {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                if (c0 + jj < ncol) out[c0 + jj] = f2bf(v[jj]);
+            }
           }
         }
       } else {  // EPI_F32, EPI_SLOT
         float* out = static_cast<float*>(p.out) + orow * p.ldo + nt * BN;
         const int ncol = min(BN, p.n_valid - nt * BN);
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          float v[16];
-          tmem_ld16(tb + c0, v);
-          if constexpr (EPI == EPI_F32) {
-            if (p.col_bias) {  // fp32 add after the dot product (the router's per-expert bias)
+        for (int c2 = 0; c2 < BN; c2 += 32) {
+          float vv[2][16];
+          tmem_ld16x2(tb + c2, tb + c2 + 16, vv[0], vv[1]);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int c0 = c2 + 16 * h;
+            float* v = vv[h];
+            if constexpr (EPI == EPI_F32) {
+              if (p.col_bias) {  // fp32 add after the dot product (the router's per-expert bias)
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj)
+                  v[jj] += (c0 + jj < ncol) ? __ldg(p.col_bias + nt * BN + c0 + jj) : 0.f;
+              }
+            }
+            if (valid && c0 + 16 <= ncol) {
+#pragma unroll
+              for (int jj = 0; jj < 16; jj += 4)
+                *reinterpret_cast<float4*>(out + c0 + jj) =
+                    make_float4(v[jj] * rs, v[jj + 1] * rs, v[jj + 2] * rs, v[jj + 3] * rs);
+            } else if (valid) {
 #pragma unroll
               for (int jj = 0; jj < 16; ++jj)
-                v[jj] += (c0 + jj < ncol) ? __ldg(p.col_bias + nt * BN + c0 + jj) : 0.f;
+                if (c0 + jj < ncol) out[c0 + jj] = v[jj] * rs;
             }
-          }
-          if (valid && c0 + 16 <= ncol) {
-#pragma unroll
-            for (int jj = 0; jj < 16; jj += 4)
-              *reinterpret_cast<float4*>(out + c0 + jj) =
-                  make_float4(v[jj] * rs, v[jj + 1] * rs, v[jj + 2] * rs, v[jj + 3] * rs);
-          } else if (valid) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj)
-              if (c0 + jj < ncol) out[c0 + jj] = v[jj] * rs;
           }
         }
       }
@@ -595,6 +604,17 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
       if (!wait_bar(&sc_full[sbuf], (j / NSC) & 1, abort_flag, p.err)) break;
       __syncwarp();
       const uint8_t* scb = smem + c.sc + (size_t)sbuf * BN * c.sstride;
+      // each job keeps four consecutive group scales in a register pair and reloads them when its group leaves the
+      // window (every 4 k-steps at G = 64): the rows a warp converts are sstride bytes apart, so their scale reads
+      // collide in a few banks, now once per window instead of once per k-step
+      const bool wide = (c.sstride & 7) == 0;
+      uint2 sreg[J];
+      int sbase[J];
+#pragma unroll
+      for (int jj = 0; jj < J; ++jj) {
+        sreg[jj] = make_uint2(0, 0);
+        sbase[jj] = -(1 << 20);
+      }
       for (int kt = 0; kt < nk; ++kt, ++g) {
         const int gr = g / c.rk, sr = gr % SR, sub = g - gr * c.rk, s = g % SA;
         ok = wait_bar(&fullR[sr], (gr / SR) & 1, abort_flag, p.err);
@@ -608,7 +628,19 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
           const int job = td + kDeqThreads * jj, r = job >> 1, h = job & 1;
           if (job >= BN * 2) continue;
           const uint4 w = *reinterpret_cast<const uint4*>(rawp + r * RB + h * 16);
-          const float sv = h2f(*reinterpret_cast<const uint16_t*>(scb + r * c.sstride + 2 * ((kt * kBK + h * 32) / p.G)));
+          const int gi = (kt * kBK + h * 32) / p.G;  // this job's group scale
+          float sv;
+          if (wide) {
+            if (gi < sbase[jj] || gi >= sbase[jj] + 4) {
+              sbase[jj] = gi & ~3;
+              sreg[jj] = *reinterpret_cast<const uint2*>(scb + r * c.sstride + 2 * sbase[jj]);
+            }
+            const int k = gi - sbase[jj];
+            const uint32_t pair = k < 2 ? sreg[jj].x : sreg[jj].y;
+            sv = h2f((uint16_t)((k & 1) ? (pair >> 16) : (pair & 0xffffu)));
+          } else {
+            sv = h2f(*reinterpret_cast<const uint16_t*>(scb + r * c.sstride + 2 * gi));
+          }
           const DqConst dc = dq_const(sv);
           const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -804,8 +836,13 @@ template <int BN, bool INT4>
 static cudaError_t launch_epi(const GemmParams& p, int epi, int max_tiles, bool pdl, cudaStream_t st, int ms) {
   if (ms == 2) {  // double tiles: the routed INT4 expert GEMMs at BN = 256
     if constexpr (BN == 256 && INT4) {
-      if (epi == EPI_SILU_TILE) return launch_t<256, true, EPI_SILU_TILE, 8, 2>(p, max_tiles, pdl, st);
-      if (epi == EPI_SLOT) return launch_t<256, true, EPI_SLOT, 8, 2>(p, max_tiles, pdl, st);
+      const bool d16 = deq_warps() == 16;
+      if (epi == EPI_SILU_TILE)
+        return d16 ? launch_t<BN, true, EPI_SILU_TILE, 16, 2>(p, max_tiles, pdl, st)
+                   : launch_t<BN, true, EPI_SILU_TILE, 8, 2>(p, max_tiles, pdl, st);
+      if (epi == EPI_SLOT)
+        return d16 ? launch_t<BN, true, EPI_SLOT, 16, 2>(p, max_tiles, pdl, st)
+                   : launch_t<BN, true, EPI_SLOT, 8, 2>(p, max_tiles, pdl, st);
     }
     return cudaErrorInvalidValue;
   }

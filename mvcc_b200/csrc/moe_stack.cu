@@ -2,19 +2,21 @@
 // attention branch of forward() (qwen.cu:413-425) and its LM head (qwen.cu:451-456), rebuilt for B200.
 //
 // Every piece streams weights or cache rows from HBM once, so each kernel is sized for memory-level parallelism:
-//   dense_gemv_kernel   y = x . W^T for T <= 4 tokens (qkv, gate, o, LM head): one warp per pair of rows, 16-byte
-//                       loads, 2 x 4 KB in flight per warp, x staged in shared memory in a bank-conflict-free
-//                       order. The first rows' weights are requested before griddepcontrol.wait, so under
-//                       programmatic dependent launch they stream while the previous kernel finishes. The LM-head
-//                       variant keeps each warp's best (logit, index) and the last CTA to finish (a ticket)
-//                       reduces the CTAs' results: argmax fused into the GEMV, one launch.
-//   qk_norm_rope_kernel per (token, head) warp: RMSNorm of the q and k heads, rotate-half RoPE, the new k and v rows
-//                       into the caches (attn_qk_norm_rope_kernel, kernels.cuh:608-663).
-//   attn_split_kernel   split-K decode attention (kernels.cuh:665-761): CTA (token, kv head, split) copies its chunk
-//                       of K and V rows into shared memory with two bulk copies, and warp g scores the chunk for
-//                       query head g: 32 keys' partial dot products per lane, one 31-shuffle reduce-scatter that
-//                       leaves key j's score in lane j, online softmax, acc += p v. Partials (acc, max, sum) per
-//                       split.
+//   dense_gemv_kernel   y = x . W^T for T <= 4 tokens (qkv, gate, o, LM head): each warp walks its rows in 4 KB
+//                       chunks (16-byte streaming loads, one row per warp at a time), two chunks in flight per
+//                       warp, two CTAs per SM; x staged in shared memory in a bank-conflict-free order. The first
+//                       chunk is requested before griddepcontrol.wait, so under programmatic dependent launch it
+//                       streams while the previous kernel finishes. The LM-head variant keeps each warp's best
+//                       (logit, index) and the last CTA to finish (a ticket) reduces the CTAs' results: argmax
+//                       fused into the GEMV, one launch.
+//   attn_split_kernel   split-K decode attention (kernels.cuh:665-761) with the per-head RMSNorm + rotate-half RoPE
+//                       of attn_qk_norm_rope_kernel (kernels.cuh:608-663) fused in: CTA (token, kv head, split)
+//                       copies its chunk of K and V rows into shared memory with two bulk copies; meanwhile warp g
+//                       normalises and rotates query head g; the step's new keys that fall in the chunk are
+//                       normalised, rotated and placed into the staged chunk (the token's own key and value row
+//                       also into the caches); then warp g scores the chunk: 32 keys' partial dot products per
+//                       lane, one 31-shuffle reduce-scatter that leaves key j's score in lane j, online softmax,
+//                       acc += p v. Partials (acc, max, sum) per split; about two CTAs per SM.
 //   attn_combine_kernel merges the splits (and applies the optional sigmoid gate, kernels.cuh:765-769).
 #include <algorithm>
 #include <cstring>
@@ -28,10 +30,9 @@ namespace moe {
 namespace {
 
 constexpr int kGemvWarps = 8;
-constexpr int kGemvRows = 2;       // rows per warp per iteration
-constexpr int kGemvU = 4;          // 16-byte loads per lane per row per iteration
+constexpr int kGemvU = 8;          // 16-byte loads per lane per chunk (a 4 KB chunk of one row)
 constexpr int kStackMaxT = 4;
-constexpr int kAttnMaxChunk = 64;  // keys per split (shared memory: 2 x 64 x 512 B)
+constexpr int kAttnMaxChunk = 64;  // keys per split at most (shared memory: 2 x 64 x 512 B)
 constexpr int kArgmaxMaxCtas = 1024;
 // Floats per split-K partial: acc [D], max, sum, padded to a multiple of 4 so that every partial starts on a 16-byte
 // boundary (its acc is stored as float4).
@@ -61,34 +62,35 @@ __device__ __forceinline__ int xs_pos(int i, int h, int nu) { return (h * nu + i
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
 template <int EPI>
-__global__ void __launch_bounds__(kGemvWarps * 32) dense_gemv_kernel(const __grid_constant__ GemvArgs g) {
+__global__ void __launch_bounds__(kGemvWarps * 32, 2) dense_gemv_kernel(const __grid_constant__ GemvArgs g) {
   extern __shared__ __align__(16) float xs[];
   __shared__ float bv_s[kGemvWarps];
   __shared__ int bi_s[kGemvWarps];
   __shared__ int is_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int K = g.K, N = g.N, T = g.T, nu = K >> 3;
-  const int stride = gridDim.x * kGemvWarps * kGemvRows;
-  int r0 = (blockIdx.x * kGemvWarps + warp) * kGemvRows;
-  // the first rows' weights do not depend on the previous kernel: request them before waiting for it
-  uint4 wv[kGemvRows][kGemvU];
+  constexpr int kChunk = 32 * kGemvU;  // 16-byte units per chunk (4 KB of a row)
+  const int cpr = (nu + kChunk - 1) / kChunk;
+  // warp wg owns rows wg, wg + nw, ...; its chunks run row by row, cpr chunks per row
+  const int wg = blockIdx.x * kGemvWarps + warp, nw = gridDim.x * kGemvWarps;
+  const int nrows = wg < N ? (N - 1 - wg) / nw + 1 : 0;
+  const int nch = nrows * cpr;
   auto row_ptr = [&](int r) -> const uint4* {
     const uint16_t* base = r < g.n0 ? g.w0 + (int64_t)r * K : g.w1 + (int64_t)(r - g.n0) * K;
     return reinterpret_cast<const uint4*>(base);
   };
-  auto load = [&](int r, int it) {
+  auto load = [&](uint4 (&w)[kGemvU], int c) {
+    const int q = c / cpr, part = c - q * cpr;
+    const uint4* p = row_ptr(wg + q * nw);
 #pragma unroll
-    for (int q = 0; q < kGemvRows; ++q) {
-      const int rr = r + q;
-      const uint4* p = rr < N ? row_ptr(rr) : nullptr;
-#pragma unroll
-      for (int u = 0; u < kGemvU; ++u) {
-        const int i = it * (32 * kGemvU) + u * 32 + lane;
-        wv[q][u] = (p && i < nu) ? ldg_stream(p + i) : make_uint4(0, 0, 0, 0);
-      }
+    for (int u = 0; u < kGemvU; ++u) {
+      const int i = part * kChunk + u * 32 + lane;
+      w[u] = i < nu ? ldg_stream(p + i) : make_uint4(0, 0, 0, 0);
     }
   };
-  if (r0 < N) load(r0, 0);
+  // two chunks in flight per warp; the first does not depend on the previous kernel: request it before waiting
+  uint4 wa[kGemvU], wb[kGemvU];
+  if (nch > 0) load(wa, 0);
   pdl_wait();
   pdl_launch_dependents();
   // x -> shared memory (fp32, permuted)
@@ -102,70 +104,62 @@ __global__ void __launch_bounds__(kGemvWarps * 32) dense_gemv_kernel(const __gri
   __syncthreads();
   float best_v = -1e30f;
   int best_i = 0;
-  const int iters = (nu + 32 * kGemvU - 1) / (32 * kGemvU);
-  for (; r0 < N; r0 += stride) {
-    float acc[kGemvRows][kStackMaxT];
+  float acc[kStackMaxT];
 #pragma unroll
-    for (int q = 0; q < kGemvRows; ++q)
+  for (int t = 0; t < kStackMaxT; ++t) acc[t] = 0.f;
+  auto compute = [&](const uint4 (&w)[kGemvU], int c) {
+    const int q = c / cpr, part = c - q * cpr;
 #pragma unroll
-      for (int t = 0; t < kStackMaxT; ++t) acc[q][t] = 0.f;
-    for (int it = 0; it < iters; ++it) {
-      if (it > 0) load(r0, it);
+    for (int u = 0; u < kGemvU; ++u) {
+      const int i = part * kChunk + u * 32 + lane;
+      if (i >= nu) break;
 #pragma unroll
-      for (int u = 0; u < kGemvU; ++u) {
-        const int i = it * (32 * kGemvU) + u * 32 + lane;
-        if (i >= nu) break;
-#pragma unroll
-        for (int t = 0; t < kStackMaxT; ++t) {
-          if (t >= T) break;
-          const float4 x0 = *reinterpret_cast<const float4*>(xs + t * K + xs_pos(i, 0, nu));
-          const float4 x1 = *reinterpret_cast<const float4*>(xs + t * K + xs_pos(i, 1, nu));
-#pragma unroll
-          for (int q = 0; q < kGemvRows; ++q) {
-            const uint4 w = wv[q][u];
-            float a = acc[q][t];
-            a = fmaf(lo_bf(w.x), x0.x, a);
-            a = fmaf(hi_bf(w.x), x0.y, a);
-            a = fmaf(lo_bf(w.y), x0.z, a);
-            a = fmaf(hi_bf(w.y), x0.w, a);
-            a = fmaf(lo_bf(w.z), x1.x, a);
-            a = fmaf(hi_bf(w.z), x1.y, a);
-            a = fmaf(lo_bf(w.w), x1.z, a);
-            a = fmaf(hi_bf(w.w), x1.w, a);
-            acc[q][t] = a;
-          }
-        }
+      for (int t = 0; t < kStackMaxT; ++t) {
+        if (t >= T) break;
+        const float4 x0 = *reinterpret_cast<const float4*>(xs + t * K + xs_pos(i, 0, nu));
+        const float4 x1 = *reinterpret_cast<const float4*>(xs + t * K + xs_pos(i, 1, nu));
+        float a = acc[t];
+        a = fmaf(lo_bf(w[u].x), x0.x, a);
+        a = fmaf(hi_bf(w[u].x), x0.y, a);
+        a = fmaf(lo_bf(w[u].y), x0.z, a);
+        a = fmaf(hi_bf(w[u].y), x0.w, a);
+        a = fmaf(lo_bf(w[u].z), x1.x, a);
+        a = fmaf(hi_bf(w[u].z), x1.y, a);
+        a = fmaf(lo_bf(w[u].w), x1.z, a);
+        a = fmaf(hi_bf(w[u].w), x1.w, a);
+        acc[t] = a;
       }
     }
-    // the next rows' first weights before this pair's reductions
-    const int r_next = r0 + stride;
+    if (part != cpr - 1) return;
+    // the row is complete: reduce across the warp (every lane gets the sums), store or keep the best
+    const int r = wg + q * nw;
 #pragma unroll
-    for (int q = 0; q < kGemvRows; ++q)
+    for (int t = 0; t < kStackMaxT; ++t) acc[t] = warp_sum(acc[t]);
+    if (EPI == EPI_BF16) {
+      if (lane < T) {
+        float v = acc[0];
 #pragma unroll
-      for (int t = 0; t < kStackMaxT; ++t) acc[q][t] = warp_sum(acc[q][t]);
-    if (r_next < N) load(r_next, 0);
-#pragma unroll
-    for (int q = 0; q < kGemvRows; ++q) {
-      const int r = r0 + q;
-      if (r >= N) break;
-      if (EPI == EPI_BF16) {
-        if (lane < T) {
-          float v = acc[q][0];
-#pragma unroll
-          for (int t = 1; t < kStackMaxT; ++t)
-            if (lane == t) v = acc[q][t];
-          if (r < g.n0) g.y0[(int64_t)lane * g.n0 + r] = f2bf(v);
-          else g.y1[(int64_t)lane * (N - g.n0) + (r - g.n0)] = f2bf(v);
-        }
-      } else {
-        const float v = acc[q][0];
-        if (lane == 0 && g.logits) g.logits[r] = v;
-        if (better(v, r, best_v, best_i)) {
-          best_v = v;
-          best_i = r;
-        }
+        for (int t = 1; t < kStackMaxT; ++t)
+          if (lane == t) v = acc[t];
+        if (r < g.n0) g.y0[(int64_t)lane * g.n0 + r] = f2bf(v);
+        else g.y1[(int64_t)lane * (N - g.n0) + (r - g.n0)] = f2bf(v);
+      }
+    } else {
+      const float v = acc[0];
+      if (lane == 0 && g.logits) g.logits[r] = v;
+      if (better(v, r, best_v, best_i)) {
+        best_v = v;
+        best_i = r;
       }
     }
+#pragma unroll
+    for (int t = 0; t < kStackMaxT; ++t) acc[t] = 0.f;
+  };
+  for (int c = 0; c < nch; c += 2) {
+    if (c + 1 < nch) load(wb, c + 1);
+    compute(wa, c);
+    if (c + 2 < nch) load(wa, c + 2);
+    if (c + 1 < nch) compute(wb, c + 1);
   }
   if (EPI != EPI_ARGMAX) return;
   // argmax: warp -> CTA -> (last CTA) grid, ties to the lowest index at every level
@@ -224,76 +218,52 @@ __global__ void __launch_bounds__(kGemvWarps * 32) dense_gemv_kernel(const __gri
   }
 }
 
-// Per (token, head) warp: RMSNorm + rotate-half RoPE of q and k heads; k and v rows into the caches at pos0 + t.
-__global__ void __launch_bounds__(256) qk_norm_rope_kernel(const uint16_t* __restrict__ qkv,
-                                                           const uint16_t* __restrict__ q_norm,
-                                                           const uint16_t* __restrict__ k_norm, uint16_t* __restrict__ q,
-                                                           uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int T,
-                                                           int Hq, int Hkv, int D, int rope_dim, float theta, int pos0,
-                                                           int ctx, float eps) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const int lane = threadIdx.x & 31;
-  const int job = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int heads = Hq + 2 * Hkv;
-  if (job >= T * heads) return;
-  const int t = job / heads, hh = job - t * heads;
-  const uint16_t* src = qkv + ((int64_t)t * heads + hh) * D;
-  const int pos = pos0 + t;
-  if (hh >= Hq + Hkv) {  // v rows are copied unchanged
-    uint16_t* dst = vc + ((int64_t)(hh - Hq - Hkv) * ctx + pos) * D;
-    for (int d = lane; d < D; d += 32) dst[d] = src[d];
-    return;
-  }
-  const bool is_q = hh < Hq;
-  const uint16_t* w = is_q ? q_norm : k_norm;
-  uint16_t* dst = is_q ? q + ((int64_t)t * Hq + hh) * D : kc + ((int64_t)(hh - Hq) * ctx + pos) * D;
-  float v[8];  // D == 256: lane holds d = lane + 32 i
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[i] = bf2f(src[lane + 32 * i]);
-    ss = fmaf(v[i], v[i], ss);
-  }
-  ss = warp_sum(ss);
-  const float inv = rsqrtf(ss / (float)D + eps);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * bf2f(w[lane + 32 * i]);
-  // pairs (d, d + rope_dim / 2) for d < rope_dim / 2; rope_dim / 2 is a multiple of 32, so both lie in this lane
-  const int half = rope_dim >> 1, hs = half >> 5;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int d = lane + 32 * i;
-    if (d < half) {
-      const float inv_freq = powf(theta, -(float)(2 * d) / (float)rope_dim);
-      float s, c;
-      sincosf((float)pos * inv_freq, &s, &c);
-      float b = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (j == i + hs) b = v[j];
-      const float a = v[i];
-      v[i] = a * c - b * s;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (j == i + hs) v[j] = b * c + a * s;
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) dst[lane + 32 * i] = f2bf(v[i]);
-}
-
-// Split-K decode attention, GQA: CTA (job = t * Hkv + kv head, split sp), warp g < G handles query head
-// kvh * G + g over keys [k0, k1) of the split. D == 256: lane owns dims 8 lane .. 8 lane + 7.
+// Split-K decode attention, GQA, with the per-head norm + RoPE of its inputs fused in. CTA (job = t * Hkv + kv head,
+// split sp); warp g < G handles query head kvh * G + g over keys [k0, k1) of the split. D == 256: lane owns dims
+// 8 lane .. 8 lane + 7.
 struct AttnArgs {
-  const uint16_t* q;
-  const uint16_t* kc;
-  const uint16_t* vc;
+  const uint16_t* qkv;     // bf16 [T][(Hq + 2 Hkv) D]: q heads, k heads, v heads of the new tokens
+  const uint16_t* q_norm;  // bf16 [D]
+  const uint16_t* k_norm;  // bf16 [D]
+  uint16_t* kc;            // bf16 [Hkv][ctx][D]
+  uint16_t* vc;
   float* part;  // [(t * Hq + h) * nsplit + sp][part_stride(D)]: acc, max, sum
   uint32_t* err;
-  int T, Hq, Hkv, ctx, pos0, nsplit;
-  float scale;
+  int T, Hq, Hkv, ctx, pos0, nsplit, rope_dim;
+  float scale, theta, eps;
 };
+
+// RMSNorm of one head row (lane holds dims 8 lane .. + 7 in v), times the norm weights, then rotate-half RoPE over
+// the first rope_dim dims at position pos (attn_qk_norm_rope_kernel, kernels.cuh:608-663): dim d < rope_dim / 2
+// pairs with d + rope_dim / 2, which another lane holds.
+__device__ __forceinline__ void head_norm_rope(float (&v)[8], const uint16_t* w, int rope_dim, float theta, int pos,
+                                               float eps, int lane) {
+  constexpr int D = 256;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)D + eps);
+  const uint4 wv = *reinterpret_cast<const uint4*>(w + lane * 8);
+  const float wf[8] = {lo_bf(wv.x), hi_bf(wv.x), lo_bf(wv.y), hi_bf(wv.y),
+                       lo_bf(wv.z), hi_bf(wv.z), lo_bf(wv.w), hi_bf(wv.w)};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * wf[i];
+  const int half = rope_dim >> 1, hl = half >> 3;  // lanes per half (half is a multiple of 32)
+  const bool rot = lane < 2 * hl, first = lane < hl;
+  const int src = rot ? (first ? lane + hl : lane - hl) : lane;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float other = __shfl_sync(0xffffffffu, v[i], src);
+    if (rot) {
+      const int d = (first ? lane : lane - hl) * 8 + i;  // the dim below half of this pair
+      const float inv_freq = powf(theta, -(float)(2 * d) / (float)rope_dim);
+      float sn, cs;
+      sincosf((float)pos * inv_freq, &sn, &cs);
+      v[i] = first ? v[i] * cs - other * sn : v[i] * cs + other * sn;
+    }
+  }
+}
 
 __global__ void __launch_bounds__(256) attn_split_kernel(const __grid_constant__ AttnArgs a) {
   constexpr int D = 256;
@@ -302,38 +272,64 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const __grid_constant__
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int job = blockIdx.x, sp = blockIdx.y;
   const int t = job / a.Hkv, kvh = job - t * a.Hkv;
-  const int G = a.Hq / a.Hkv;
+  const int G = a.Hq / a.Hkv, heads = a.Hq + 2 * a.Hkv;
   const int nkeys = a.pos0 + t + 1;
   const int chunk = (nkeys + a.nsplit - 1) / a.nsplit;
   const int k0 = min(nkeys, sp * chunk), k1 = min(nkeys, k0 + chunk), n = k1 - k0;
   uint8_t* ks = smem;
-  uint8_t* vs = smem + kAttnMaxChunk * D * 2;
+  uint8_t* vs = smem + (size_t)chunk * D * 2;
+  // The cached rows do not depend on the previous kernel (the qkv GEMV): the caches were last written by earlier
+  // steps' launches, which completed before that kernel started. So the chunk is requested before
+  // griddepcontrol.wait and streams in while the GEMV finishes; rows of this step's new keys are overwritten below.
   if (threadIdx.x == 0) {
     mbar_init(&kvbar, 1);
     mbar_fence_init();
-  }
-  __syncthreads();
-  pdl_wait();
-  pdl_launch_dependents();
-  if (threadIdx.x == 0) {
     expect_tx(&kvbar, (uint32_t)(2 * n * D * 2));
     if (n > 0) {
       bulk_g2s(ks, a.kc + ((int64_t)kvh * a.ctx + k0) * D, n * D * 2, &kvbar);
       bulk_g2s(vs, a.vc + ((int64_t)kvh * a.ctx + k0) * D, n * D * 2, &kvbar);
     }
   }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch_dependents();
+  // while the chunk lands: warp g normalises and rotates its query head (bf16, as stored by the reference)
+  float qf[8];
+  if (warp < G) {
+    const int h = kvh * G + warp;
+    const uint4 qv = reinterpret_cast<const uint4*>(a.qkv + ((int64_t)t * heads + h) * D)[lane];
+    float v[8] = {lo_bf(qv.x), hi_bf(qv.x), lo_bf(qv.y), hi_bf(qv.y), lo_bf(qv.z), hi_bf(qv.z), lo_bf(qv.w), hi_bf(qv.w)};
+    head_norm_rope(v, a.q_norm, a.rope_dim, a.theta, a.pos0 + t, a.eps, lane);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qf[i] = bf2f(f2bf(v[i])) * a.scale;
+  }
   const bool ok = bar_wait(&kvbar, 0);
   if (!ok && threadIdx.x == 0) atomicOr(a.err, (uint32_t)MOE_ERR_TIMEOUT);
+  // keys of this step's tokens (positions pos0 .. pos0 + t) inside the chunk: the cache does not hold them yet, so
+  // they are normalised and rotated here (k) or copied (v) into the staged chunk; token t's own key also goes to the
+  // caches (this CTA is the only one whose token ends at that position)
+  const int p0 = max(k0, a.pos0);
+  for (int p = p0 + warp; p < k1; p += blockDim.x >> 5) {
+    const int tn = p - a.pos0;
+    const uint16_t* row = a.qkv + (int64_t)tn * heads * D;
+    const uint4 kr = reinterpret_cast<const uint4*>(row + (int64_t)(a.Hq + kvh) * D)[lane];
+    const uint4 vr = reinterpret_cast<const uint4*>(row + (int64_t)(a.Hq + a.Hkv + kvh) * D)[lane];
+    float v[8] = {lo_bf(kr.x), hi_bf(kr.x), lo_bf(kr.y), hi_bf(kr.y), lo_bf(kr.z), hi_bf(kr.z), lo_bf(kr.w), hi_bf(kr.w)};
+    head_norm_rope(v, a.k_norm, a.rope_dim, a.theta, p, a.eps, lane);
+    const uint4 ko = make_uint4((uint32_t)f2bf(v[0]) | ((uint32_t)f2bf(v[1]) << 16),
+                                (uint32_t)f2bf(v[2]) | ((uint32_t)f2bf(v[3]) << 16),
+                                (uint32_t)f2bf(v[4]) | ((uint32_t)f2bf(v[5]) << 16),
+                                (uint32_t)f2bf(v[6]) | ((uint32_t)f2bf(v[7]) << 16));
+    *reinterpret_cast<uint4*>(ks + (size_t)(p - k0) * D * 2 + lane * 16) = ko;
+    *reinterpret_cast<uint4*>(vs + (size_t)(p - k0) * D * 2 + lane * 16) = vr;
+    if (tn == t) {
+      reinterpret_cast<uint4*>(a.kc + ((int64_t)kvh * a.ctx + p) * D)[lane] = ko;
+      reinterpret_cast<uint4*>(a.vc + ((int64_t)kvh * a.ctx + p) * D)[lane] = vr;
+    }
+  }
+  __syncthreads();
   if (warp >= G) return;
   const int h = kvh * G + warp;
-  float qf[8];
-  {
-    const uint4 qv = reinterpret_cast<const uint4*>(a.q + ((int64_t)t * a.Hq + h) * D)[lane];
-    qf[0] = lo_bf(qv.x); qf[1] = hi_bf(qv.x); qf[2] = lo_bf(qv.y); qf[3] = hi_bf(qv.y);
-    qf[4] = lo_bf(qv.z); qf[5] = hi_bf(qv.z); qf[6] = lo_bf(qv.w); qf[7] = hi_bf(qv.w);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) qf[i] *= a.scale;
-  }
   float m = -1e30f, l = 0.f, acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
@@ -402,36 +398,43 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const __grid_constant__
   }
 }
 
-// Merge of the nsplit partials of each (token, query head): CTA (job, quarter) handles dims [64 quarter, +64) with
-// 4 groups of 64 threads over the splits, merged in shared memory; o = bf16(acc / sum), then optionally
-// o = bf16(o * sigmoid(gate)).
+// Merge of the nsplit partials of each (token, query head): CTA (job, part) handles dims [32 part, +32); every warp
+// finds the largest split max itself (lanes over splits), then warp w sums splits w, w + 8, ... for its 32 dims
+// (independent loads, four in flight), and warp 0 adds the 8 warps' sums in warp order; o = bf16(acc / sum), then
+// optionally o = bf16(o * sigmoid(gate)).
 __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part, const uint16_t* __restrict__ z,
                                                            uint16_t* __restrict__ o, int nsplit) {
-  constexpr int D = 256;
-  __shared__ float acc_s[4][64], l_s[4];
+  constexpr int D = 256, kW = 8;
+  __shared__ float acc_s[kW][32], l_s[kW];
   pdl_wait();
   pdl_launch_dependents();
-  const int job = blockIdx.x >> 2, quarter = blockIdx.x & 3;
-  const int grp = threadIdx.x >> 6, d = quarter * 64 + (threadIdx.x & 63);
+  const int job = blockIdx.x >> 3, prt = blockIdx.x & 7;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, d = prt * 32 + lane;
   constexpr int PS = part_stride(D);
   const float* src = part + (int64_t)job * nsplit * PS;
-  // global max over all splits (every thread computes it; the reads are broadcasts)
   float gm = -1e30f;
-  for (int s = 0; s < nsplit; ++s) gm = fmaxf(gm, __ldcg(src + s * PS + D));
+  for (int s = lane; s < nsplit; s += 32) gm = fmaxf(gm, __ldcg(src + (int64_t)s * PS + D));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, off));
   float acc = 0.f, gl = 0.f;
-  for (int s = grp; s < nsplit; s += 4) {
-    const float* p = src + s * PS;
-    const float pl = __ldcg(p + D + 1);
-    const float c = pl > 0.f ? __expf(__ldcg(p + D) - gm) : 0.f;
+#pragma unroll 4
+  for (int s = warp; s < nsplit; s += kW) {
+    const float* p = src + (int64_t)s * PS;
+    const float pl = __ldcg(p + D + 1), pm = __ldcg(p + D), pv = __ldcg(p + d);
+    const float c = pl > 0.f ? __expf(pm - gm) : 0.f;
     gl += pl * c;
-    acc = fmaf(__ldcg(p + d), c, acc);
+    acc = fmaf(pv, c, acc);
   }
-  acc_s[grp][threadIdx.x & 63] = acc;
-  if ((threadIdx.x & 63) == 0) l_s[grp] = gl;
+  acc_s[warp][lane] = acc;
+  if (lane == 0) l_s[warp] = gl;
   __syncthreads();
-  if (grp != 0) return;
-  const float tot = acc_s[0][threadIdx.x] + acc_s[1][threadIdx.x] + acc_s[2][threadIdx.x] + acc_s[3][threadIdx.x];
-  const float lsum = l_s[0] + l_s[1] + l_s[2] + l_s[3];
+  if (warp != 0) return;
+  float tot = 0.f, lsum = 0.f;
+#pragma unroll
+  for (int w = 0; w < kW; ++w) {
+    tot += acc_s[w][lane];
+    lsum += l_s[w];
+  }
   uint16_t ov = f2bf(tot / lsum);
   if (z) ov = f2bf(bf2f(ov) * sigmoid(bf2f(z[(int64_t)job * D + d])));
   o[(int64_t)job * D + d] = ov;
@@ -487,8 +490,7 @@ cudaError_t launch_gemv(const GemvArgs& g, int max_ctas, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     granted = smem;
   }
-  const int per_cta = kGemvWarps * kGemvRows;
-  const int ctas = std::max(1, std::min(max_ctas, (g.N + per_cta - 1) / per_cta));
+  const int ctas = std::max(1, std::min(max_ctas, (g.N + kGemvWarps - 1) / kGemvWarps));  // a row per warp at least
   GemvArgs a = g;
   void* args[] = {&a};
   return launch_pdl(reinterpret_cast<const void*>(dense_gemv_kernel<EPI>), dim3(ctas), dim3(kGemvWarps * 32), smem,
@@ -496,7 +498,7 @@ cudaError_t launch_gemv(const GemvArgs& g, int max_ctas, cudaStream_t s) {
 }
 
 struct AttnWs {
-  size_t qkv, z, q, o, part, err, total;
+  size_t qkv, z, o, part, err, total;
   int nsplit_max;
 };
 
@@ -507,7 +509,6 @@ AttnWs attn_ws(const moe_attn_weights* w, int max_T, int ctx) {
   L.nsplit_max = (ctx + 15) / 16;
   L.qkv = off;  off = ws_align(off + (size_t)max_T * nqkv * 2);
   L.z = off;    off = ws_align(off + (w->gate ? (size_t)max_T * nq * 2 : 0));
-  L.q = off;    off = ws_align(off + (size_t)max_T * nq * 2);
   L.o = off;    off = ws_align(off + (size_t)max_T * nq * 2);
   L.part = off; off = ws_align(off + (size_t)max_T * w->Hq * L.nsplit_max * part_stride(w->D) * 4);
   L.err = off;  off = ws_align(off + 4);
@@ -552,12 +553,11 @@ int moe_attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, int 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint16_t* qkv = reinterpret_cast<uint16_t*>(ws + L.qkv);
   uint16_t* z = w->gate ? reinterpret_cast<uint16_t*>(ws + L.z) : nullptr;
-  uint16_t* q = reinterpret_cast<uint16_t*>(ws + L.q);
   uint16_t* o = reinterpret_cast<uint16_t*>(ws + L.o);
   float* part = reinterpret_cast<float*>(ws + L.part);
   uint32_t* err = reinterpret_cast<uint32_t*>(ws + L.err);
   const int nq = w->Hq * w->D, nqkv = (w->Hq + 2 * w->Hkv) * w->D;
-  const int gemv_ctas = stack_sms() * 3;
+  const int gemv_ctas = stack_sms() * 2;  // two CTAs per SM (the GEMV's launch bounds)
   // 1. qkv (and the gate) = normed . W^T, one launch
   GemvArgs g;
   memset(&g, 0, sizeof g);
@@ -572,33 +572,26 @@ int moe_attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, int 
   g.y1 = z;
   cudaError_t e = launch_gemv<EPI_BF16>(g, gemv_ctas, s);
   if (e != cudaSuccess) return (int)e;
-  // 2. per-head norm + RoPE, cache append
-  {
-    const uint16_t* a0 = qkv;
-    const uint16_t* a1 = w->q_norm;
-    const uint16_t* a2 = w->k_norm;
-    int Hq = w->Hq, Hkv = w->Hkv, D = w->D, rd = w->rope_dim, p0 = pos0, cx = ctx, TT = T;
-    float th = w->theta, eps = w->eps;
-    void* args[] = {&a0, &a1, &a2, &q, &kc, &vc, &TT, &Hq, &Hkv, &D, &rd, &th, &p0, &cx, &eps};
-    const int jobs = T * (w->Hq + 2 * w->Hkv);
-    e = launch_pdl(reinterpret_cast<const void*>(qk_norm_rope_kernel), dim3((jobs + 7) / 8), dim3(256), 0, s, args);
-    if (e != cudaSuccess) return (int)e;
-  }
-  // 3. split-K attention: about one wave of CTAs, 16 .. 64 keys per split
+  // 2. per-head norm + RoPE, cache append and split-K attention in one launch: about two CTAs per SM, 16 .. 64
+  // keys per split
   {
     const int nkeys = pos0 + T, jobs = T * w->Hkv;
-    const int want = (stack_sms() + jobs - 1) / jobs;
+    const int want = (2 * stack_sms() + jobs - 1) / jobs;
     int nsplit = std::max((nkeys + kAttnMaxChunk - 1) / kAttnMaxChunk, std::min(want, (nkeys + 15) / 16));
     nsplit = std::max(1, std::min(nsplit, L.nsplit_max));
-    const size_t smem = (size_t)2 * kAttnMaxChunk * w->D * 2;
+    const int chunk = (nkeys + nsplit - 1) / nsplit;  // the longest token's chunk
+    const size_t smem = (size_t)2 * chunk * w->D * 2;
     static bool granted = false;
     if (!granted) {
-      e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               2 * kAttnMaxChunk * 256 * 2);
       if (e != cudaSuccess) return (int)e;
       granted = true;
     }
     AttnArgs a;
-    a.q = q;
+    a.qkv = qkv;
+    a.q_norm = w->q_norm;
+    a.k_norm = w->k_norm;
     a.kc = kc;
     a.vc = vc;
     a.part = part;
@@ -609,7 +602,10 @@ int moe_attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, int 
     a.ctx = ctx;
     a.pos0 = pos0;
     a.nsplit = nsplit;
+    a.rope_dim = w->rope_dim;
     a.scale = 1.f / sqrtf((float)w->D);
+    a.theta = w->theta;
+    a.eps = w->eps;
     void* args[] = {&a};
     e = launch_pdl(reinterpret_cast<const void*>(attn_split_kernel), dim3(jobs, nsplit), dim3(256), smem, s, args);
     if (e != cudaSuccess) return (int)e;
@@ -617,10 +613,10 @@ int moe_attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, int 
     const uint16_t* zz = z;
     int ns = nsplit;
     void* cargs[] = {&pp, &zz, &o, &ns};
-    e = launch_pdl(reinterpret_cast<const void*>(attn_combine_kernel), dim3(T * w->Hq * 4), dim3(256), 0, s, cargs);
+    e = launch_pdl(reinterpret_cast<const void*>(attn_combine_kernel), dim3(T * w->Hq * 8), dim3(256), 0, s, cargs);
     if (e != cudaSuccess) return (int)e;
   }
-  // 4. attn_out = o . Wo^T
+  // 3. attn_out = o . Wo^T
   memset(&g, 0, sizeof g);
   g.x = o;
   g.w0 = w->o;
@@ -663,7 +659,7 @@ int moe_lm_head_argmax(const uint16_t* normed, const uint16_t* lm_head, int V, i
   g.pv = reinterpret_cast<float*>(ws + 256);
   g.pi = reinterpret_cast<int32_t*>(ws + 256 + (size_t)kArgmaxMaxCtas * 4);
   g.next = next;
-  return (int)launch_gemv<EPI_ARGMAX>(g, std::min(kArgmaxMaxCtas, stack_sms() * 4), (cudaStream_t)stream);
+  return (int)launch_gemv<EPI_ARGMAX>(g, std::min(kArgmaxMaxCtas, stack_sms() * 2), (cudaStream_t)stream);
 }
 
 }  // extern "C"

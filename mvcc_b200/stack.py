@@ -169,3 +169,29 @@ class DecodeStack:
             nxt = self.rms1[i + 1] if i + 1 < self.L else self.final_norm
             self.moe[i].forward(hidden, self.attn_out[:T], self.normed[:T], next_rms1=nxt, T=T, stream=stream)
         self.head.argmax(self.normed[T - 1], self.next, logits=logits, stream=stream)
+
+
+def main(argv=None):
+    """`python -m mvcc_b200.stack [--steps N] [--layers L]`: N plain decode steps (no CUDA graph) of BASELINE config 3
+    on cuda:0 -- seeded synthetic weights and a 4096-token cache, each step at position 4095 from the same residual --
+    printing the next token of each. Used to capture the step's kernel launch list with a profiler."""
+    import argparse
+    ap = argparse.ArgumentParser(prog="python -m mvcc_b200.stack")
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=40)
+    args = ap.parse_args(argv)
+    s = torch.cuda.Stream()
+    stk = DecodeStack(L=args.layers, ctx=4096, vocab=151936, seed=5)
+    h0, _ = synth_activations(stk.moe_shape, 1, seed=41, stream=s)
+    h = h0.clone()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for _ in range(args.steps):
+            h.copy_(h0)
+            stk.step(h, 4095, stream=s)
+            s.synchronize()
+            print("next token", int(stk.next.item()), flush=True)
+
+
+if __name__ == "__main__":
+    main()
