@@ -267,6 +267,8 @@ class NcclExchange:
 
     def a2a(self, out, inp, out_splits, in_splits):
         import torch.distributed as dist
+        if out.dtype == torch.int16:  # bf16 bit patterns (the partial rows): NCCL has no 16-bit integer type
+            out, inp = out.view(torch.bfloat16), inp.view(torch.bfloat16)
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
 
