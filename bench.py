@@ -719,12 +719,12 @@ def decode_stack_case(m, stream, world, peaks, tokens=16, W=3):
 
     def attn_only(i):
         for j in range(stk.L):
-            stk.attn[j].forward(normed, attn_out, 4095, T=1, stream=stream)
+            stk.attn[j].forward_rms(hidden, stk.rms1[j], attn_out, 4095, T=1, stream=stream)
 
     def moe_only(i):
         hidden.copy_(hidden0)
         for j in range(stk.L):
-            nxt = stk.rms1[j + 1] if j + 1 < stk.L else stk.final_norm
+            nxt = stk.final_norm if j + 1 == stk.L else None
             stk.moe[j].forward(hidden, attn_out, normed, next_rms1=nxt, T=1, stream=stream)
 
     def head_only(i):
@@ -749,8 +749,9 @@ def decode_stack_case(m, stream, world, peaks, tokens=16, W=3):
            "roofline_ms_per_token": nb / (peaks["hbm"] * 1e9) * 1e3,
            "stage_ms_per_token": split, "stage_hbm_frac": stage_frac,
            "gpu_launches_per_token": per, "next_token": next_token, "clocks": clk,
-           "how": "mvcc_b200.stack.DecodeStack.step: moe_rmsnorm, 40 x (moe_attn_forward, moe_block_forward with the "
-                  "next layer's norm), moe_lm_head_argmax; one CUDA graph of the token steps"}
+           "how": "mvcc_b200.stack.DecodeStack.step: 40 x (moe_attn_forward_rms: the layer's input norm fused into "
+                  "its qkv GEMV, moe_block_forward; the last one with the final norm), moe_lm_head_argmax; one CUDA "
+                  "graph of the token steps"}
     del stk
     return out
 

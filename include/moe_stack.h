@@ -51,8 +51,18 @@ MOE_API int moe_attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* 
                              const uint16_t* normed, uint16_t* attn_out, int T, void* workspace, size_t workspace_bytes,
                              moe_stream_t stream);
 
-/* y = bf16(x * rsqrt(mean(x^2) + eps) * w) per row (rmsnorm_kernel, kernels.cuh:83-93): the first layer's input norm
- * of a decode step (every later norm is fused into the MoE block: next_rms1). x fp32 [T,H], w and y bf16. */
+/* moe_attn_forward with the layer's input RMSNorm (qwen.cu:411, rmsnorm_kernel, kernels.cuh:83-93) fused into its
+ * first GEMV: the fp32 residual hidden [T,H] is normalised with rms1 (bf16 [H], eps = w->eps) by every CTA of that
+ * GEMV as it stages its input, instead of a normed input being read. A decode step then needs neither the first
+ * layer's separate norm launch nor the MoE block's fused next-layer norm (a serial tail: the last CTA of that kernel
+ * normalises the row while the GPU waits). Same shapes and errors as moe_attn_forward; hidden and rms1 16-byte
+ * aligned. */
+MOE_API int moe_attn_forward_rms(const moe_attn_weights* w, const uint16_t* rms1, const float* hidden, uint16_t* kc,
+                                 uint16_t* vc, int ctx, int pos0, uint16_t* attn_out, int T, void* workspace,
+                                 size_t workspace_bytes, moe_stream_t stream);
+
+/* y = bf16(x * rsqrt(mean(x^2) + eps) * w) per row (rmsnorm_kernel, kernels.cuh:83-93): a layer's input norm as a
+ * launch of its own (moe_attn_forward_rms fuses it instead). x fp32 [T,H], w and y bf16. */
 MOE_API int moe_rmsnorm(const float* x, const uint16_t* w, uint16_t* y, int T, int H, float eps, moe_stream_t stream);
 
 /* Bytes of caller-owned workspace for moe_lm_head_argmax over a vocabulary of V rows of H. */

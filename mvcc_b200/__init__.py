@@ -113,6 +113,8 @@ _SIGS = {
     # attention layer, first-layer norm and LM head of a decode step (include/moe_stack.h)
     "moe_attn_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeAttnWeights), _I, _I]),
     "moe_attn_forward": (_I, [ctypes.POINTER(MoeAttnWeights), _P, _P, _I, _I, _P, _P, _I, _P, ctypes.c_size_t, _P]),
+    "moe_attn_forward_rms": (_I, [ctypes.POINTER(MoeAttnWeights), _P, _P, _P, _P, _I, _I, _P, _I, _P, ctypes.c_size_t,
+                                  _P]),
     "moe_rmsnorm": (_I, [_P, _P, _P, _I, _I, ctypes.c_float, _P]),
     "moe_lm_head_workspace_bytes": (ctypes.c_size_t, [_I, _I]),
     "moe_lm_head_argmax": (_I, [_P, _P, _I, _I, _P, _P, _P, ctypes.c_size_t, _P]),

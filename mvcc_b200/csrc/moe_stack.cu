@@ -17,7 +17,8 @@
 //                       also into the caches); then warp g scores the chunk: 32 keys' partial dot products per
 //                       lane, one 31-shuffle reduce-scatter that leaves key j's score in lane j, online softmax,
 //                       acc += p v. Partials (acc, max, sum) per split; about two CTAs per SM.
-//   attn_combine_kernel merges the splits (and applies the optional sigmoid gate, kernels.cuh:765-769).
+//   attn_combine_kernel merges the splits in one pass (online-softmax merging, eight splits' loads in flight per
+//                       warp) and applies the optional sigmoid gate (kernels.cuh:765-769).
 #include <algorithm>
 #include <cstring>
 
@@ -41,7 +42,10 @@ __host__ __device__ constexpr int part_stride(int D) { return D + 4; }
 enum { EPI_BF16 = 0, EPI_ARGMAX = 1 };
 
 struct GemvArgs {
-  const uint16_t* x;   // bf16 [T][K]
+  const uint16_t* x;   // bf16 [T][K], or (x == null):
+  const float* xf;     //   fp32 [T][K] rows normalised in the prologue: bf16(xf * rsqrt(mean(xf^2) + eps) * xw)
+  const uint16_t* xw;  //   bf16 [K]
+  float eps;
   const uint16_t* w0;  // bf16 [n0][K]
   const uint16_t* w1;  // bf16 [N - n0][K] (rows n0 .. N - 1), may be null when n0 == N
   int n0, N, K, T;
@@ -88,18 +92,51 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) dense_gemv_kernel(const __
       w[u] = i < nu ? ldg_stream(p + i) : make_uint4(0, 0, 0, 0);
     }
   };
-  // two chunks in flight per warp; the first does not depend on the previous kernel: request it before waiting
+  // two chunks in flight per warp; weights do not depend on the previous kernel: the first two are requested before
+  // waiting for it
   uint4 wa[kGemvU], wb[kGemvU];
   if (nch > 0) load(wa, 0);
+  if (nch > 1) load(wb, 1);
   pdl_wait();
   pdl_launch_dependents();
   // x -> shared memory (fp32, permuted)
-  for (int e = threadIdx.x; e < T * nu; e += blockDim.x) {
-    const int t = e / nu, i = e - t * nu;
-    const uint4 v = reinterpret_cast<const uint4*>(g.x + (int64_t)t * K)[i];
-    float* dst = xs + t * K;
-    *reinterpret_cast<float4*>(dst + xs_pos(i, 0, nu)) = make_float4(lo_bf(v.x), hi_bf(v.x), lo_bf(v.y), hi_bf(v.y));
-    *reinterpret_cast<float4*>(dst + xs_pos(i, 1, nu)) = make_float4(lo_bf(v.z), hi_bf(v.z), lo_bf(v.w), hi_bf(v.w));
+  if (g.x) {
+    for (int e = threadIdx.x; e < T * nu; e += blockDim.x) {
+      const int t = e / nu, i = e - t * nu;
+      const uint4 v = reinterpret_cast<const uint4*>(g.x + (int64_t)t * K)[i];
+      float* dst = xs + t * K;
+      *reinterpret_cast<float4*>(dst + xs_pos(i, 0, nu)) = make_float4(lo_bf(v.x), hi_bf(v.x), lo_bf(v.y), hi_bf(v.y));
+      *reinterpret_cast<float4*>(dst + xs_pos(i, 1, nu)) = make_float4(lo_bf(v.z), hi_bf(v.z), lo_bf(v.w), hi_bf(v.w));
+    }
+  } else {
+    // every CTA normalises the rows itself (rmsnorm_kernel, kernels.cuh:83-93): x = bf16(xf * inv * xw)
+    for (int t = 0; t < T; ++t) {
+      const float4* row = reinterpret_cast<const float4*>(g.xf + (int64_t)t * K);
+      float ss = 0.f;
+      for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+        const float4 v = __ldcg(row + i);
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) bv_s[warp] = ss;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGemvWarps; ++w) tot += bv_s[w];
+      const float inv = rsqrtf(tot / (float)K + g.eps);
+      __syncthreads();  // bv_s is reused by the next row
+      float* dst = xs + t * K;
+      for (int i = threadIdx.x; i < nu; i += blockDim.x) {
+        const float4 a = __ldcg(row + 2 * i), b = __ldcg(row + 2 * i + 1);
+        const uint4 wv = reinterpret_cast<const uint4*>(g.xw)[i];
+        *reinterpret_cast<float4*>(dst + xs_pos(i, 0, nu)) =
+            make_float4(bf2f(f2bf(a.x * inv * lo_bf(wv.x))), bf2f(f2bf(a.y * inv * hi_bf(wv.x))),
+                        bf2f(f2bf(a.z * inv * lo_bf(wv.y))), bf2f(f2bf(a.w * inv * hi_bf(wv.y))));
+        *reinterpret_cast<float4*>(dst + xs_pos(i, 1, nu)) =
+            make_float4(bf2f(f2bf(b.x * inv * lo_bf(wv.z))), bf2f(f2bf(b.y * inv * hi_bf(wv.z))),
+                        bf2f(f2bf(b.z * inv * lo_bf(wv.w))), bf2f(f2bf(b.w * inv * hi_bf(wv.w))));
+      }
+    }
   }
   __syncthreads();
   float best_v = -1e30f;
@@ -156,10 +193,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) dense_gemv_kernel(const __
     for (int t = 0; t < kStackMaxT; ++t) acc[t] = 0.f;
   };
   for (int c = 0; c < nch; c += 2) {
-    if (c + 1 < nch) load(wb, c + 1);
     compute(wa, c);
     if (c + 2 < nch) load(wa, c + 2);
-    if (c + 1 < nch) compute(wb, c + 1);
+    if (c + 1 < nch) {
+      compute(wb, c + 1);
+      if (c + 3 < nch) load(wb, c + 3);
+    }
   }
   if (EPI != EPI_ARGMAX) return;
   // argmax: warp -> CTA -> (last CTA) grid, ties to the lowest index at every level
@@ -257,9 +296,10 @@ __device__ __forceinline__ void head_norm_rope(float (&v)[8], const uint16_t* w,
     const float other = __shfl_sync(0xffffffffu, v[i], src);
     if (rot) {
       const int d = (first ? lane : lane - hl) * 8 + i;  // the dim below half of this pair
-      const float inv_freq = powf(theta, -(float)(2 * d) / (float)rope_dim);
+      // the reference's fast intrinsics (kernels.cuh:650-653): its rounding, and no slow-path code in this kernel
+      const float inv_freq = __powf(theta, -(float)(2 * d) / (float)rope_dim);
       float sn, cs;
-      sincosf((float)pos * inv_freq, &sn, &cs);
+      __sincosf((float)pos * inv_freq, &sn, &cs);
       v[i] = first ? v[i] * cs - other * sn : v[i] * cs + other * sn;
     }
   }
@@ -398,42 +438,63 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const __grid_constant__
   }
 }
 
-// Merge of the nsplit partials of each (token, query head): CTA (job, part) handles dims [32 part, +32); every warp
-// finds the largest split max itself (lanes over splits), then warp w sums splits w, w + 8, ... for its 32 dims
-// (independent loads, four in flight), and warp 0 adds the 8 warps' sums in warp order; o = bf16(acc / sum), then
-// optionally o = bf16(o * sigmoid(gate)).
+// Merge of the nsplit partials of each (token, query head): CTA (job, part) handles dims [32 part, +32); warp w merges
+// splits w, w + 8, ... eight at a time (their loads issued together) into a running (max, sum, acc) as online softmax
+// does, and warp 0 merges the eight warps' results in warp order; o = bf16(acc / sum), then optionally
+// o = bf16(o * sigmoid(gate)).
 __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part, const uint16_t* __restrict__ z,
                                                            uint16_t* __restrict__ o, int nsplit) {
-  constexpr int D = 256, kW = 8;
-  __shared__ float acc_s[kW][32], l_s[kW];
+  constexpr int D = 256, kW = 8, kB = 8;
+  __shared__ float acc_s[kW][32], l_s[kW], m_s[kW];
   pdl_wait();
   pdl_launch_dependents();
   const int job = blockIdx.x >> 3, prt = blockIdx.x & 7;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, d = prt * 32 + lane;
   constexpr int PS = part_stride(D);
   const float* src = part + (int64_t)job * nsplit * PS;
-  float gm = -1e30f;
-  for (int s = lane; s < nsplit; s += 32) gm = fmaxf(gm, __ldcg(src + (int64_t)s * PS + D));
+  float m = -1e30f, l = 0.f, acc = 0.f;
+  for (int s0 = warp; s0 < nsplit; s0 += kW * kB) {
+    float pm[kB], pl[kB], pv[kB];
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, off));
-  float acc = 0.f, gl = 0.f;
-#pragma unroll 4
-  for (int s = warp; s < nsplit; s += kW) {
-    const float* p = src + (int64_t)s * PS;
-    const float pl = __ldcg(p + D + 1), pm = __ldcg(p + D), pv = __ldcg(p + d);
-    const float c = pl > 0.f ? __expf(pm - gm) : 0.f;
-    gl += pl * c;
-    acc = fmaf(pv, c, acc);
+    for (int k = 0; k < kB; ++k) {
+      const int s = s0 + k * kW;
+      const float* p = src + (int64_t)min(s, nsplit - 1) * PS;
+      pm[k] = __ldcg(p + D);
+      pl[k] = s < nsplit ? __ldcg(p + D + 1) : 0.f;
+      pv[k] = __ldcg(p + d);
+    }
+    float mn = m;
+#pragma unroll
+    for (int k = 0; k < kB; ++k)
+      if (pl[k] > 0.f) mn = fmaxf(mn, pm[k]);
+    const float c0 = __expf(m - mn);
+    l *= c0;
+    acc *= c0;
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const float c = pl[k] > 0.f ? __expf(pm[k] - mn) : 0.f;
+      l = fmaf(pl[k], c, l);
+      acc = fmaf(pv[k], c, acc);
+    }
+    m = mn;
   }
   acc_s[warp][lane] = acc;
-  if (lane == 0) l_s[warp] = gl;
+  if (lane == 0) {
+    l_s[warp] = l;
+    m_s[warp] = m;
+  }
   __syncthreads();
   if (warp != 0) return;
+  float gm = -1e30f;
+#pragma unroll
+  for (int w = 0; w < kW; ++w)
+    if (l_s[w] > 0.f) gm = fmaxf(gm, m_s[w]);
   float tot = 0.f, lsum = 0.f;
 #pragma unroll
   for (int w = 0; w < kW; ++w) {
-    tot += acc_s[w][lane];
-    lsum += l_s[w];
+    const float c = l_s[w] > 0.f ? __expf(m_s[w] - gm) : 0.f;
+    tot = fmaf(acc_s[w][lane], c, tot);
+    lsum = fmaf(l_s[w], c, lsum);
   }
   uint16_t ov = f2bf(tot / lsum);
   if (z) ov = f2bf(bf2f(ov) * sigmoid(bf2f(z[(int64_t)job * D + d])));
@@ -485,7 +546,8 @@ template <int EPI>
 cudaError_t launch_gemv(const GemvArgs& g, int max_ctas, cudaStream_t s) {
   const size_t smem = (size_t)g.T * g.K * 4;
   static size_t granted = 0;
-  if (smem > 48 * 1024 && smem > granted) {
+  // past 48 KB of dynamic plus static shared memory (the kernel's few reduction slots) a launch needs the opt-in
+  if (smem + 1024 > 48 * 1024 && smem > granted) {
     cudaError_t e = cudaFuncSetAttribute(dense_gemv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     granted = smem;
@@ -539,11 +601,17 @@ size_t moe_attn_workspace_bytes(const moe_attn_weights* w, int max_T, int ctx) {
   return attn_ws(w, max_T, ctx).total;
 }
 
-int moe_attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, int ctx, int pos0, const uint16_t* normed,
-                     uint16_t* attn_out, int T, void* workspace, size_t workspace_bytes, moe_stream_t stream) {
-  if (!attn_ok(w) || !kc || !vc || !normed || !attn_out || !workspace || T < 1 || T > kStackMaxT || pos0 < 0 ||
-      ctx < 1 || pos0 + T > ctx)
+}  // extern "C"
+
+// The attention branch; its input is normed (bf16) or, when normed is null, hidden (fp32) normalised with rms1
+// inside the first GEMV.
+static int attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, int ctx, int pos0, const uint16_t* normed,
+                        const float* hidden, const uint16_t* rms1, uint16_t* attn_out, int T, void* workspace,
+                        size_t workspace_bytes, moe_stream_t stream) {
+  if (!attn_ok(w) || !kc || !vc || !(normed || (hidden && rms1)) || !attn_out || !workspace || T < 1 ||
+      T > kStackMaxT || pos0 < 0 || ctx < 1 || pos0 + T > ctx)
     return (int)cudaErrorInvalidValue;
+  if (!normed && (!al16(hidden) || !al16(rms1))) return (int)cudaErrorInvalidValue;
   const AttnWs L = attn_ws(w, T, ctx);
   if (workspace_bytes < L.total) return (int)cudaErrorInvalidValue;
   if (!al16(kc) || !al16(vc) || !al16(normed) || !al16(workspace) || !al16(w->qkv) || !al16(w->o) ||
@@ -562,6 +630,9 @@ int moe_attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, int 
   GemvArgs g;
   memset(&g, 0, sizeof g);
   g.x = normed;
+  g.xf = hidden;
+  g.xw = rms1;
+  g.eps = w->eps;
   g.w0 = w->qkv;
   g.w1 = w->gate;
   g.n0 = nqkv;
@@ -626,6 +697,21 @@ int moe_attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, int 
   g.T = T;
   g.y0 = attn_out;
   return (int)launch_gemv<EPI_BF16>(g, gemv_ctas, s);
+}
+
+extern "C" {
+
+int moe_attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, int ctx, int pos0, const uint16_t* normed,
+                     uint16_t* attn_out, int T, void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  if (!normed) return (int)cudaErrorInvalidValue;
+  return attn_forward(w, kc, vc, ctx, pos0, normed, nullptr, nullptr, attn_out, T, workspace, workspace_bytes, stream);
+}
+
+int moe_attn_forward_rms(const moe_attn_weights* w, const uint16_t* rms1, const float* hidden, uint16_t* kc,
+                         uint16_t* vc, int ctx, int pos0, uint16_t* attn_out, int T, void* workspace,
+                         size_t workspace_bytes, moe_stream_t stream) {
+  if (!rms1 || !hidden) return (int)cudaErrorInvalidValue;
+  return attn_forward(w, kc, vc, ctx, pos0, nullptr, hidden, rms1, attn_out, T, workspace, workspace_bytes, stream);
 }
 
 int moe_rmsnorm(const float* x, const uint16_t* w, uint16_t* y, int T, int H, float eps, moe_stream_t stream) {

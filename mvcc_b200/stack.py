@@ -81,6 +81,14 @@ class AttnBlock:
                                      _ptr(normed), _ptr(attn_out), T, _ptr(self.ws), self.ws.numel(),
                                      _stream(stream)), "moe_attn_forward")
 
+    def forward_rms(self, hidden, rms1, attn_out, pos0, T=None, stream=None):
+        """forward() with the layer's input RMSNorm fused in: hidden fp32 [T,H] normalised with rms1 (bf16 bits [H])
+        inside the first GEMV (moe_attn_forward_rms)."""
+        T = hidden.shape[0] if T is None else T
+        _check(_lib.moe_attn_forward_rms(ctypes.byref(self.layer.c), _ptr(rms1), _ptr(hidden), _ptr(self.kc),
+                                         _ptr(self.vc), self.ctx, pos0, _ptr(attn_out), T, _ptr(self.ws),
+                                         self.ws.numel(), _stream(stream)), "moe_attn_forward_rms")
+
 
 def rmsnorm(x, w, y, eps=1e-6, stream=None):
     """y = bf16(x * rsqrt(mean(x^2) + eps) * w) per row (rmsnorm_kernel, kernels.cuh:83-93)."""
@@ -163,10 +171,11 @@ class DecodeStack:
     def step(self, hidden, pos0, T=1, stream=None, logits=None):
         """One decode step for T tokens whose fp32 residual is `hidden` [T,H] (updated in place) at positions
         pos0 .. pos0 + T - 1; the next token of the last one lands in self.next."""
-        rmsnorm(hidden, self.rms1[0], self.normed, self.attn_shape.eps, stream=stream)
+        # each layer's input norm runs inside its first GEMV (moe_attn_forward_rms); the last MoE block applies the
+        # final norm for the LM head
         for i in range(self.L):
-            self.attn[i].forward(self.normed[:T], self.attn_out[:T], pos0, T=T, stream=stream)
-            nxt = self.rms1[i + 1] if i + 1 < self.L else self.final_norm
+            self.attn[i].forward_rms(hidden[:T], self.rms1[i], self.attn_out[:T], pos0, T=T, stream=stream)
+            nxt = self.final_norm if i + 1 == self.L else None
             self.moe[i].forward(hidden, self.attn_out[:T], self.normed[:T], next_rms1=nxt, T=T, stream=stream)
         self.head.argmax(self.normed[T - 1], self.next, logits=logits, stream=stream)
 

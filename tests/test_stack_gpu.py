@@ -122,9 +122,38 @@ def _stack_host(stk, moe_host):
             "final": host(stk.final_norm), "head": host(stk.head.w), "moe": moe_host}
 
 
+@pytest.mark.parametrize("T", [1, 3])
+def test_attention_with_fused_input_norm_matches_the_separate_norm(T):
+    """moe_attn_forward_rms (the input RMSNorm computed by every CTA of the qkv GEMV) against moe_rmsnorm followed by
+    moe_attn_forward, on the same caches: the normed rows agree to the last bit except where the two sum-of-squares
+    orders round rsqrt differently, so the outputs agree within the bf16 bar and the cache rows written are equal."""
+    from mvcc_b200 import stack as st
+    a = st.AttnShape()
+    layer = st.synth_attn_layer(a, seed=77)
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    kc = (torch.randn(a.Hkv, 1024, a.D, generator=gen, device="cuda")).to(torch.bfloat16).view(torch.int16)
+    vc = (torch.randn(a.Hkv, 1024, a.D, generator=gen, device="cuda")).to(torch.bfloat16).view(torch.int16)
+    rms1 = (1.0 + 0.1 * torch.randn(a.H, generator=gen, device="cuda")).to(torch.bfloat16).view(torch.int16)
+    hidden = 3.0 * torch.randn(T, a.H, generator=gen, device="cuda")
+    b1 = st.AttnBlock(layer, 1024, max_T=T, caches=(kc.clone(), vc.clone()))
+    b2 = st.AttnBlock(layer, 1024, max_T=T, caches=(kc.clone(), vc.clone()))
+    normed = torch.zeros(T, a.H, dtype=torch.int16, device="cuda")
+    o1 = torch.zeros(T, a.H, dtype=torch.int16, device="cuda")
+    o2 = torch.zeros(T, a.H, dtype=torch.int16, device="cuda")
+    st.rmsnorm(hidden, rms1, normed, a.eps)
+    b1.forward(normed, o1, 600, T=T)
+    b2.forward_rms(hidden, rms1, o2, 600, T=T)
+    torch.cuda.synchronize()
+    assert rel(host(o2), host(o1)) < TOL_BF16
+    new = slice(600, 600 + T)
+    assert np.array_equal(host(b2.vc)[:, new], host(b1.vc)[:, new])
+    assert rel(host(b2.kc)[:, new], host(b1.kc)[:, new]) < TOL_BF16
+
+
 def test_two_layer_decode_step_against_oracle(orc):
-    """rmsnorm -> (attention, MoE block with the next layer's norm) x 2 -> LM head argmax, against the oracle's
-    composition of the same steps (decode numerics for the T = 1 MoE block)."""
+    """(attention with its input RMSNorm fused into the qkv GEMV, MoE block) x 2, the last block applying the final
+    norm -> LM head argmax, against the oracle's composition of the same steps (rmsnorm, attention, the block with the
+    next layer's norm; decode numerics for the T = 1 MoE block)."""
     import mvcc_b200 as m
     from mvcc_b200 import stack as st
     ms = O.Shape(H=2048, E=32, TOPK=8, I=512, Is=512, G=64)
