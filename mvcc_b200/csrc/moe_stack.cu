@@ -65,7 +65,9 @@ __device__ __forceinline__ int xs_pos(int i, int h, int nu) { return (h * nu + i
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
-template <int EPI>
+// MT: the most tokens this instantiation handles (1, or kStackMaxT): the single-token build carries a quarter of the
+// inner-loop code, which matters for short launches that start on a cold instruction cache.
+template <int EPI, int MT>
 __global__ void __launch_bounds__(kGemvWarps * 32, 2) dense_gemv_kernel(const __grid_constant__ GemvArgs g) {
   extern __shared__ __align__(16) float xs[];
   __shared__ float bv_s[kGemvWarps];
@@ -141,9 +143,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) dense_gemv_kernel(const __
   __syncthreads();
   float best_v = -1e30f;
   int best_i = 0;
-  float acc[kStackMaxT];
+  float acc[MT];
 #pragma unroll
-  for (int t = 0; t < kStackMaxT; ++t) acc[t] = 0.f;
+  for (int t = 0; t < MT; ++t) acc[t] = 0.f;
   auto compute = [&](const uint4 (&w)[kGemvU], int c) {
     const int q = c / cpr, part = c - q * cpr;
 #pragma unroll
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) dense_gemv_kernel(const __
       const int i = part * kChunk + u * 32 + lane;
       if (i >= nu) break;
 #pragma unroll
-      for (int t = 0; t < kStackMaxT; ++t) {
+      for (int t = 0; t < MT; ++t) {
         if (t >= T) break;
         const float4 x0 = *reinterpret_cast<const float4*>(xs + t * K + xs_pos(i, 0, nu));
         const float4 x1 = *reinterpret_cast<const float4*>(xs + t * K + xs_pos(i, 1, nu));
@@ -171,12 +173,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) dense_gemv_kernel(const __
     // the row is complete: reduce across the warp (every lane gets the sums), store or keep the best
     const int r = wg + q * nw;
 #pragma unroll
-    for (int t = 0; t < kStackMaxT; ++t) acc[t] = warp_sum(acc[t]);
+    for (int t = 0; t < MT; ++t) acc[t] = warp_sum(acc[t]);
     if (EPI == EPI_BF16) {
       if (lane < T) {
         float v = acc[0];
 #pragma unroll
-        for (int t = 1; t < kStackMaxT; ++t)
+        for (int t = 1; t < MT; ++t)
           if (lane == t) v = acc[t];
         if (r < g.n0) g.y0[(int64_t)lane * g.n0 + r] = f2bf(v);
         else g.y1[(int64_t)lane * (N - g.n0) + (r - g.n0)] = f2bf(v);
@@ -190,7 +192,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) dense_gemv_kernel(const __
       }
     }
 #pragma unroll
-    for (int t = 0; t < kStackMaxT; ++t) acc[t] = 0.f;
+    for (int t = 0; t < MT; ++t) acc[t] = 0.f;
   };
   for (int c = 0; c < nch; c += 2) {
     compute(wa, c);
@@ -542,21 +544,27 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaS
   return launched(cudaLaunchKernelExC(&cfg, fn, args));
 }
 
-template <int EPI>
-cudaError_t launch_gemv(const GemvArgs& g, int max_ctas, cudaStream_t s) {
+template <int EPI, int MT>
+cudaError_t launch_gemv_t(const GemvArgs& g, int max_ctas, cudaStream_t s) {
   const size_t smem = (size_t)g.T * g.K * 4;
   static size_t granted = 0;
   // past 48 KB of dynamic plus static shared memory (the kernel's few reduction slots) a launch needs the opt-in
   if (smem + 1024 > 48 * 1024 && smem > granted) {
-    cudaError_t e = cudaFuncSetAttribute(dense_gemv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e =
+        cudaFuncSetAttribute(dense_gemv_kernel<EPI, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     granted = smem;
   }
   const int ctas = std::max(1, std::min(max_ctas, (g.N + kGemvWarps - 1) / kGemvWarps));  // a row per warp at least
   GemvArgs a = g;
   void* args[] = {&a};
-  return launch_pdl(reinterpret_cast<const void*>(dense_gemv_kernel<EPI>), dim3(ctas), dim3(kGemvWarps * 32), smem,
+  return launch_pdl(reinterpret_cast<const void*>(dense_gemv_kernel<EPI, MT>), dim3(ctas), dim3(kGemvWarps * 32), smem,
                     s, args);
+}
+
+template <int EPI>
+cudaError_t launch_gemv(const GemvArgs& g, int max_ctas, cudaStream_t s) {
+  return g.T == 1 ? launch_gemv_t<EPI, 1>(g, max_ctas, s) : launch_gemv_t<EPI, kStackMaxT>(g, max_ctas, s);
 }
 
 struct AttnWs {
