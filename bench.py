@@ -19,7 +19,8 @@ Further objects on the same line:
                   the whole block, its own e2e and clocks, and the C oracle on a bounded token sample;
   e2e             the headline steps with each step's input (hidden fp32, attn_out bf16) copied from pinned host
                   memory and its outputs (hidden, normed) copied back inside the timed region, one copy each way
-                  (the tensors sit back to back in one device buffer);
+                  (the tensors sit back to back in one device buffer), the copies on their own streams over two
+                  buffer sets so that they overlap the neighbouring steps' kernels;
   ep_prefill      BASELINE config 5: 16384 tokens per step through one int4 MoE layer, the 256 experts sharded over
                   the N ranks (N = 1: the single-GPU prefill block; N > 1: mvcc_b200.ep, records and partial rows
                   moved by the kernels' peer-memory stores (or NCCL all-to-all with --ep-exchange nccl), each
@@ -270,18 +271,54 @@ def packed_io(hidden, attn, normed):
 
 def e2e_time(block_at, hidden, attn, normed, K, stream, world):
     """The same steps fed from pinned host memory: inside the timed region, every step copies its inputs (attn_out
-    + hidden, one contiguous range) host-to-device and its results (hidden + normed) device-to-host."""
-    _, a_v, h_v, n_v, inp, out = packed_io(hidden, attn, normed)
-    host_in = inp.cpu().pin_memory()
-    host_out = torch.empty(out.numel(), dtype=torch.uint8).pin_memory()
+    + hidden, one contiguous range) host-to-device and its results (hidden + normed) device-to-host. As a server
+    would, the copies run on their own streams over two device buffer sets: step i + 1's inputs land while step i
+    computes and step i's results leave while step i + 1 computes (a step's inputs do not depend on the previous
+    step's results here). Every step's two copies are inside the timed region."""
+    sets = [packed_io(hidden, attn, normed) for _ in range(2)]
+    host_in = sets[0][4].cpu().pin_memory()
+    host_out = [torch.empty(sets[0][5].numel(), dtype=torch.uint8).pin_memory() for _ in range(2)]
+    dev = hidden.device
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    fork = torch.cuda.Event()
+    ready = [torch.cuda.Event() for _ in range(2)]     # a set's inputs have landed
+    computed = [torch.cuda.Event() for _ in range(2)]  # a set's step has run
+    drained = [torch.cuda.Event() for _ in range(2)]   # a set's results have left
 
-    def step(i):
-        inp.copy_(host_in, non_blocking=True)
-        block_at(i).forward(h_v, a_v, n_v, stream=stream)
-        host_out.copy_(out, non_blocking=True)
+    def steps(n):
+        fork.record(stream)
+        s_in.wait_event(fork)
+        s_out.wait_event(fork)
+        for i in range(n):
+            b = i % 2
+            _, a_v, h_v, n_v, inp, out = sets[b]
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(drained[b])  # step i - 2's results have left this set
+                inp.copy_(host_in, non_blocking=True)
+                ready[b].record(s_in)
+            stream.wait_event(ready[b])
+            block_at(i).forward(h_v, a_v, n_v, stream=stream)
+            computed[b].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(computed[b])
+                host_out[b].copy_(out, non_blocking=True)
+                drained[b].record(s_out)
+        stream.wait_event(drained[(n - 1) % 2])  # join: the last results (s_out runs in order)
+        stream.wait_event(ready[(n - 1) % 2])
 
-    ms, _ = timed(graph_plan(step, K, stream), stream, world)
-    return ms, host_in.numel(), host_out.numel()
+    def cap(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            steps(n)
+        return g
+
+    S = min(K, GRAPH_STEPS)
+    plan = [(cap(S), K // S)] + ([(cap(K % S), 1)] if K % S else [])
+    run_graphs([(plan[0][0], 1)], stream)  # upload, untimed
+    torch.cuda.synchronize()
+    ms, _ = timed(plan, stream, world)
+    return ms, host_in.numel(), host_out[0].numel()
 
 
 def launches_per_step(T, fused_max=7, prefill_min=8, chunk=16):

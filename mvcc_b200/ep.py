@@ -339,7 +339,8 @@ class ExpertParallelMoe:
     """The expert-parallel MoE layer of one rank: `forward` is MoeBlock.forward for this rank's tokens, with the
     routed experts sharded over the process group."""
 
-    def __init__(self, layer: MoeLayer, max_tokens: int, group=None, rank=None, world=None, exchange="peers"):
+    def __init__(self, layer: MoeLayer, max_tokens: int, group=None, rank=None, world=None, exchange="peers",
+                 liveness_s=None):
         """exchange: "peers" (records and partial rows stored by the kernels into the peers' buffers over NVLink,
         CUDA IPC mappings set up here) or "nccl" (all_to_all_single of packed buffers, one host read per step)."""
         import torch.distributed as dist
@@ -348,6 +349,16 @@ class ExpertParallelMoe:
         self.world = dist.get_world_size(group) if world is None else world
         self.state = EpRank(layer, self.rank, self.world, max_tokens)
         self.mode = exchange
+        # liveness_s (optional): before every step each rank posts a key to the process group's store and waits at
+        # most this long for every peer's: a rank that has left is found on the host, before any collective of the
+        # step is launched (a collective waiting for a peer that is gone would hold its GPU until the group's
+        # timeout, or for good where the timeout cannot end it)
+        self.liveness_s = liveness_s
+        self._steps = 0
+        self._store = None
+        if liveness_s is not None:
+            from torch.distributed import distributed_c10d as c10d
+            self._store = c10d._get_default_store()
         self.exchange = NcclExchange(group)
         self.flag = torch.zeros(1, device=self.state.device)
         if exchange == "peers":
@@ -355,7 +366,24 @@ class ExpertParallelMoe:
         elif exchange != "nccl":
             raise ValueError(f"unknown exchange {exchange!r}")
 
+    def _check_peers(self):
+        """Every rank reaches step k or this rank raises EpError (the store's wait runs out)."""
+        import datetime
+        k = self._steps
+        self._steps += 1
+        st = self._store
+        st.set(f"mvcc_ep/{k}/{self.rank}", "1")
+        try:
+            st.wait([f"mvcc_ep/{k}/{d}" for d in range(self.world)], datetime.timedelta(seconds=self.liveness_s))
+        except Exception as e:  # noqa: BLE001 -- the store raises its own timeout / connection errors
+            raise EpError(f"rank {self.rank}: expert-parallel step {k} not reached by every rank within "
+                          f"{self.liveness_s} s ({e})") from e
+        if k >= 2:
+            st.delete_key(f"mvcc_ep/{k - 2}/{self.rank}")
+
     def forward(self, hidden, attn_out, normed, next_rms1=None, stream=None):
+        if self._store is not None:
+            self._check_peers()
         if self.mode == "peers":
             return ep_step_peers(self.state, hidden, attn_out, normed, next_rms1, stream, self.group, self.flag)
         return ep_step(self.state, self.exchange, hidden, attn_out, normed, next_rms1, stream)

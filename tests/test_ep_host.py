@@ -232,3 +232,54 @@ def test_missing_rank_ends_the_step_with_an_error(mode):
     for rank, out, dt in res[:-1]:
         assert out.startswith("EpError: ") and "count exchange" in out, res
         assert dt < 3 * PG_TIMEOUT_S + 10, res  # bounded by the group's timeout, not a hang
+
+
+def liveness_worker(rank, world, port, q):
+    """ExpertParallelMoe's step-entry liveness check, alone (no device state): every rank passes step 0, the last rank
+    then leaves; the others must raise EpError at step 1 within the check's bound."""
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from torch.distributed import distributed_c10d as c10d
+
+    from mvcc_b200.ep import EpError, ExpertParallelMoe
+    moe = object.__new__(ExpertParallelMoe)  # the check only: no layer, no device buffers
+    moe.rank, moe.world, moe.liveness_s, moe._steps, moe._store = rank, world, 2, 0, c10d._get_default_store()
+    moe._check_peers()  # step 0: everyone arrives
+    if rank == world - 1:
+        q.put((rank, "left", 0.0))
+        q.close()
+        q.join_thread()
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        moe._check_peers()
+        out = "passed"
+    except EpError as e:
+        out = f"EpError: {e}"
+    q.put((rank, out, time.monotonic() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_liveness_check_finds_a_rank_that_left_before_any_collective():
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=liveness_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=120) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.exitcode is None:
+                p.kill()
+    assert res[-1][:2] == (world - 1, "left"), res
+    for rank, out, dt in res[:-1]:
+        assert out.startswith("EpError: ") and "step 1 not reached" in out, res
+        assert dt < 2 + 10, res
