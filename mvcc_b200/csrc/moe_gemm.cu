@@ -273,6 +273,22 @@ __device__ __forceinline__ GemmTile load_tile(const GemmParams& p, int ti) {
   return t;
 }
 
+// Position in a ring of n stages: the stage, the parity of its current use and whether the ring has wrapped (the
+// stage's previous use must be released first). Kept incrementally: g % n and g / n are runtime divisions, about
+// twenty instructions each, in every role's per-k-step loop.
+struct Ring {
+  int s = 0;
+  uint32_t ph = 0;
+  bool reused = false;
+  __device__ __forceinline__ void next(int n) {
+    if (++s == n) {
+      s = 0;
+      ph ^= 1u;
+      reused = true;
+    }
+  }
+};
+
 template <int BN, bool INT4, int EPI, int NDW, int MS>
 __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
     moe_gemm_kernel(const __grid_constant__ GemmParams p, const __grid_constant__ CUtensorMap tmA,
@@ -333,14 +349,14 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
     // ---- A producers
     if (c.a_tma) {
       if (warp == 0 && lane == 0) {
-        int g = 0;
+        Ring ra;
         bool ok = true;
         for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
           const GemmTile t = load_tile<MS>(p, it / nN);
           const int nsub = MS > 1 && t.mcount > kTileM ? MS : 1;
-          for (int kt = 0; kt < nk; ++kt, ++g) {
-            const int s = g % SA;
-            if (g >= SA && !wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+          for (int kt = 0; kt < nk; ++kt, ra.next(SA)) {
+            const int s = ra.s;
+            if (ra.reused && !wait_bar(&empty[s], ra.ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
             mbar_expect_tx(&full[s], (uint32_t)nsub * kSubBytes);
             for (int u = 0; u < nsub; ++u)
               tma_load_2d(smem + c.a + ((size_t)s * MS + u) * kSubBytes, &tmA, kt * kBK, t.m0 + u * kTileM,
@@ -352,7 +368,7 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
       // gathered rows: lane l of the 64 fetches 16-byte chunk l % 8 of rows l / 8 + 8 i (i < 16 MS), so that each
       // warp instruction covers four whole 128-byte rows; sub-tile u's rows land kSubBytes further on
       const int t64 = threadIdx.x, ch = t64 & 7, r0 = t64 >> 3;
-      int g = 0;
+      Ring ra;
       bool ok = true;
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
         const GemmTile t = load_tile<MS>(p, it / nN);
@@ -367,9 +383,9 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
             soff[i] = (int)((int64_t)src * p.lda) + ch * 8;
           }
         }
-        for (int kt = 0; kt < nk; ++kt, ++g) {
-          const int s = g % SA;
-          if (g >= SA && !wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+        for (int kt = 0; kt < nk; ++kt, ra.next(SA)) {
+          const int s = ra.s;
+          if (ra.reused && !wait_bar(&empty[s], ra.ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           uint8_t* dst = smem + c.a + (size_t)s * MS * kSubBytes;
 #pragma unroll
           for (int i = 0; i < 16 * MS; ++i) {
@@ -385,7 +401,8 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
   } else if (warp == 2) {
     // ---- B producer: lane 0 issues the TMA tiles; all lanes copy scales when their rows are under 16 bytes
     constexpr int HB = BN / 2;
-    int g = 0, j = 0;
+    Ring rr, rb;  // the raw ring (INT4) or the A + B ring (bf16 B); lane 0 issues
+    int j = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
       const GemmTile t = load_tile<MS>(p, it / nN);
@@ -422,9 +439,9 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
         }
         if (lane == 0) {
           const int RB = 32 * c.rk;
-          for (int kt = 0; kt < nk; kt += c.rk, g += c.rk) {
-            const int gr = g / c.rk, s = gr % SR;
-            if (gr >= SR && !wait_bar(&freeR[s], ((gr / SR) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+          for (int kt = 0; kt < nk; kt += c.rk, rr.next(SR)) {
+            const int s = rr.s;
+            if (rr.reused && !wait_bar(&freeR[s], rr.ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
             uint8_t* dst = smem + c.raw + (size_t)s * BN * RB;
             mbar_expect_tx(&fullR[s], (uint32_t)(BN * RB));
             if (p.paired) tma_load_4d(dst, &tmB, kt * 32, nt * HB, 0, t.e, &fullR[s]);
@@ -433,9 +450,9 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
         }
       } else {
         if (lane == 0) {
-          for (int kt = 0; kt < nk; ++kt, ++g) {
-            const int s = g % SA;
-            if (g >= SA && !wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+          for (int kt = 0; kt < nk; ++kt, rb.next(SA)) {
+            const int s = rb.s;
+            if (rb.reused && !wait_bar(&empty[s], rb.ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
             uint8_t* dst = smem + c.b + (size_t)s * BN * 128;
             mbar_expect_tx(&full[s], (uint32_t)(BN * 128));
             if (p.paired) tma_load_4d(dst, &tmB, kt * kBK, nt * HB, 0, t.e, &full[s]);
@@ -443,7 +460,6 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
           }
         }
       }
-      g = __shfl_sync(0xffffffffu, g, 0);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -451,8 +467,12 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
     // ---- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(kTileM, BN);
-      int g = 0, j = 0;
+      Ring ra;
+      int j = 0;
       bool ok = true;
+      // shared-memory descriptors of stage 0; a stage, sub-tile or K step is an offset added to the start-address
+      // field (bits [0,14) hold address >> 4, and every address here stays below 256 KB, so no carry leaves it)
+      const uint64_t a_desc0 = sw128_desc(smem_u32(smem + c.a)), b_desc0 = sw128_desc(smem_u32(smem + c.b));
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
         const int ab = j % NB, use = j / NB;
         if (use >= 1 && !wait_bar(&acc_empty[ab], (use - 1) & 1, abort_flag, p.err)) break;
@@ -460,20 +480,20 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
         // sub-tiles past the tile's rows are neither loaded nor multiplied (their epilogue warps skip them)
         const int nsub = MS > 1 && load_tile<MS>(p, it / nN).mcount > kTileM ? MS : 1;
         const uint32_t d = tmem + (uint32_t)(ab * MS * BN);
-        for (int kt = 0; kt < nk; ++kt, ++g) {
-          const int s = g % SA;
-          ok = wait_bar(&full[s], (g / SA) & 1, abort_flag, p.err);
+        for (int kt = 0; kt < nk; ++kt, ra.next(SA)) {
+          const int s = ra.s;
+          ok = wait_bar(&full[s], ra.ph, abort_flag, p.err);
           if (!ok) break;
           fence_after_sync();
-          const uint32_t a_addr = smem_u32(smem + c.a + (size_t)s * MS * kSubBytes);
-          const uint32_t b_addr = smem_u32(smem + c.b + (size_t)s * BN * 128);
+          const uint64_t ad = a_desc0 + (uint64_t)((s * MS * kSubBytes) >> 4);
+          const uint64_t bd = b_desc0 + (uint64_t)((s * BN * 128) >> 4);
 #pragma unroll
           for (int u = 0; u < MS; ++u) {
             if (u >= nsub) break;
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)
-              mma_bf16(d + (uint32_t)(u * BN), sw128_desc(a_addr + u * kSubBytes + kk * 32),
-                       sw128_desc(b_addr + kk * 32), idesc, (kt | kk) != 0);
+              mma_bf16(d + (uint32_t)(u * BN), ad + (uint64_t)((u * kSubBytes + kk * 32) >> 4),
+                       bd + (uint64_t)((kk * 32) >> 4), idesc, (kt | kk) != 0);
           }
           mma_commit(&empty[s]);
         }
@@ -596,8 +616,9 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
     // td + kDeqThreads * j
     constexpr int J = (BN * 2 + kDeqThreads - 1) / kDeqThreads;  // jobs per thread (2 at BN = 256, NDW = 8)
     const int td = threadIdx.x - kDeqWarp0 * 32;
-    const int RB = 32 * c.rk;
-    int g = 0, j = 0;
+    const int RB = 32 * c.rk, gsh = __ffs(p.G) - 1;  // G is 32, 64 or 128
+    Ring rr, ra;  // the raw ring (advanced every rk k-steps) and the A + B ring
+    int sub = 0, j = 0;  // k-step within the raw stage
     bool ok = true;
     for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++j) {
       const int sbuf = j % NSC;
@@ -615,10 +636,10 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
         sreg[jj] = make_uint2(0, 0);
         sbase[jj] = -(1 << 20);
       }
-      for (int kt = 0; kt < nk; ++kt, ++g) {
-        const int gr = g / c.rk, sr = gr % SR, sub = g - gr * c.rk, s = g % SA;
-        ok = wait_bar(&fullR[sr], (gr / SR) & 1, abort_flag, p.err);
-        ok = ok && (g < SA || wait_bar(&empty[s], ((g / SA) - 1) & 1, abort_flag, p.err));
+      for (int kt = 0; kt < nk; ++kt) {
+        const int sr = rr.s, s = ra.s;
+        ok = wait_bar(&fullR[sr], rr.ph, abort_flag, p.err);
+        ok = ok && (!ra.reused || wait_bar(&empty[s], ra.ph ^ 1u, abort_flag, p.err));
         if (!ok) break;
         __syncwarp();  // lane 0's arrives of the previous step can leave the warp split until here
         const uint8_t* rawp = smem + c.raw + (size_t)sr * BN * RB + sub * 32;
@@ -628,7 +649,7 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
           const int job = td + kDeqThreads * jj, r = job >> 1, h = job & 1;
           if (job >= BN * 2) continue;
           const uint4 w = *reinterpret_cast<const uint4*>(rawp + r * RB + h * 16);
-          const int gi = (kt * kBK + h * 32) / p.G;  // this job's group scale
+          const int gi = (kt * kBK + h * 32) >> gsh;  // this job's group scale
           float sv;
           if (wide) {
             if (gi < sbase[jj] || gi >= sbase[jj] + 4) {
@@ -653,6 +674,11 @@ __global__ void __launch_bounds__(gemm_threads(NDW, MS), 1)
           if (sub == c.rk - 1) mbar_arrive(&freeR[sr]);  // the raw stage's last k-step
           mbar_arrive(&full[s]);
         }
+        if (++sub == c.rk) {
+          sub = 0;
+          rr.next(SR);
+        }
+        ra.next(SA);
       }
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(&sc_free[sbuf]);
