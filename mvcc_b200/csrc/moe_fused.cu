@@ -767,7 +767,15 @@ __global__ void __launch_bounds__(kFThreads, 1) moe_fused_decode_kernel(FusedArg
     }
     release(c);
   }
-  if (live && hw < h1 && __all_sync(0xffffffffu, bar_wait(&sbar, 0))) {
+  bool sdn_ok = live && hw < h1;
+  if (sdn_ok) {
+    sdn_ok = __all_sync(0xffffffffu, bar_wait(&sbar, 0));
+    if (!sdn_ok && lane == 0) {  // this warp's output row is not written: the call's results are invalid
+      atomicOr(a.err, (uint32_t)MOE_ERR_BARRIER);
+      abort_s = 1;
+    }
+  }
+  if (sdn_ok) {
     float routed_t = 0.f, shared_t = 0.f;
     for (int t = 0; t < T; ++t) {
       const float v = warp_sum(acc_w[t * 32 + lane]);

@@ -161,9 +161,11 @@ PG_TIMEOUT_S = 4
 def failing_worker(rank, world, port, q, mode):
     import datetime
     import time
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=PG_TIMEOUT_S))
+    # the rendezvous gets a long timeout of its own (spawned ranks may take seconds to import torch); the short
+    # group timeout bounds the collectives of the step
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=120))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=PG_TIMEOUT_S))
     from mvcc_b200.ep import EpError, NcclExchange, ep_step
     x = np.random.default_rng(rank).standard_normal((5 + rank, H)).astype(np.float32)
     st = HostRank(rank, world, max_tokens=16)
