@@ -64,6 +64,7 @@ __host__ __device__ constexpr int deq_warp0(int ms) { return 4 + 4 * ms; }
 __host__ __device__ constexpr int gemm_threads(int ndw, int ms) { return (deq_warp0(ms) + ndw) * 32; }
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far beyond any item's main loop
 constexpr uint32_t kMinPolls = 1u << 18;               // polls before a wait may give up at all
+constexpr uint32_t kMaxPolls = 1u << 26;               // polls after which a wait gives up whatever the timer says
 
 struct GemmCfg {
   int bn, sa;            // BN, A + B ring depth
@@ -151,7 +152,8 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // Wait for the phase with the given parity; bounded in time (kWaitNs from the first miss, and at least kMinPolls
 // polls: %globaltimer may step when the driver re-aligns it, so a step backwards restarts the interval and a step
-// forwards alone cannot end a wait), and gives up early when another role of the CTA has aborted.
+// forwards alone cannot end a wait) and in polls (kMaxPolls, should the timer stand still), and gives up early when
+// another role of the CTA has aborted.
 __device__ __forceinline__ bool wait_bar(uint64_t* mbar, uint32_t parity, volatile int* abort_flag, uint32_t* err) {
   const uint32_t a = smem_u32(mbar);
   unsigned long long t0 = 0;
@@ -173,7 +175,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t* mbar, uint32_t parity, volati
       const long long dt = (long long)(now - t0);
       if (t0 == 0 || dt < 0) {
         t0 = now;
-      } else if (i >= kMinPolls && dt > (long long)kWaitNs) {
+      } else if ((i >= kMinPolls && dt > (long long)kWaitNs) || i >= kMaxPolls) {
         *abort_flag = 1;
         if (err) atomicOr(err, (uint32_t)MOE_ERR_TIMEOUT);
         return false;

@@ -17,6 +17,7 @@ using tc::smem_u32;
 constexpr long long kSpinLimit = 1 << 21;          // grid-barrier polls (x ~100 ns) before giving up
 constexpr unsigned long long kWaitNs = 1000000000; // stage-barrier wait limit (1 s of global time)
 constexpr int kMinPolls = 1 << 18;                 // stage-barrier polls before a wait may give up at all
+constexpr int kMaxPolls = 1 << 26;                 // stage-barrier polls after which a wait gives up whatever the timer
 
 // ------------------------------------------------------------------ bulk copies and barriers
 
@@ -49,9 +50,10 @@ __device__ __forceinline__ unsigned long long gtime() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Waits for phase `parity` of the mbarrier; false once kWaitNs of global time and kMinPolls polls have both passed.
-// %globaltimer is not guaranteed monotone (the driver may re-align it with the host clock), so the elapsed time is
-// taken signed, a step backwards restarts the interval, and a step forwards alone cannot end a wait.
+// Waits for phase `parity` of the mbarrier; false once kWaitNs of global time and kMinPolls polls have both passed,
+// or after kMaxPolls polls. %globaltimer is not guaranteed monotone (the driver may re-align it with the host clock),
+// so the elapsed time is taken signed, a step backwards restarts the interval, a step forwards alone cannot end a
+// wait, and the poll cap ends it even if the timer stood still.
 __device__ __forceinline__ bool bar_wait(uint64_t* mbar, uint32_t parity) {
   const uint32_t addr = smem_u32(mbar);
   unsigned long long t0 = 0;
@@ -69,7 +71,7 @@ __device__ __forceinline__ bool bar_wait(uint64_t* mbar, uint32_t parity) {
       const unsigned long long t = gtime();
       const long long dt = (long long)(t - t0);
       if (i == 0 || dt < 0) t0 = t;
-      else if (i >= kMinPolls && dt > (long long)kWaitNs) return false;
+      else if ((i >= kMinPolls && dt > (long long)kWaitNs) || i >= kMaxPolls) return false;
     }
   }
 }
