@@ -469,7 +469,15 @@ __global__ void __launch_bounds__(kLThreads, 1) moe_lean_decode_kernel(const __g
       }
     }
   }
-  if (live && __all_sync(0xffffffffu, bar_wait(&sbar, 0))) {
+  bool sdn_ok = live;
+  if (sdn_ok) {
+    sdn_ok = __all_sync(0xffffffffu, bar_wait(&sbar, 0));
+    if (!sdn_ok && lane == 0) {  // this warp's output row is not written: the call's results are invalid
+      atomicOr(a.err, (uint32_t)MOE_ERR_BARRIER);
+      abort_s = 1;
+    }
+  }
+  if (sdn_ok) {
     const float rt0 = warp_sum(acc0), rt1 = warp_sum(acc1);
     const float routed_t = lane == 0 ? rt0 : rt1;
     const uint8_t* srow = sdn + (size_t)(hw - h0) * Is * 2;
