@@ -90,9 +90,10 @@ typedef struct moe_stats {
 MOE_API void moe_stats_get(moe_stats* out);
 MOE_API void moe_stats_reset(void);
 
-/* Error-word bits. MOE_ERR_BARRIER: a grid barrier of the fused decode kernel gave up waiting (bounded spin); the
- * call's results are invalid and the workspace must be re-initialised with moe_workspace_init. MOE_ERR_TIMEOUT: a
- * bounded pipeline wait inside a prefill GEMM tile gave up; that call's results are invalid. */
+/* Error-word bits. MOE_ERR_BARRIER: a grid barrier or a weight-copy wait of the fused decode kernel gave up waiting
+ * (bounded); the call's results are invalid and the workspace must be re-initialised with moe_workspace_init.
+ * MOE_ERR_TIMEOUT: a bounded pipeline wait inside a prefill GEMM tile, or a cache-copy wait of the attention kernel,
+ * gave up; that call's results are invalid. */
 enum moe_errc { MOE_ERR_NONE = 0, MOE_ERR_EXPERT_INDEX = 1, MOE_ERR_SHAPE = 2, MOE_ERR_BARRIER = 4, MOE_ERR_TIMEOUT = 8 };
 
 /* The whole block, replacing qwen.cu:429-448 for one layer:
