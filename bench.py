@@ -1,5 +1,6 @@
 #!/usr/bin/env python3
-"""bench.py -- throughput of the B200 MoE block on BASELINE configs 2 (int4 decode) and 4 (Zipf-skewed prefill).
+"""bench.py -- throughput of the B200 MoE block on BASELINE configs 2 (int4 decode), 3 (the 40-layer decode stack),
+4 (Zipf-skewed prefill) and 5 (expert-parallel prefill).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference] [--quick]
 
@@ -13,7 +14,16 @@ graphs and timed with CUDA events on the launching stream, bracketed by barrier 
 Further objects on the same line:
   roofline        the dominant kernel of the headline step (the fused decode kernel: the whole block is one launch
                   for B < 8), algorithmic block bytes per launch over its mean duration from graph-captured events;
-  decode_batches  the other batch sizes of config 2 (1, 4, 16) on the default path selection;
+  expert_gemv, block
+                  the headline step's expert-weight bytes and whole-block bytes over its time, as fractions of the
+                  measured HBM peak;
+  decode_batches  the other batch sizes of config 2 (1, 4, 16) on the default path selection, and batches 8 and 16
+                  on the decode kernels (decode numerics) beside the default's tile path;
+  g128            the library on group-128 layers (the group the reference's kernels hard-code), timed as the
+                  reference arm's `ref_gpu` object times the reference's own kernels: decode batches 1-16 and the
+                  routed experts of a 4096-token prefill (N = 1);
+  decode_stack    BASELINE config 3: one token through 40 x (attention over a 4096-token cache, MoE block) and the
+                  LM head with argmax, one CUDA graph per token, with the attention / MoE / LM-head split;
   prefill         BASELINE config 4: 4096 tokens through one layer with the per-expert Zipf(1.1) router bias:
                   tok/s, the tensor-pipe roofline of its dominant kernel (the routed gate/up grouped GEMM) and of
                   the whole block, its own e2e and clocks, and the C oracle on a bounded token sample;
