@@ -362,14 +362,18 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const __grid_constant__
                                 (uint32_t)f2bf(v[2]) | ((uint32_t)f2bf(v[3]) << 16),
                                 (uint32_t)f2bf(v[4]) | ((uint32_t)f2bf(v[5]) << 16),
                                 (uint32_t)f2bf(v[6]) | ((uint32_t)f2bf(v[7]) << 16));
-    *reinterpret_cast<uint4*>(ks + (size_t)(p - k0) * D * 2 + lane * 16) = ko;
-    *reinterpret_cast<uint4*>(vs + (size_t)(p - k0) * D * 2 + lane * 16) = vr;
+    if (ok) {  // after a wait that gave up the copies may still land here: leave the stage to them
+      *reinterpret_cast<uint4*>(ks + (size_t)(p - k0) * D * 2 + lane * 16) = ko;
+      *reinterpret_cast<uint4*>(vs + (size_t)(p - k0) * D * 2 + lane * 16) = vr;
+    }
     if (tn == t) {
       reinterpret_cast<uint4*>(a.kc + ((int64_t)kvh * a.ctx + p) * D)[lane] = ko;
       reinterpret_cast<uint4*>(a.vc + ((int64_t)kvh * a.ctx + p) * D)[lane] = vr;
     }
   }
   __syncthreads();
+  // no copy may still be landing when the CTA exits: after a wait that gave up, thread 0 waits once more (bounded)
+  if (!ok && threadIdx.x == 0) bar_wait(&kvbar, 0);
   if (warp >= G) return;
   const int h = kvh * G + warp;
   float m = -1e30f, l = 0.f, acc[8];
