@@ -36,9 +36,15 @@ typedef struct moe_attn_weights {
 } moe_attn_weights;
 
 /* Bytes of caller-owned workspace for attention calls of up to max_T tokens over a cache of ctx positions; 0 for an
- * unsupported geometry. One workspace per concurrently running call (it holds the qkv, q, gate and o activations and
- * the split-K partials). */
+ * unsupported geometry. One workspace per concurrently running call (it holds an error word, the qkv, q, gate and o
+ * activations and the split-K partials). Zero it once before its first call (cudaMemset), as for the block's
+ * workspace: the calls set bits of the error word and never clear it. */
 MOE_API size_t moe_attn_workspace_bytes(const moe_attn_weights* w, int max_T, int ctx);
+
+/* Reads and clears the attention workspace's error word, synchronising the stream: MOE_ERR_TIMEOUT (include/
+ * moe_block.h) when a cache-copy wait of a call gave up (that call's attention output is invalid), else 0; a
+ * negative value is -cudaError. */
+MOE_API int moe_attn_workspace_error(void* workspace, size_t workspace_bytes, moe_stream_t stream);
 
 /* The attention branch of one layer (qwen.cu:413-425) for T new tokens at positions pos0 .. pos0 + T - 1:
  * qkv = normed . Wqkv^T (bf16); per-head RMSNorm of q and k heads and rotate-half RoPE over the first rope_dim dims

@@ -112,6 +112,7 @@ _SIGS = {
     "moe_ipc_close": (_I, [_P]),
     # attention layer, first-layer norm and LM head of a decode step (include/moe_stack.h)
     "moe_attn_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeAttnWeights), _I, _I]),
+    "moe_attn_workspace_error": (_I, [_P, ctypes.c_size_t, _P]),
     "moe_attn_forward": (_I, [ctypes.POINTER(MoeAttnWeights), _P, _P, _I, _I, _P, _P, _I, _P, ctypes.c_size_t, _P]),
     "moe_attn_forward_rms": (_I, [ctypes.POINTER(MoeAttnWeights), _P, _P, _P, _P, _I, _I, _P, _I, _P, ctypes.c_size_t,
                                   _P]),

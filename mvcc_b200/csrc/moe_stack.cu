@@ -581,11 +581,11 @@ AttnWs attn_ws(const moe_attn_weights* w, int max_T, int ctx) {
   size_t off = 0;
   const int nq = w->Hq * w->D, nqkv = (w->Hq + 2 * w->Hkv) * w->D;
   L.nsplit_max = (ctx + 15) / 16;
+  L.err = off;  off = ws_align(off + 4);  // first, so that its offset does not depend on T or ctx
   L.qkv = off;  off = ws_align(off + (size_t)max_T * nqkv * 2);
   L.z = off;    off = ws_align(off + (w->gate ? (size_t)max_T * nq * 2 : 0));
   L.o = off;    off = ws_align(off + (size_t)max_T * nq * 2);
   L.part = off; off = ws_align(off + (size_t)max_T * w->Hq * L.nsplit_max * part_stride(w->D) * 4);
-  L.err = off;  off = ws_align(off + 4);
   L.total = off;
   return L;
 }
@@ -611,6 +611,18 @@ extern "C" {
 size_t moe_attn_workspace_bytes(const moe_attn_weights* w, int max_T, int ctx) {
   if (!attn_ok(w) || max_T < 1 || max_T > kStackMaxT || ctx < 1) return 0;
   return attn_ws(w, max_T, ctx).total;
+}
+
+int moe_attn_workspace_error(void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  if (!workspace || workspace_bytes < 4 || !al16(workspace)) return -(int)cudaErrorInvalidValue;
+  uint32_t* errp = static_cast<uint32_t*>(workspace);  // the error word leads the layout (attn_ws)
+  uint32_t v = 0;
+  const cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(&v, errp, sizeof v, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(errp, 0, sizeof v, s);
+  if (e != cudaSuccess) return -(int)e;
+  return (int)v;
 }
 
 }  // extern "C"

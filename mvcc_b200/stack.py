@@ -81,6 +81,13 @@ class AttnBlock:
                                      _ptr(normed), _ptr(attn_out), T, _ptr(self.ws), self.ws.numel(),
                                      _stream(stream)), "moe_attn_forward")
 
+    def error_word(self, stream=None):
+        """Reads and clears the workspace's error word (MOE_ERR_TIMEOUT: a cache-copy wait gave up)."""
+        rc = _lib.moe_attn_workspace_error(_ptr(self.ws), self.ws.numel(), _stream(stream))
+        if rc < 0:
+            raise RuntimeError(f"moe_attn_workspace_error failed: cudaError {-rc}")
+        return rc
+
     def forward_rms(self, hidden, rms1, attn_out, pos0, T=None, stream=None):
         """forward() with the layer's input RMSNorm fused in: hidden fp32 [T,H] normalised with rms1 (bf16 bits [H])
         inside the first GEMV (moe_attn_forward_rms)."""

@@ -83,6 +83,10 @@ def test_entry_points_reject_bad_arguments_before_launch():
     assert lib.moe_router_topk(ctypes.byref(w), ctypes.c_void_p(256), 1 << 30, None, None, None, None, 0, None) == 1
     # misaligned workspace
     assert lib.moe_shared_expert(ctypes.byref(w), ctypes.c_void_p(8), 1 << 30, None, None, 1, None) == 1
+    # the attention workspace's error-word reader: null, too small or misaligned workspaces
+    assert lib.moe_attn_workspace_error(None, 1 << 20, None) == -1
+    assert lib.moe_attn_workspace_error(ctypes.c_void_p(256), 2, None) == -1
+    assert lib.moe_attn_workspace_error(ctypes.c_void_p(8), 1 << 20, None) == -1
 
 
 def test_expert_bytes_match_reference_formula():

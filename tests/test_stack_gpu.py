@@ -53,6 +53,7 @@ def test_attention_layer_against_oracle(gate, ctx, pos0, T):
     keep = np.ones(ctx, bool)
     keep[new] = False
     assert np.array_equal(kg[:, keep], kc0[:, keep]) and np.array_equal(vg[:, keep], vc0[:, keep])
+    assert blk.error_word() == 0
 
 
 def test_attention_rejects_bad_shapes():
