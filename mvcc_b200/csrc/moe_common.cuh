@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/moe_block.h"
 
 namespace moe {
@@ -158,6 +160,27 @@ void note_block_call();
 void note_pack_bytes(uint64_t n);
 inline cudaError_t launched(cudaError_t e) {
   if (e == cudaSuccess) note_launches(1);
+  return e;
+}
+
+// Raises a kernel's dynamic shared-memory limit on the current device to at least `bytes`, and to `floor_bytes` at
+// once so that later, larger requests rarely need another call; after a kernel's first launch on a device, its later
+// launches there (including those inside CUDA-graph capture) make no attribute call. Kernel attributes belong to
+// each device's context, so what was granted is recorded per device: a process that drives several GPUs raises each
+// kernel's limit on each of them. One SmemGrant per kernel instantiation, as a function-local static (zero at start).
+struct SmemGrant {
+  static constexpr int kDevices = 64;
+  std::atomic<size_t> dev[kDevices];
+};
+inline cudaError_t grant_smem(const void* kern, size_t bytes, size_t floor_bytes, SmemGrant& g) {
+  int d = 0;
+  cudaError_t e = cudaGetDevice(&d);
+  if (e != cudaSuccess) return e;
+  const bool kept = d >= 0 && d < SmemGrant::kDevices;  // devices past the table are raised on every launch
+  if (kept && bytes <= g.dev[d].load(std::memory_order_relaxed)) return cudaSuccess;
+  const size_t want = bytes > floor_bytes ? bytes : floor_bytes;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
+  if (e == cudaSuccess && kept) g.dev[d].store(want, std::memory_order_relaxed);
   return e;
 }
 

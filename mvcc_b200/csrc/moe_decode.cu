@@ -650,17 +650,12 @@ static int sm_count() {
   return n;
 }
 
-// Raises a kernel's dynamic shared-memory limit on its first launch, to at least 200 KB, so that later launches
-// (including those inside CUDA-graph capture) make no attribute calls. Raised even for small requests: the default
-// 48 KB limit covers static plus dynamic shared memory, so a dynamic request just under 48 KB can still exceed it.
-// `granted` is a static of the caller, one per kernel instantiation.
+// Raises a kernel's dynamic shared-memory limit on its first launch on a device, to at least 200 KB (grant_smem).
+// Raised even for small requests: the default 48 KB limit covers static plus dynamic shared memory, so a dynamic
+// request just under 48 KB can still exceed it. `granted` is a static of the caller, one per kernel instantiation.
 template <typename F>
-static cudaError_t set_smem(F* kern, size_t bytes, size_t& granted) {
-  if (bytes <= granted) return cudaSuccess;
-  const size_t want = std::max(bytes, (size_t)200 * 1024);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
-  if (e == cudaSuccess) granted = want;
-  return e;
+static cudaError_t set_smem(F* kern, size_t bytes, SmemGrant& granted) {
+  return grant_smem(reinterpret_cast<const void*>(kern), bytes, (size_t)200 * 1024, granted);
 }
 
 // Programmatic dependent launch is on unless the environment sets MOE_B200_PDL=0 (read once per process).
@@ -693,7 +688,7 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_
 
 template <int NB8>
 static cudaError_t route_dispatch(const BlockArgs& a, int flags, cudaStream_t s) {
-  static size_t granted = 0;
+  static SmemGrant granted;
   const size_t smem = (size_t)a.T * a.w.H * sizeof(uint16_t);
   cudaError_t err = set_smem(route_kernel<NB8>, smem, granted);
   if (err != cudaSuccess) return err;
@@ -714,7 +709,7 @@ cudaError_t launch_route_table(const BlockArgs& a, cudaStream_t s) {
 
 template <int NCL>
 static cudaError_t gate_up_dispatch(const BlockArgs& a, int flags, cudaStream_t s) {
-  static size_t granted = 0;
+  static SmemGrant granted;
   const size_t smem = gate_up_smem_bytes(a.T, a.w.H);
   cudaError_t err = set_smem(gate_up_kernel<NCL>, smem, granted);
   if (err != cudaSuccess) return err;
@@ -740,7 +735,7 @@ size_t down_smem_bytes(int T, int TOPK, int I, int Is, bool xf32) {
 
 template <int NCD, int NBS, bool XF32>
 static cudaError_t down_dispatch(const BlockArgs& a, int mode, cudaStream_t s) {
-  static size_t granted = 0;
+  static SmemGrant granted;
   const size_t smem = down_smem_bytes(a.T, a.w.TOPK, a.w.I, a.w.Is, XF32);
   cudaError_t err = set_smem(down_kernel<NCD, NBS, XF32>, smem, granted);
   if (err != cudaSuccess) return err;

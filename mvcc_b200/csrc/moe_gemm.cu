@@ -828,12 +828,11 @@ static cudaError_t launch_t(const GemmParams& p, int max_tiles, bool pdl, cudaSt
                                          (uint64_t)p.n_valid, (uint64_t)p.K * 2, kBK, rows_box, true);
     if (!okb) return cudaErrorInvalidValue;
   }
-  static size_t granted = 0;
-  if (c.total > granted) {
-    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<BN, INT4, EPI, NDW, MS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.total);
+  static SmemGrant granted;
+  {
+    cudaError_t e = grant_smem(reinterpret_cast<const void*>(moe_gemm_kernel<BN, INT4, EPI, NDW, MS>), c.total, 0,
+                               granted);
     if (e != cudaSuccess) return e;
-    granted = c.total;
   }
   static int sms = 0;
   if (!sms) sms = dev_attr(cudaDevAttrMultiProcessorCount, 148);

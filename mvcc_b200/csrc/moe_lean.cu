@@ -636,14 +636,9 @@ bool lean_config(const moe_layer_weights& w, int T) {
 cudaError_t launch_lean_decode(const BlockArgs& a, unsigned long long* gbar, bool next_norm, cudaStream_t s) {
   LeanCfg c;
   if (!lean_plan(a.w, a.T, &c)) return cudaErrorInvalidValue;
-  static size_t granted = 0;
-  if (c.smem > granted) {
-    const size_t want = std::max(c.smem, (size_t)160 * 1024);
-    cudaError_t e =
-        cudaFuncSetAttribute(moe_lean_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
-    if (e != cudaSuccess) return e;
-    granted = want;
-  }
+  static SmemGrant granted;
+  cudaError_t e = grant_smem(reinterpret_cast<const void*>(moe_lean_decode_kernel), c.smem, (size_t)160 * 1024, granted);
+  if (e != cudaSuccess) return e;
   LeanArgs f;
   memset(&f, 0, sizeof f);
   f.a = a;

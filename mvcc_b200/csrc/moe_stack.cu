@@ -551,13 +551,11 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaS
 template <int EPI, int MT>
 cudaError_t launch_gemv_t(const GemvArgs& g, int max_ctas, cudaStream_t s) {
   const size_t smem = (size_t)g.T * g.K * 4;
-  static size_t granted = 0;
+  static SmemGrant granted;
   // past 48 KB of dynamic plus static shared memory (the kernel's few reduction slots) a launch needs the opt-in
-  if (smem + 1024 > 48 * 1024 && smem > granted) {
-    cudaError_t e =
-        cudaFuncSetAttribute(dense_gemv_kernel<EPI, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem + 1024 > 48 * 1024) {
+    cudaError_t e = grant_smem(reinterpret_cast<const void*>(dense_gemv_kernel<EPI, MT>), smem, 0, granted);
     if (e != cudaSuccess) return e;
-    granted = smem;
   }
   const int ctas = std::max(1, std::min(max_ctas, (g.N + kGemvWarps - 1) / kGemvWarps));  // a row per warp at least
   GemvArgs a = g;
@@ -676,13 +674,9 @@ static int attn_forward(const moe_attn_weights* w, uint16_t* kc, uint16_t* vc, i
     nsplit = std::max(1, std::min(nsplit, L.nsplit_max));
     const int chunk = (nkeys + nsplit - 1) / nsplit;  // the longest token's chunk
     const size_t smem = (size_t)2 * chunk * w->D * 2;
-    static bool granted = false;
-    if (!granted) {
-      e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               2 * kAttnMaxChunk * 256 * 2);
-      if (e != cudaSuccess) return (int)e;
-      granted = true;
-    }
+    static SmemGrant granted;
+    e = grant_smem(reinterpret_cast<const void*>(attn_split_kernel), (size_t)2 * kAttnMaxChunk * 256 * 2, 0, granted);
+    if (e != cudaSuccess) return (int)e;
     AttnArgs a;
     a.qkv = qkv;
     a.q_norm = w->q_norm;
