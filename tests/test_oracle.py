@@ -112,23 +112,31 @@ def _np_block(shape, L, hidden, attn, next_rms1, mode):
 
 
 @pytest.mark.parametrize("mode", [0, 1])
-def test_oracle_matches_float64_restatement(orc, layer_small, mode):
+@pytest.mark.parametrize("T", [3, 8])
+def test_oracle_matches_float64_restatement(orc, layer_small, mode, T):
+    """The C oracle against the float64 restatement with the same bf16 rounding points: what is left is the fp32
+    accumulation and the bf16 roundings it flips by one ulp. Measured at these inputs: with the router input equal,
+    logits within 3e-7; one router-input element one ulp apart (T = 8) moves them by 9.6e-5; routed within 6.1e-4;
+    sout and the next layer's normed within one bf16 ulp (2^-8 relative); hidden within 1.3e-4. The bars keep a few
+    times that: fp32 accumulation takes at most 1/6 of the int4 outputs' parity tolerance (2e-2) and 1/10 of the
+    fp32 hidden's (1e-2)."""
     s = SMALL
-    hidden, attn = O.make_activations(s, 3, 11)
+    hidden, attn = O.make_activations(s, T, 8 + T)
     nr = O.f32_to_bf16(1.0 + 0.1 * O.normal(3, 3, s.H))
     got = orc.block_forward(s, layer_small, hidden, attn, next_rms1=nr, mode=mode)
     ref = _np_block(s, layer_small, hidden, attn, nr, mode)
-    assert O.max_rel_err(got["logits"], ref["logits"]) < 1e-5
-    # routing identical wherever the 8th/9th margin is not a near-tie
+    assert O.max_rel_err(got["logits"], ref["logits"]) < 5e-4
+    # routing identical wherever the 8th/9th margin exceeds twice the logit difference
+    lerr = np.abs(got["logits"] - ref["logits"]).max(axis=1)
     srt = np.sort(ref["logits"], axis=1)[:, ::-1]
     margin = srt[:, s.TOPK - 1] - srt[:, s.TOPK]
-    for t in range(3):
-        if margin[t] > 1e-4:
+    for t in range(T):
+        if margin[t] > 2 * lerr[t] + 1e-6:
             assert sorted(got["idx"][t]) == sorted(ref["idx"][t])
-    assert O.max_rel_err(got["routed"], ref["routed"]) < 2e-2
-    assert O.max_rel_err(O.bf16_to_f32(got["sout"]), ref["sout"]) < 1e-2
-    assert O.max_rel_err(got["hidden"], ref["hidden"]) < 1e-2
-    assert O.max_rel_err(O.bf16_to_f32(got["normed"]), ref["normed"]) < 1e-2
+    assert O.max_rel_err(got["routed"], ref["routed"]) < 3e-3
+    assert O.max_rel_err(O.bf16_to_f32(got["sout"]), ref["sout"]) < 2 ** -8 + 1e-6
+    assert O.max_rel_err(got["hidden"], ref["hidden"]) < 1e-3
+    assert O.max_rel_err(O.bf16_to_f32(got["normed"]), ref["normed"]) < 2 ** -8 + 1e-6
 
 
 def test_decode_and_tile_numerics_agree(orc, layer_small):
