@@ -965,12 +965,25 @@ def time_oracle(L, shape, B, seconds, mode=0, max_steps=None, threads=None):
     return steps, el, n
 
 
+def cpu_model():
+    """The host CPU's model name (the first `model name` line of /proc/cpuinfo), or None where it cannot be read."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def cpu_baseline(layer, shape, B, seconds):
     """The oracle's block on every host thread, plus a shorter single-thread (scalar) timing beside it."""
     L = host_layer(layer)
     steps, el, n = time_oracle(L, shape, B, seconds)
     s1, el1, _ = time_oracle(L, shape, B, max(1.0, seconds / 4), threads=1)
-    return {"value": steps * B / el, "unit": "tok/s", "cores": n, "kind": "port",
+    return {"value": steps * B / el, "unit": "tok/s", "cores": n, "kind": "port", "cpu": cpu_model(),
+            "logical_cpus": os.cpu_count(),
             "sample": f"{steps} decode steps of batch {B} through the C oracle of the block (decode numerics) on one "
                       f"layer, {el:.1f} s, {n} threads ({os.cpu_count()} logical CPUs)",
             "single_thread": {"value": s1 * B / el1, "unit": "tok/s", "cores": 1,
@@ -1128,7 +1141,8 @@ def reference_arm(args, rank, world, local):
         "steps": steps, "warmup": args.warmup, "ms_per_step": el / steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": DTYPE, "data": DATA,
         "config": decode_config(shape, B, world, args.steps, args.layer_copies),
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": n, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": n, "kind": "port", "sample": sample,
+                         "cpu": cpu_model(), "logical_cpus": os.cpu_count()},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference implements the block only as GPU kernels (examples/qwen/kernels.cuh); its CPU "
                 "arm is the oracle's scalar restatement of those kernels; `ref_gpu` times those kernels themselves",

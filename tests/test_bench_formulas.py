@@ -129,3 +129,9 @@ def test_packed_io_layout():
     assert torch.equal(o[:T * H * 4].view(torch.float32).view(T, H), h + 1)
     assert bool((o[T * H * 4:].view(torch.int16) == 7).all())
     assert all(t.data_ptr() % 16 == 0 for t in (av, hv, nv))
+
+
+def test_cpu_model_is_read_from_the_host():
+    b = load_bench()
+    name = b.cpu_model()
+    assert name is None or (isinstance(name, str) and name)
