@@ -164,6 +164,25 @@ def reset_stats():
     _lib.moe_stats_reset()
 
 
+def tensor_stats(t, bf16=None):
+    """The reference's `--debug` statistics of one tensor (qwen.cu:66-89): element count, mean and rms over all
+    elements with the non-finite ones left out of the sums, absmax of the finite ones, the count of NaN/inf values and
+    the first four values. `bf16` (default: int16 or uint16 storage) decodes bf16 bits. Synchronises the device the
+    tensor lives on and copies it to the host."""
+    x = t.detach()
+    if bf16 is None:
+        bf16 = x.dtype in (torch.int16, torch.uint16)
+    x = x.contiguous().reshape(-1)
+    x = x.view(torch.bfloat16) if bf16 else x
+    x = x.to("cpu", torch.float64)
+    n = x.numel()
+    fin = torch.isfinite(x)
+    v = torch.where(fin, x, torch.zeros_like(x))
+    return {"n": n, "mean": float(v.sum()) / n if n else 0.0, "rms": float((v * v).sum() / n) ** 0.5 if n else 0.0,
+            "absmax": float(v.abs().max()) if n else 0.0, "nonfinite": int(n - int(fin.sum())),
+            "head": [float(a) for a in x[:4]]}
+
+
 def _ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
@@ -340,6 +359,17 @@ class MoeBlock:
         if tr.sorted:  # prefill path: the stable expert sort
             out["sorted"] = view(tr.sorted, T * s.TOPK, torch.int32)
             out["offsets"] = view(tr.offsets, s.E + 1, torch.int32)
+        return out
+
+    def debug_stats(self, T, hidden=None, normed=None):
+        """The reference's `--debug` report for the last forward of T tokens (qwen.cu:382-449 print the same
+        statistics per stage): tensor_stats of every traced intermediate, plus hidden and normed when given."""
+        tr = self.trace(T)
+        out = {n: tensor_stats(v, bf16=(n == "sout")) for n, v in tr.items() if n not in ("idx", "sorted", "offsets")}
+        if hidden is not None:
+            out["hidden"] = tensor_stats(hidden)
+        if normed is not None:
+            out["normed"] = tensor_stats(normed, bf16=True)
         return out
 
 

@@ -200,3 +200,18 @@ def test_cpp_block_host_builds(tmp_path):
     assert run.returncode == 2 and "usage" in run.stderr
     run = subprocess.run([exe, str(tmp_path / "missing.mvccq")], capture_output=True, text=True, timeout=60)
     assert run.returncode == 1 and "cannot open" in run.stderr  # refused before any CUDA call
+
+
+def test_tensor_stats_follow_the_reference_debug_report():
+    """tensor_stats (the reference's --debug statistics, qwen.cu:66-89) on host tensors: non-finite values are
+    counted and left out of the sums, the mean and rms divide by every element, bf16 bits are decoded."""
+    import torch
+    import mvcc_b200
+    x = torch.tensor([1.0, -3.0, float("nan"), float("inf"), 2.0], dtype=torch.float32)
+    st = mvcc_b200.tensor_stats(x)
+    assert st["n"] == 5 and st["nonfinite"] == 2
+    assert st["mean"] == 0.0 and abs(st["rms"] - (14 / 5) ** 0.5) < 1e-12 and st["absmax"] == 3.0
+    assert st["head"][:2] == [1.0, -3.0]
+    b = torch.tensor([0.5, -0.25], dtype=torch.bfloat16).view(torch.int16)
+    sb = mvcc_b200.tensor_stats(b)
+    assert sb["absmax"] == 0.5 and sb["mean"] == 0.125 and sb["nonfinite"] == 0

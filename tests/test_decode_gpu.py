@@ -218,6 +218,9 @@ def test_block_forward(orc, name, T, with_next):
         assert O.max_rel_err(tr["routed"].cpu().numpy()[ok], ref["routed"][ok]) < TOL_INT4
         assert O.max_rel_err(O.bf16_to_f32(host16(tr["sout"])), O.bf16_to_f32(ref["sout"])) < TOL_BF16
         assert np.allclose(tr["gate"].cpu().numpy()[ok], ref["gate"][ok], rtol=2e-3)
+        dbg = blk.debug_stats(T)  # the reference's --debug report over the traced intermediates
+        assert all(v["nonfinite"] == 0 for v in dbg.values())
+        assert abs(dbg["routed"]["absmax"] - float(np.abs(tr["routed"].cpu().numpy()).max())) < 1e-6
     assert blk.error_word() == 0
 
 
