@@ -91,6 +91,39 @@ def test_lm_head_logits_and_argmax(V):
         assert int(nxt.item()) == S.argmax_lowest(gl)
 
 
+def _best_ms(fn, reps=5):
+    """Best of `reps` CUDA-event timings of fn() on the current stream, after one warm-up call."""
+    fn()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return best
+
+
+def test_lm_head_streams_at_the_copy_bandwidth():
+    """A bandwidth gate in the manner of the reference's attention test (tests/kernels/qwen_attention.cu:70-108,
+    at least 70 % of the device-to-device copy's GB/s): the 2048 x 151936 LM head GEMV with its argmax reads its
+    622 MB of weights at no less than half the rate a plain device copy of the same bytes moves them (read + write),
+    timed in the same process. The weights exceed the 126 MB L2, so neither side is served from cache."""
+    from mvcc_b200 import stack as st
+    V, H = 151936, 2048
+    w = torch.zeros(V, H, dtype=torch.int16, device="cuda")
+    x = torch.zeros(H, dtype=torch.int16, device="cuda")
+    head = st.LmHead(w)
+    nxt = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gemv_ms = _best_ms(lambda: head.argmax(x, nxt))
+    dst = torch.empty_like(w)
+    copy_ms = _best_ms(lambda: dst.copy_(w))
+    nbytes = w.numel() * 2
+    gemv_gbs, copy_gbs = nbytes / gemv_ms / 1e6, 2 * nbytes / copy_ms / 1e6
+    assert gemv_gbs >= 0.5 * copy_gbs, (gemv_gbs, copy_gbs)
+
+
 def test_lm_head_ties_go_to_the_lowest_index_and_nan_never_wins():
     from mvcc_b200 import stack as st
     V, H = 8192, 256
