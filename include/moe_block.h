@@ -145,12 +145,18 @@ MOE_API int moe_shared_expert(const moe_layer_weights* w, void* workspace, size_
  * E <= 256, TOPK <= 8) lives in a fixed 8 KiB array in the library's device memory, held on every GPU that loads
  * the library until exit; shapes whose scratch would not fit are rejected with cudaErrorInvalidValue. Each call
  * looks up the array's device address on the current device (cudaGetSymbolAddress); the first call on a device
- * loads the library's device code there, so make it before any stream capture. Errors are reported through the
- * return code only: the scratch error word is not readable by the caller (the router's own top-k never produces the
- * invalid-expert condition it records). All calls share the array: calls that overlap on the GPU race and must be
- * serialised by the caller. Allocates nothing. */
+ * loads the library's device code there, so make it before any stream capture. Launch errors come back through the
+ * return code; the scratch error word, which the kernels set as in a workspace, is read by
+ * moe_router_topk_noalloc_error (the router's own top-k never produces the invalid-expert condition it records).
+ * All calls share the array: calls that overlap on the GPU race and must be serialised by the caller. Allocates
+ * nothing. */
 MOE_API int moe_router_topk_noalloc(const moe_layer_weights* w, const uint16_t* normed, float* logits, int32_t* idx,
                                     float* wts, int T, moe_stream_t stream);
+
+/* Reads and clears the error word of moe_router_topk_noalloc's scratch on the current device, after synchronising
+ * the stream: the MOE_ERR_* bits of the last call (each call clears the word before its launches), or -cudaError.
+ * Allocates nothing. */
+MOE_API int moe_router_topk_noalloc_error(moe_stream_t stream);
 
 /* Intermediates of the last moe_block_forward of T tokens on this workspace (device pointers into it, valid until
  * the next call): logits [T,E], idx [T,TOPK], wts [T,TOPK], routed [T,H] fp32, sout [T,H] bf16, gate [T] fp32; on

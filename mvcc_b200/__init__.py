@@ -84,6 +84,7 @@ _SIGS = {
     "moe_event_elapsed_ms": (_I, [_P, _P, ctypes.POINTER(ctypes.c_float)]),
     "moe_router_topk": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _I, _P]),
     "moe_router_topk_noalloc": (_I, [_W, _P, _P, _P, _P, _I, _P]),
+    "moe_router_topk_noalloc_error": (_I, [_P]),
     "moe_routed_experts": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _P, _P, _P, _I, _P]),
     "moe_shared_expert": (_I, [_W, _P, ctypes.c_size_t, _P, _P, _I, _P]),
     "moe_workspace_trace": (_I, [_W, _P, ctypes.c_size_t, _I, ctypes.POINTER(MoeTrace)]),
@@ -385,6 +386,14 @@ def router_topk_noalloc(layer: MoeLayer, normed, logits, idx, wts, T=None, strea
     T = normed.shape[0] if T is None else T
     _check(_lib.moe_router_topk_noalloc(ctypes.byref(layer.c), _ptr(normed), _ptr(logits), _ptr(idx), _ptr(wts), T,
                                         _stream(stream)), "moe_router_topk_noalloc")
+
+
+def router_topk_noalloc_error(stream=None):
+    """Reads and clears the allocation-free router's error word on the current device (moe_router_topk_noalloc_error)."""
+    rc = _lib.moe_router_topk_noalloc_error(_stream(stream))
+    if rc < 0:
+        raise MoeError(f"moe_router_topk_noalloc_error failed: cudaError {-rc}")
+    return rc
 
 
 def synth_layer(shape: MoeShape, seed: int, device="cuda", std=0.02, stream=None) -> MoeLayer:

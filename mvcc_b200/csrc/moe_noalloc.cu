@@ -15,8 +15,9 @@
 // GPU (concurrent streams, or several host threads) race on the array and must be serialised by the caller.
 //
 // The router always runs the decode kernels (route_kernel: GEMV + the reference's top-k), chunk by chunk, whatever
-// the prefill threshold. The error word it clears is not read back: the caller gets errors through the return code,
-// and the route kernel's own top-k cannot produce the invalid-expert index the word records.
+// the prefill threshold. moe_router_topk_noalloc_error reads the array's error word back (and clears it) for the
+// current device; the route kernel's own top-k cannot produce the invalid-expert index the word records, so it
+// stays zero unless the kernels misbehave.
 #include <cstring>
 
 #include "moe_common.cuh"
@@ -94,4 +95,18 @@ extern "C" int moe_router_topk_noalloc(const moe_layer_weights* w, const uint16_
     if (e != cudaSuccess) return (int)e;
   }
   return 0;
+}
+
+extern "C" int moe_router_topk_noalloc_error(moe_stream_t stream) {
+  uint8_t* base = nullptr;
+  cudaError_t e = scratch_address(&base);
+  if (e != cudaSuccess) return -(int)e;
+  uint32_t* errp = reinterpret_cast<uint32_t*>(base + scratch_layout(1, 1).err);  // offset independent of the shape
+  uint32_t v = 0;
+  const cudaStream_t s = (cudaStream_t)stream;
+  e = cudaMemcpyAsync(&v, errp, sizeof v, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(errp, 0, sizeof v, s);
+  if (e != cudaSuccess) return -(int)e;
+  return (int)v;
 }

@@ -54,6 +54,7 @@ def test_noalloc_router_matches_workspace_router(name, T):
         assert O.max_rel_err(got[0].cpu().numpy(), ref[0].cpu().numpy()) < 1e-5
         assert np.array_equal(got[1].cpu().numpy(), ref[1].cpu().numpy())
         assert np.allclose(got[2].cpu().numpy(), ref[2].cpu().numpy(), rtol=1e-5, atol=1e-7)
+        assert m.router_topk_noalloc_error() == 0  # the scratch error word, read back and cleared
 
 
 @pytest.mark.gpu
